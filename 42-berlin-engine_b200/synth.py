@@ -1,0 +1,159 @@
+"""Seeded synthetic Llama-style decoders for tests and the benchmark.
+
+The reference ships no weights (its benches need Ministral/SmolLM checkpoints
+that are not in the repository), so every run here uses random-init models of
+the configured shapes, the same approach as the reference's
+scripts/gen_dummy.py:18-48:
+
+* matrices ~ N(0, 0.02), quantised per output row to symmetric INT8 with an
+  fp32 scale (``pow2=True`` rounds each scale up to a power of two, which makes
+  q * scale exactly representable in BF16, so the reference's BF16 path sees
+  the identical weights), or cast to FP8 E4M3 with one per-tensor scale;
+* token embedding BF16 ~ N(0, 0.02); RMSNorm weights BF16 1 + N(0, 0.1).
+"""
+from dataclasses import dataclass, asdict
+
+import numpy as np
+
+
+@dataclass
+class ModelConfig:
+    dim: int
+    hidden_dim: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    vocab_size: int
+    seq_len: int
+    head_dim: int
+    rope_theta: float
+    norm_eps: float = 1e-5
+
+    def as_dict(self):
+        return asdict(self)
+
+
+TINY = ModelConfig(dim=512, hidden_dim=1408, n_layers=8, n_heads=8, n_kv_heads=8,
+                   vocab_size=32000, seq_len=8192, head_dim=64, rope_theta=1e4)
+LLAMA3_8B = ModelConfig(dim=4096, hidden_dim=14336, n_layers=32, n_heads=32, n_kv_heads=8,
+                        vocab_size=128256, seq_len=8192, head_dim=128, rope_theta=5e5)
+LLAMA_70B = ModelConfig(dim=8192, hidden_dim=28672, n_layers=80, n_heads=64, n_kv_heads=8,
+                        vocab_size=128256, seq_len=32768, head_dim=128, rope_theta=5e5)
+
+MATS = ("wq", "wk", "wv", "wo", "w1", "w2", "w3")
+
+
+def mat_shapes(cfg):
+    qd = cfg.n_heads * cfg.head_dim
+    kvd = cfg.n_kv_heads * cfg.head_dim
+    return {"wq": (qd, cfg.dim), "wk": (kvd, cfg.dim), "wv": (kvd, cfg.dim),
+            "wo": (cfg.dim, qd), "w1": (cfg.hidden_dim, cfg.dim),
+            "w2": (cfg.dim, cfg.hidden_dim), "w3": (cfg.hidden_dim, cfg.dim)}
+
+
+def f32_to_bf16(a):
+    """Round-to-nearest-even, as src/tensor/tensor.c:67-76 does."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def bf16_to_f32(a):
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+def quant_int8_rows(w, pow2=True):
+    amax = np.abs(w).max(axis=1)
+    amax = np.where(amax > 0, amax, 1.0).astype(np.float32)
+    if pow2:
+        s = np.exp2(np.ceil(np.log2(amax / np.float32(127.0)))).astype(np.float32)
+    else:
+        s = (amax / np.float32(127.0)).astype(np.float32)
+    q = np.clip(np.rint(w / s[:, None]), -127, 127).astype(np.int8)
+    return q, s
+
+
+_E4M3 = None
+
+
+def e4m3_table():
+    """Decode value of every E4M3 code as the reference defines it
+    (src/compute/ops_quant.c:27-50; no NaN code)."""
+    global _E4M3
+    if _E4M3 is None:
+        t = np.zeros(256, np.float32)
+        for c in range(256):
+            e, m = (c >> 3) & 15, c & 7
+            v = np.ldexp(m / 8.0, -6) if e == 0 else np.ldexp(1.0 + m / 8.0, e - 7)
+            t[c] = -v if c & 0x80 else v
+        _E4M3 = t
+    return _E4M3
+
+
+def quant_fp8_tensor(w):
+    """Per-tensor E4M3 with a power-of-two scale; round to the nearest code
+    (ties to even mantissa) among codes 0x00..0x7E (the OCP E4M3 cast; the
+    NaN code 0x7F is never produced)."""
+    amax = float(np.abs(w).max()) or 1.0
+    s = np.float32(2.0 ** np.ceil(np.log2(amax / 448.0)))
+    x = (w / s).astype(np.float32)
+    pos = e4m3_table()[:0x7F]          # ascending magnitudes 0 .. 448
+    a = np.abs(x)
+    i = np.clip(np.searchsorted(pos, a), 1, 0x7E)
+    lo, hi = pos[i - 1], pos[i]
+    pick_hi = (a - lo > hi - a) | ((a - lo == hi - a) & ((i & 1) == 0))
+    code = np.where(pick_hi, i, i - 1).astype(np.uint8)
+    code = np.where(x < 0, code | 0x80, code).astype(np.uint8)
+    code = np.where(code == 0x80, 0, code).astype(np.uint8)
+    return code, np.array([s], np.float32)
+
+
+class Model:
+    """Host copy of a synthetic model: quantised matrices + BF16 vectors."""
+
+    def __init__(self, cfg, kind, emb, final_norm, lm, layers, seed):
+        self.cfg, self.kind, self.emb, self.final_norm = cfg, kind, emb, final_norm
+        self.lm, self.layers, self.seed = lm, layers, seed
+
+    def dequant(self, q, s):
+        if self.kind == "int8":
+            return q.astype(np.float32) * s[:, None]
+        return e4m3_table()[q] * s[0]
+
+    def bf16_weights(self):
+        """BF16 matrices q * scale for the reference's BF16 path."""
+        out = {"emb": self.emb, "final_norm": self.final_norm,
+               "lm": f32_to_bf16(self.dequant(*self.lm)), "layers": []}
+        for lw in self.layers:
+            d = {n: f32_to_bf16(self.dequant(*lw[n])) for n in MATS}
+            d["attention_norm"] = lw["attention_norm"]
+            d["ffn_norm"] = lw["ffn_norm"]
+            out["layers"].append(d)
+        return out
+
+
+def make_model(cfg, seed=1234, kind="int8", pow2=True):
+    rng = np.random.default_rng(seed)
+    shapes = mat_shapes(cfg)
+
+    def mat(shape):
+        w = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+        return quant_int8_rows(w, pow2) if kind == "int8" else quant_fp8_tensor(w)
+
+    def norm():
+        return f32_to_bf16(1.0 + 0.1 * rng.standard_normal(cfg.dim, dtype=np.float32))
+
+    emb = f32_to_bf16(rng.standard_normal((cfg.vocab_size, cfg.dim), dtype=np.float32)
+                      * np.float32(0.02))
+    layers = []
+    for _ in range(cfg.n_layers):
+        lw = {n: mat(shapes[n]) for n in MATS}
+        lw["attention_norm"] = norm()
+        lw["ffn_norm"] = norm()
+        layers.append(lw)
+    final_norm = norm()
+    lm = mat((cfg.vocab_size, cfg.dim))
+    return Model(cfg, kind, emb, final_norm, lm, layers, seed)
+
+
+def prompt(cfg, n, seed=99):
+    return np.random.default_rng(seed).integers(0, cfg.vocab_size, n).astype(np.int32)
