@@ -1,0 +1,61 @@
+// attn.cuh -- KV append, LSH index and decode attention kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ec {
+
+// Device layout of the decode state of one context (all sequences, layers).
+struct KvLayout {
+  int n_layers, n_heads, n_kv_heads, head_dim, seq_len;
+  int max_blocks;       // per (sequence, layer): ceil(seq_len / 16)
+  int paged;            // 1 paged INT8, 0 linear BF16
+  // paged INT8: block (seq, layer, physical b) at index ((seq*L + layer)*MB + b)
+  int8_t* kq;           // [S*L*MB][KV][16][hd]
+  int8_t* vq;
+  float* ks;            // [S*L*MB][KV][16]
+  float* vs;
+  float* centroid;      // [S*L*MB][hd]
+  int* page_table;      // [S*L*MB] logical -> physical (within the sequence+layer)
+  // linear BF16: [S*L][seq_len][KV][hd]
+  uint16_t* lk;
+  uint16_t* lv;
+};
+
+struct LshLayout {
+  int tables, bits, unit, max_units, radius, max_cand;
+  const float* hp;      // [tables][bits][head_dim]
+  // per sequence
+  float* acc;           // [S][head_dim]
+  int* meta;            // [S][4]: acc_count, acc_start, n_units, pad
+  uint32_t* unit_hash;  // [S][tables][max_units]
+  int* unit_start;      // [S][max_units]
+  int* unit_len;        // [S][max_units]
+  int* heads;           // [S][tables][1 << bits]
+  int* next;            // [S][tables][max_units]
+  unsigned long long* counters;  // [S][2]: sparse queries, sum of attended K
+};
+
+struct StepBuffers {
+  const int* pos;       // [B]
+  float* qkv;           // [B][(H + 2KV) * hd]  (q rotated in place)
+  float* att;           // [B][H * hd]
+  int* sel;             // [B][L?] per-sequence selection scratch: [B][max_sel]
+  int* nsel;            // [B]
+  int max_sel;
+  const float* rope_cos;  // [seq_len][hd/2]
+  const float* rope_sin;
+  int sparse_k, window, sparse_blocks_k;
+  int* err;
+};
+
+// Shared-memory attributes for the current device (outside stream capture).
+cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb);
+cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
+                             int layer, int B, cudaStream_t s, bool pdl);
+cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
+                                 int layer, int B, cudaStream_t s, bool pdl);
+cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
+                             cudaStream_t s, bool pdl);
+
+}  // namespace ec

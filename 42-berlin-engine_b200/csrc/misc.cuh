@@ -1,0 +1,18 @@
+// misc.cuh -- embedding, argmax and per-op kernels.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace ec {
+cudaError_t launch_embed(const uint16_t* emb, const int* tokens, float* x, int dim, int vocab, int B,
+                         cudaStream_t s, bool pdl);
+cudaError_t launch_argmax(const float* logits, int n, int B, int* out, int* tokens, int* pos,
+                          cudaStream_t s, bool pdl);
+cudaError_t launch_rmsnorm(float* out, const float* x, const uint16_t* w, int n, float eps,
+                           cudaStream_t s);
+cudaError_t launch_rope(float* data, int n_heads, int hd, int pos, const float* c, const float* sn,
+                        int max_seq, cudaStream_t s);
+cudaError_t launch_silu(float* out, const float* g, const float* u, int n, cudaStream_t s);
+cudaError_t launch_quant(int8_t* out, float* scales, const float* in, int rows, int n,
+                         cudaStream_t s);
+}  // namespace ec

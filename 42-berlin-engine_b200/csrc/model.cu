@@ -1,0 +1,863 @@
+// model.cu -- the decode context behind include/engine_cuda.h: device copies of
+// the weights in fused layouts, the KV / LSH state, host-computed constant
+// tables, and the decode step (one CUDA graph per batch shape, kernels chained
+// with programmatic dependent launch).
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "attn.cuh"
+#include "ec_internal.cuh"
+#include "gemv.cuh"
+#include "misc.cuh"
+
+static thread_local char g_err[512];
+
+extern "C" void ec_set_last_error(const char* msg) {
+  snprintf(g_err, sizeof(g_err), "%s", msg ? msg : "");
+}
+
+extern "C" const char* ec_last_error(void) { return g_err; }
+
+namespace {
+
+struct Mat {
+  uint8_t* w = nullptr;
+  float* scale = nullptr;  // per row (INT8 and FP8 alike, FP8 expanded)
+  int rows = 0, cols = 0;
+};
+
+}  // namespace
+
+struct ec_ctx {
+  ec_model_config c;
+  int device = 0;
+  int n_sm = 148;
+  cudaStream_t stream = nullptr;
+  int esize = 1;
+  // weights
+  std::vector<Mat> qkv, wo, w13, w2;
+  Mat lm;
+  std::vector<uint16_t*> attn_norm, ffn_norm;
+  uint16_t* emb = nullptr;
+  uint16_t* final_norm = nullptr;
+  std::vector<unsigned> have;  // bit per tensor per layer
+  unsigned have_global = 0;
+  // state
+  ec::KvLayout kv{};
+  ec::LshLayout lsh{};
+  float *x = nullptr, *qkvb = nullptr, *att = nullptr, *hbuf = nullptr, *logits = nullptr;
+  int *argmax = nullptr, *tokens = nullptr, *pos = nullptr, *sel = nullptr, *nsel = nullptr;
+  int* err = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
+  int max_sel = 0;
+  ec::GemvPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_lm{};
+  // graph cache
+  cudaGraphExec_t gexec = nullptr;
+  int g_B = -1, g_fb = -1;
+  const int *g_tok = nullptr, *g_pos = nullptr;
+  int launches = 0;
+  std::vector<void*> allocs;
+  // profiling
+  bool prof = false;
+  struct Rec { int kind; cudaEvent_t a, b; double bytes; };
+  std::vector<Rec> recs;
+  std::vector<cudaEvent_t> ev_pool;
+  double prof_ms[EC_K_COUNT] = {0};
+  int prof_n[EC_K_COUNT] = {0};
+  double prof_bytes[EC_K_COUNT] = {0};
+};
+
+namespace {
+
+template <typename T>
+cudaError_t dalloc(ec_ctx* c, T** p, size_t n) {
+  void* v = nullptr;
+  cudaError_t e = cudaMalloc(&v, n * sizeof(T) + 16);
+  if (e != cudaSuccess) return e;
+  c->allocs.push_back(v);
+  *p = static_cast<T*>(v);
+  return cudaSuccess;
+}
+
+// rand_gaussian, src/compute/ops_lsh.c:22-34 (host libm, same formula)
+float rand_gaussian(unsigned* seed) {
+  *seed = *seed * 1103515245u + 12345u;
+  float u1 = (float)((*seed >> 16) & 0x7FFF) / 32767.0f;
+  *seed = *seed * 1103515245u + 12345u;
+  float u2 = (float)((*seed >> 16) & 0x7FFF) / 32767.0f;
+  if (u1 < 1e-6f) u1 = 1e-6f;
+  return sqrtf(-2.0f * logf(u1)) * cosf(2.0f * 3.14159265f * u2);
+}
+
+int fail(int code, const char* msg) {
+  ec_set_last_error(msg);
+  return code;
+}
+
+cudaEvent_t take_event(ec_ctx* c) {
+  if (!c->ev_pool.empty()) {
+    cudaEvent_t e = c->ev_pool.back();
+    c->ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Brackets one launch with events when profiling (never inside a capture).
+struct ProfScope {
+  ec_ctx* c;
+  int kind;
+  double bytes;
+  cudaEvent_t a = nullptr;
+  ProfScope(ec_ctx* ctx, int k, double by) : c(ctx), kind(k), bytes(by) {
+    if (c->prof) {
+      a = take_event(c);
+      cudaEventRecord(a, c->stream);
+    }
+  }
+  ~ProfScope() {
+    if (c->prof) {
+      cudaEvent_t b = take_event(c);
+      cudaEventRecord(b, c->stream);
+      c->recs.push_back({kind, a, b, bytes});
+    }
+  }
+};
+
+void prof_collect(ec_ctx* c) {
+  for (auto& r : c->recs) {
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+      c->prof_ms[r.kind] += ms;
+      c->prof_n[r.kind] += 1;
+      c->prof_bytes[r.kind] += r.bytes;
+    }
+    c->ev_pool.push_back(r.a);
+    c->ev_pool.push_back(r.b);
+  }
+  c->recs.clear();
+}
+
+}  // namespace
+
+extern "C" int ec_config_default(ec_model_config* c) {
+  if (!c) return EC_ERR_ARG;
+  memset(c, 0, sizeof(*c));
+  c->dim = 4096;
+  c->hidden_dim = 14336;
+  c->n_layers = 32;
+  c->n_heads = 32;
+  c->n_kv_heads = 8;
+  c->vocab_size = 128256;
+  c->seq_len = 8192;
+  c->head_dim = 128;
+  c->rope_theta = 500000.0f;
+  c->norm_eps = 1e-5f;
+  c->weight_kind = EC_W_INT8;
+  c->use_paged_kv = 1;
+  c->sparse_k = 64;
+  c->window = 128;
+  c->sparse_blocks_k = 64;
+  c->lsh_tables = 1;
+  c->lsh_bits = 16;
+  c->lsh_unit = 64;
+  c->lsh_max_units = 4096;
+  c->lsh_radius = 4;
+  c->lsh_max_cand = 64;
+  c->max_batch = 1;
+  return EC_OK;
+}
+
+extern "C" void ec_destroy(ec_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->gexec) cudaGraphExecDestroy(ctx->gexec);
+  cudaStreamSynchronize(ctx->stream);
+  for (auto& r : ctx->recs) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (auto e : ctx->ev_pool) cudaEventDestroy(e);
+  for (void* p : ctx->allocs) cudaFree(p);
+  if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
+  if (!cfg || !out) return fail(EC_ERR_ARG, "null argument");
+  const ec_model_config& c = *cfg;
+  if (c.dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
+      c.n_heads % c.n_kv_heads || c.head_dim % 32 || c.head_dim > 128 || c.dim % 32 ||
+      c.hidden_dim % 32 || c.vocab_size <= 0 || c.seq_len <= 0 || c.max_batch <= 0)
+    return fail(EC_ERR_UNSUPPORTED, "unsupported model shape (head_dim <= 128, dims % 32)");
+  if (c.weight_kind != EC_W_INT8 && c.weight_kind != EC_W_FP8)
+    return fail(EC_ERR_ARG, "weight_kind must be EC_W_INT8 or EC_W_FP8");
+  if (c.lsh_tables < 0 || c.lsh_tables > 16 || c.lsh_bits < 1 || c.lsh_bits > 16 ||
+      c.lsh_max_units > 4096 || c.lsh_unit <= 0 || c.lsh_max_cand > 64)
+    return fail(EC_ERR_UNSUPPORTED, "LSH settings out of range");
+  if (c.sparse_blocks_k < 1 || c.sparse_blocks_k > 64)
+    return fail(EC_ERR_UNSUPPORTED, "sparse_blocks_k must be in 1..64 (select_top_k_blocks)");
+  if (!c.use_paged_kv && c.sparse_k <= 0)
+    return fail(EC_ERR_UNSUPPORTED, "linear KV mode needs sparse_k > 0");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+  ec_ctx* ctx = new ec_ctx();
+  ctx->c = c;
+  ctx->device = device;
+  cudaDeviceGetAttribute(&ctx->n_sm, cudaDevAttrMultiProcessorCount, device);
+  ctx->esize = 1;
+#define TRY(x)                                  \
+  do {                                          \
+    cudaError_t e_ = (x);                       \
+    if (e_ != cudaSuccess) {                    \
+      ec_set_last_error(cudaGetErrorString(e_)); \
+      ec_destroy(ctx);                          \
+      return e_ == cudaErrorMemoryAllocation ? EC_ERR_OOM : EC_ERR_CUDA; \
+    }                                           \
+  } while (0)
+  TRY(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+  const int L = c.n_layers, H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim;
+  const int F = c.hidden_dim, V = c.vocab_size, S = c.max_batch;
+  ctx->qkv.resize(L);
+  ctx->wo.resize(L);
+  ctx->w13.resize(L);
+  ctx->w2.resize(L);
+  ctx->attn_norm.assign(L, nullptr);
+  ctx->ffn_norm.assign(L, nullptr);
+  ctx->have.assign(L, 0);
+  for (int l = 0; l < L; l++) {
+    Mat* ms[4] = {&ctx->qkv[l], &ctx->wo[l], &ctx->w13[l], &ctx->w2[l]};
+    const int rows[4] = {(H + 2 * KV) * hd, D, 2 * F, D};
+    const int cols[4] = {D, H * hd, D, F};
+    for (int i = 0; i < 4; i++) {
+      ms[i]->rows = rows[i];
+      ms[i]->cols = cols[i];
+      TRY(dalloc(ctx, &ms[i]->w, (size_t)rows[i] * cols[i]));
+      TRY(dalloc(ctx, &ms[i]->scale, (size_t)rows[i]));
+    }
+    TRY(dalloc(ctx, &ctx->attn_norm[l], (size_t)D));
+    TRY(dalloc(ctx, &ctx->ffn_norm[l], (size_t)D));
+  }
+  ctx->lm.rows = V;
+  ctx->lm.cols = D;
+  TRY(dalloc(ctx, &ctx->lm.w, (size_t)V * D));
+  TRY(dalloc(ctx, &ctx->lm.scale, (size_t)V));
+  TRY(dalloc(ctx, &ctx->emb, (size_t)V * D));
+  TRY(dalloc(ctx, &ctx->final_norm, (size_t)D));
+  // activations
+  TRY(dalloc(ctx, &ctx->x, (size_t)S * D));
+  TRY(dalloc(ctx, &ctx->qkvb, (size_t)S * (H + 2 * KV) * hd));
+  TRY(dalloc(ctx, &ctx->att, (size_t)S * H * hd));
+  TRY(dalloc(ctx, &ctx->hbuf, (size_t)S * F));
+  TRY(dalloc(ctx, &ctx->logits, (size_t)S * V));
+  TRY(dalloc(ctx, &ctx->argmax, (size_t)S));
+  TRY(dalloc(ctx, &ctx->tokens, (size_t)S));
+  TRY(dalloc(ctx, &ctx->pos, (size_t)S));
+  ctx->max_sel = c.sparse_k > c.sparse_blocks_k + 2 ? c.sparse_k : c.sparse_blocks_k + 2;
+  TRY(dalloc(ctx, &ctx->sel, (size_t)S * ctx->max_sel));
+  TRY(dalloc(ctx, &ctx->nsel, (size_t)S));
+  TRY(dalloc(ctx, &ctx->err, 1));
+  TRY(cudaMemset(ctx->err, 0, sizeof(int)));
+  // KV
+  ec::KvLayout& kv = ctx->kv;
+  kv.n_layers = L;
+  kv.n_heads = H;
+  kv.n_kv_heads = KV;
+  kv.head_dim = hd;
+  kv.seq_len = c.seq_len;
+  kv.max_blocks = (c.seq_len + 15) / 16;
+  kv.paged = c.use_paged_kv ? 1 : 0;
+  const size_t nblk = (size_t)S * L * kv.max_blocks;
+  if (kv.paged) {
+    TRY(dalloc(ctx, &kv.kq, nblk * KV * 16 * hd));
+    TRY(dalloc(ctx, &kv.vq, nblk * KV * 16 * hd));
+    TRY(dalloc(ctx, &kv.ks, nblk * KV * 16));
+    TRY(dalloc(ctx, &kv.vs, nblk * KV * 16));
+    TRY(dalloc(ctx, &kv.centroid, nblk * hd));
+    TRY(dalloc(ctx, &kv.page_table, nblk));
+    std::vector<int> pt(nblk);
+    for (size_t i = 0; i < nblk; i++) pt[i] = (int)(i % kv.max_blocks);
+    TRY(cudaMemcpy(kv.page_table, pt.data(), nblk * sizeof(int), cudaMemcpyHostToDevice));
+  } else {
+    TRY(dalloc(ctx, &kv.lk, (size_t)S * L * c.seq_len * KV * hd));
+    TRY(dalloc(ctx, &kv.lv, (size_t)S * L * c.seq_len * KV * hd));
+  }
+  // RoPE tables (rope_cache_init, ops_rope.c:30-96) on the host
+  {
+    const int half = hd / 2;
+    std::vector<float> inv(half), ct((size_t)c.seq_len * half), st((size_t)c.seq_len * half);
+    for (int i = 0; i < half; i++)
+      inv[i] = 1.0f / powf(c.rope_theta, (float)(i * 2) / (float)hd);
+    for (int p = 0; p < c.seq_len; p++)
+      for (int i = 0; i < half; i++) {
+        const float th = (float)p * inv[i];
+        ct[(size_t)p * half + i] = cosf(th);
+        st[(size_t)p * half + i] = sinf(th);
+      }
+    TRY(dalloc(ctx, &ctx->rope_cos, ct.size()));
+    TRY(dalloc(ctx, &ctx->rope_sin, st.size()));
+    TRY(cudaMemcpy(ctx->rope_cos, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(ctx->rope_sin, st.data(), st.size() * 4, cudaMemcpyHostToDevice));
+  }
+  // LSH hyperplanes (lsh_init, ops_lsh.c:40-85; table t seeded 42 + t)
+  ec::LshLayout& lsh = ctx->lsh;
+  lsh.tables = c.lsh_tables;
+  lsh.bits = c.lsh_bits;
+  lsh.unit = c.lsh_unit;
+  lsh.max_units = c.lsh_max_units;
+  lsh.radius = c.lsh_radius;
+  lsh.max_cand = c.lsh_max_cand;
+  if (lsh.tables > 0) {
+    std::vector<float> hp((size_t)lsh.tables * lsh.bits * hd);
+    for (int t = 0; t < lsh.tables; t++) {
+      unsigned seed = 42u + (unsigned)t;
+      for (int b = 0; b < lsh.bits; b++) {
+        float* row = &hp[((size_t)t * lsh.bits + b) * hd];
+        float norm = 0.0f;
+        for (int d = 0; d < hd; d++) {
+          row[d] = rand_gaussian(&seed);
+          norm = norm + row[d] * row[d];
+        }
+        norm = sqrtf(norm);
+        if (norm > 1e-6f)
+          for (int d = 0; d < hd; d++) row[d] = row[d] / norm;
+      }
+    }
+    TRY(dalloc(ctx, &ctx->hp, hp.size()));
+    TRY(cudaMemcpy(ctx->hp, hp.data(), hp.size() * 4, cudaMemcpyHostToDevice));
+    lsh.hp = ctx->hp;
+    TRY(dalloc(ctx, &lsh.acc, (size_t)S * hd));
+    TRY(dalloc(ctx, &lsh.meta, (size_t)S * 4));
+    TRY(dalloc(ctx, &lsh.unit_hash, (size_t)S * lsh.tables * lsh.max_units));
+    TRY(dalloc(ctx, &lsh.unit_start, (size_t)S * lsh.max_units));
+    TRY(dalloc(ctx, &lsh.unit_len, (size_t)S * lsh.max_units));
+    TRY(dalloc(ctx, &lsh.heads, ((size_t)S * lsh.tables) << lsh.bits));
+    TRY(dalloc(ctx, &lsh.next, (size_t)S * lsh.tables * lsh.max_units));
+    TRY(dalloc(ctx, &lsh.counters, (size_t)S * 2));
+  }
+  // GEMV plans
+  const int wk = c.weight_kind;
+  if (!ec::gemv_plan(wk, (H + 2 * KV) * hd, D, ec::EPI_STORE, ctx->n_sm, &ctx->p_qkv) ||
+      !ec::gemv_plan(wk, D, H * hd, ec::EPI_RESID, ctx->n_sm, &ctx->p_o) ||
+      !ec::gemv_plan(wk, 2 * F, D, ec::EPI_SWIGLU, ctx->n_sm, &ctx->p_w13) ||
+      !ec::gemv_plan(wk, D, F, ec::EPI_RESID, ctx->n_sm, &ctx->p_w2) ||
+      !ec::gemv_plan(wk, V, D, ec::EPI_STORE, ctx->n_sm, &ctx->p_lm)) {
+    ec_destroy(ctx);
+    return fail(EC_ERR_UNSUPPORTED, "no GEMV plan for this shape");
+  }
+  {
+    ec::StepBuffers sb{};
+    sb.sparse_k = c.sparse_k;
+    sb.window = c.window;
+    sb.sparse_blocks_k = c.sparse_blocks_k;
+    TRY(ec::gemv_prepare());
+    TRY(ec::attn_prepare(ctx->kv, ctx->lsh, sb));
+  }
+#undef TRY
+  *out = ctx;
+  for (int s = 0; s < S; s++) ec_reset(ctx, s);
+  return cudaDeviceSynchronize() == cudaSuccess ? EC_OK : EC_ERR_CUDA;
+}
+
+extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data,
+                             const float* scales, int on_device) {
+  if (!ctx || !data) return fail(EC_ERR_ARG, "null argument");
+  const ec_model_config& c = ctx->c;
+  cudaSetDevice(ctx->device);
+  const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  const cudaMemcpyKind skind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  const int D = c.dim, F = c.hidden_dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads;
+  const bool fp8 = c.weight_kind == EC_W_FP8;
+  // FP8 per-tensor scale -> per-row scale vector (same value on every row)
+  auto put_scales = [&](float* dst, int rows, int stride) -> cudaError_t {
+    if (!scales) return cudaErrorInvalidValue;
+    if (!fp8) return cudaMemcpy2D(dst, stride * 4, scales, 4, 4, rows, skind);
+    float s = 0.0f;
+    cudaError_t e = cudaMemcpy(&s, scales, 4, on_device ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost);
+    if (e != cudaSuccess) return e;
+    std::vector<float> v(rows, s);
+    return cudaMemcpy2D(dst, stride * 4, v.data(), 4, 4, rows, cudaMemcpyHostToDevice);
+  };
+  cudaError_t e = cudaSuccess;
+  if (layer < 0) {
+    switch (which) {
+      case EC_EMBEDDING:
+        e = cudaMemcpy(ctx->emb, data, (size_t)c.vocab_size * D * 2, kind);
+        break;
+      case EC_FINAL_NORM:
+        e = cudaMemcpy(ctx->final_norm, data, (size_t)D * 2, kind);
+        break;
+      case EC_LM_HEAD:
+        e = cudaMemcpy(ctx->lm.w, data, (size_t)c.vocab_size * D, kind);
+        if (e == cudaSuccess) e = put_scales(ctx->lm.scale, c.vocab_size, 1);
+        break;
+      default:
+        return fail(EC_ERR_ARG, "unknown global tensor id");
+    }
+    if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+    ctx->have_global |= 1u << (which - EC_EMBEDDING);
+    return EC_OK;
+  }
+  if (layer >= c.n_layers) return fail(EC_ERR_ARG, "layer out of range");
+  switch (which) {
+    case EC_WQ: case EC_WK: case EC_WV: {
+      const int r0 = which == EC_WQ ? 0 : (which == EC_WK ? H * hd : (H + KV) * hd);
+      const int nr = which == EC_WQ ? H * hd : KV * hd;
+      Mat& m = ctx->qkv[layer];
+      e = cudaMemcpy(m.w + (size_t)r0 * D, data, (size_t)nr * D, kind);
+      if (e == cudaSuccess) e = put_scales(m.scale + r0, nr, 1);
+      break;
+    }
+    case EC_WO:
+      e = cudaMemcpy(ctx->wo[layer].w, data, (size_t)D * H * hd, kind);
+      if (e == cudaSuccess) e = put_scales(ctx->wo[layer].scale, D, 1);
+      break;
+    case EC_W1: case EC_W3: {
+      // interleave: row 2i = gate i, row 2i+1 = up i
+      Mat& m = ctx->w13[layer];
+      const int off = which == EC_W1 ? 0 : 1;
+      e = cudaMemcpy2D(m.w + (size_t)off * D, 2 * (size_t)D, data, D, D, F, kind);
+      if (e == cudaSuccess) e = put_scales(m.scale + off, F, 2);
+      break;
+    }
+    case EC_W2:
+      e = cudaMemcpy(ctx->w2[layer].w, data, (size_t)D * F, kind);
+      if (e == cudaSuccess) e = put_scales(ctx->w2[layer].scale, D, 1);
+      break;
+    case EC_ATTN_NORM:
+      e = cudaMemcpy(ctx->attn_norm[layer], data, (size_t)D * 2, kind);
+      break;
+    case EC_FFN_NORM:
+      e = cudaMemcpy(ctx->ffn_norm[layer], data, (size_t)D * 2, kind);
+      break;
+    default:
+      return fail(EC_ERR_ARG, "unknown layer tensor id");
+  }
+  if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+  ctx->have[layer] |= 1u << which;
+  return EC_OK;
+}
+
+extern "C" int ec_reset(ec_ctx* ctx, int seq) {
+  if (!ctx || seq < 0 || seq >= ctx->c.max_batch) return fail(EC_ERR_ARG, "bad sequence");
+  cudaSetDevice(ctx->device);
+  const ec::KvLayout& kv = ctx->kv;
+  const size_t per = (size_t)kv.n_layers * kv.max_blocks;
+  if (kv.paged) {
+    EC_CUDA_TRY(cudaMemsetAsync(kv.centroid + seq * per * kv.head_dim, 0,
+                                per * kv.head_dim * 4, ctx->stream));
+  }
+  const ec::LshLayout& l = ctx->lsh;
+  if (l.tables > 0) {
+    EC_CUDA_TRY(cudaMemsetAsync(l.acc + (size_t)seq * kv.head_dim, 0, kv.head_dim * 4, ctx->stream));
+    EC_CUDA_TRY(cudaMemsetAsync(l.meta + seq * 4, 0, 16, ctx->stream));
+    EC_CUDA_TRY(cudaMemsetAsync(l.heads + (((size_t)seq * l.tables) << l.bits), 0xFF,
+                                ((size_t)l.tables << l.bits) * 4, ctx->stream));
+    EC_CUDA_TRY(cudaMemsetAsync(l.counters + seq * 2, 0, 16, ctx->stream));
+  }
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  return EC_OK;
+}
+
+namespace {
+
+cudaError_t gemv(ec_ctx* ctx, int kind, const Mat& m, const ec::GemvPlan& plan, int pro,
+                 int epi, const float* x, const uint16_t* nw, float* y) {
+  // algorithmic bytes: weights + row scales + x (+ norm weight) + y (+ y read)
+  const double by = (double)m.rows * m.cols + 4.0 * m.rows + 4.0 * m.cols +
+                    (pro == ec::PRO_RMSNORM ? 2.0 * m.cols : 0.0) +
+                    (epi == ec::EPI_SWIGLU ? 2.0 * m.rows : 4.0 * m.rows) +
+                    (epi == ec::EPI_RESID ? 4.0 * m.rows : 0.0);
+  ProfScope ps(ctx, kind, by);
+  ec::GemvParams p{};
+  p.w = m.w;
+  p.scale = m.scale;
+  p.scale_stride = 1;
+  p.x = x;
+  p.norm_w = nw;
+  p.eps = ctx->c.norm_eps;
+  p.y = y;
+  p.N = m.rows;
+  p.K = m.cols;
+  p.silu_vec_limit = (m.rows / 2) & ~7;
+  p.err = ctx->err;
+  ctx->launches++;
+  return ec::gemv_launch(ctx->c.weight_kind, pro, epi, plan, p, ctx->stream, true);
+}
+
+// Enqueue one decode step for B sequences (tokens/pos in device memory).
+cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback) {
+  const ec_model_config& c = ctx->c;
+  const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
+  cudaError_t e;
+  ctx->launches = 0;
+  ec::StepBuffers sb{};
+  sb.rope_cos = ctx->rope_cos;
+  sb.rope_sin = ctx->rope_sin;
+  sb.sparse_k = c.sparse_k;
+  sb.window = c.window;
+  sb.sparse_blocks_k = c.sparse_blocks_k;
+  sb.err = ctx->err;
+  sb.max_sel = ctx->max_sel;
+  for (int b = 0; b < B; b++) {
+    // Batch-1 kernels: sequence b's state lives at offset b of every buffer.
+    float* x = ctx->x + (size_t)b * D;
+    sb.pos = pos + b;
+    sb.qkv = ctx->qkvb + (size_t)b * (H + 2 * KV) * hd;
+    sb.att = ctx->att + (size_t)b * H * hd;
+    sb.sel = ctx->sel + (size_t)b * ctx->max_sel;
+    sb.nsel = ctx->nsel + b;
+    ec::KvLayout kv = ctx->kv;
+    ec::LshLayout lsh = ctx->lsh;
+    const size_t per = (size_t)kv.n_layers * kv.max_blocks;
+    if (kv.paged) {
+      kv.kq += b * per * KV * 16 * hd;
+      kv.vq += b * per * KV * 16 * hd;
+      kv.ks += b * per * KV * 16;
+      kv.vs += b * per * KV * 16;
+      kv.centroid += b * per * hd;
+      kv.page_table += b * per;
+    } else {
+      kv.lk += (size_t)b * kv.n_layers * kv.seq_len * KV * hd;
+      kv.lv += (size_t)b * kv.n_layers * kv.seq_len * KV * hd;
+    }
+    if (lsh.tables > 0) {
+      lsh.acc += (size_t)b * hd;
+      lsh.meta += b * 4;
+      lsh.unit_hash += (size_t)b * lsh.tables * lsh.max_units;
+      lsh.unit_start += (size_t)b * lsh.max_units;
+      lsh.unit_len += (size_t)b * lsh.max_units;
+      lsh.heads += ((size_t)b * lsh.tables) << lsh.bits;
+      lsh.next += (size_t)b * lsh.tables * lsh.max_units;
+      lsh.counters += b * 2;
+    }
+    {
+      ProfScope ps(ctx, EC_K_EMBED, 2.0 * D + 4.0 * D);
+      if ((e = ec::launch_embed(ctx->emb, tokens + b, x, D, c.vocab_size, 1, ctx->stream, true)))
+        return e;
+    }
+    ctx->launches++;
+    for (int l = 0; l < c.n_layers; l++) {
+      if ((e = gemv(ctx, EC_K_GEMV_QKV, ctx->qkv[l], ctx->p_qkv, ec::PRO_RMSNORM, ec::EPI_STORE, x,
+                    ctx->attn_norm[l], sb.qkv)))
+        return e;
+      {
+        ProfScope ps(ctx, EC_K_KV_APPEND, 4.0 * (H + 2 * KV) * hd * 2 + 2.0 * KV * hd);
+        if ((e = ec::launch_kv_append(kv, lsh, sb, l, 1, ctx->stream, true))) return e;
+      }
+      ctx->launches++;
+      if (!kv.paged) {
+        ProfScope ps(ctx, EC_K_SELECT, 0.0);
+        if ((e = ec::launch_linear_select(kv, lsh, sb, l, 1, ctx->stream, true))) return e;
+        ctx->launches++;
+      }
+      {
+        ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
+        if ((e = ec::launch_attention(kv, sb, l, 1, ctx->stream, true))) return e;
+      }
+      ctx->launches++;
+      if ((e = gemv(ctx, EC_K_GEMV_O, ctx->wo[l], ctx->p_o, ec::PRO_NONE, ec::EPI_RESID, sb.att, nullptr, x)))
+        return e;
+      if ((e = gemv(ctx, EC_K_GEMV_GATEUP, ctx->w13[l], ctx->p_w13, ec::PRO_RMSNORM, ec::EPI_SWIGLU, x,
+                    ctx->ffn_norm[l], ctx->hbuf + (size_t)b * F)))
+        return e;
+      if ((e = gemv(ctx, EC_K_GEMV_DOWN, ctx->w2[l], ctx->p_w2, ec::PRO_NONE, ec::EPI_RESID,
+                    ctx->hbuf + (size_t)b * F, nullptr, x)))
+        return e;
+    }
+    float* lg = ctx->logits + (size_t)b * c.vocab_size;
+    if ((e = gemv(ctx, EC_K_GEMV_LM, ctx->lm, ctx->p_lm, ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->final_norm, lg)))
+      return e;
+    ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * c.vocab_size);
+    if ((e = ec::launch_argmax(lg, c.vocab_size, 1, ctx->argmax + b,
+                               feedback ? const_cast<int*>(tokens) + b : nullptr,
+                               feedback ? const_cast<int*>(pos) + b : nullptr, ctx->stream, true)))
+      return e;
+    ctx->launches++;
+  }
+  return cudaSuccess;
+}
+
+int check_weights(ec_ctx* ctx) {
+  const unsigned need = (1u << EC_WQ) | (1u << EC_WK) | (1u << EC_WV) | (1u << EC_WO) |
+                        (1u << EC_W1) | (1u << EC_W2) | (1u << EC_W3) | (1u << EC_ATTN_NORM) |
+                        (1u << EC_FFN_NORM);
+  for (int l = 0; l < ctx->c.n_layers; l++)
+    if ((ctx->have[l] & need) != need) return fail(EC_ERR_STATE, "layer weights missing");
+  if ((ctx->have_global & 7u) != 7u) return fail(EC_ERR_STATE, "global weights missing");
+  return EC_OK;
+}
+
+int run_step(ec_ctx* ctx, const int* tokens_dev, const int* pos_dev, int B, int feedback) {
+  if (B <= 0 || B > ctx->c.max_batch) return fail(EC_ERR_ARG, "B out of range");
+  int rc = check_weights(ctx);
+  if (rc) return rc;
+  const bool use_graph = getenv("EC_NO_GRAPH") == nullptr && !ctx->prof;
+  if (!use_graph) {
+    cudaError_t e = enqueue_step(ctx, tokens_dev, pos_dev, B, feedback != 0);
+    if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+    return EC_OK;
+  }
+  if (!ctx->gexec || ctx->g_B != B || ctx->g_fb != feedback || ctx->g_tok != tokens_dev ||
+      ctx->g_pos != pos_dev) {
+    if (ctx->gexec) {
+      cudaGraphExecDestroy(ctx->gexec);
+      ctx->gexec = nullptr;
+    }
+    cudaGraph_t g;
+    EC_CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = enqueue_step(ctx, tokens_dev, pos_dev, B, feedback != 0);
+    cudaError_t e2 = cudaStreamEndCapture(ctx->stream, &g);
+    if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+    if (e2 != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e2));
+    e = cudaGraphInstantiate(&ctx->gexec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+    ctx->g_B = B;
+    ctx->g_fb = feedback;
+    ctx->g_tok = tokens_dev;
+    ctx->g_pos = pos_dev;
+  }
+  EC_CUDA_TRY(cudaGraphLaunch(ctx->gexec, ctx->stream));
+  return EC_OK;
+}
+
+int check_err(ec_ctx* ctx) {
+  int h = 0;
+  EC_CUDA_TRY(cudaMemcpy(&h, ctx->err, 4, cudaMemcpyDeviceToHost));
+  if (h) {
+    cudaMemset(ctx->err, 0, 4);
+    return fail(h, "a bounded device wait timed out");
+  }
+  return EC_OK;
+}
+
+}  // namespace
+
+extern "C" int ec_decode_step_device(ec_ctx* ctx, int* tokens_dev, int* pos_dev, int B,
+                                     int greedy_feedback) {
+  if (!ctx || !tokens_dev || !pos_dev) return fail(EC_ERR_ARG, "null argument");
+  cudaSetDevice(ctx->device);
+  return run_step(ctx, tokens_dev, pos_dev, B, greedy_feedback);
+}
+
+extern "C" int ec_decode_step(ec_ctx* ctx, const int* tokens, const int* pos, int B,
+                              float* logits_host, int* argmax_host) {
+  if (!ctx || !tokens || !pos) return fail(EC_ERR_ARG, "null argument");
+  if (B <= 0 || B > ctx->c.max_batch) return fail(EC_ERR_ARG, "B out of range");
+  cudaSetDevice(ctx->device);
+  for (int b = 0; b < B; b++)
+    if (tokens[b] < 0 || tokens[b] >= ctx->c.vocab_size || pos[b] < 0)
+      return fail(EC_ERR_ARG, "token or position out of range");
+  EC_CUDA_TRY(cudaMemcpyAsync(ctx->tokens, tokens, B * 4, cudaMemcpyHostToDevice, ctx->stream));
+  EC_CUDA_TRY(cudaMemcpyAsync(ctx->pos, pos, B * 4, cudaMemcpyHostToDevice, ctx->stream));
+  int rc = run_step(ctx, ctx->tokens, ctx->pos, B, 0);
+  if (rc) return rc;
+  if (logits_host)
+    EC_CUDA_TRY(cudaMemcpyAsync(logits_host, ctx->logits, (size_t)B * ctx->c.vocab_size * 4,
+                                cudaMemcpyDeviceToHost, ctx->stream));
+  if (argmax_host)
+    EC_CUDA_TRY(cudaMemcpyAsync(argmax_host, ctx->argmax, B * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (ctx->prof) prof_collect(ctx);
+  return check_err(ctx);
+}
+
+extern "C" float* ec_logits_device(ec_ctx* ctx) { return ctx ? ctx->logits : nullptr; }
+extern "C" int* ec_argmax_device(ec_ctx* ctx) { return ctx ? ctx->argmax : nullptr; }
+extern "C" void* ec_stream(ec_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+extern "C" int ec_synchronize(ec_ctx* ctx) {
+  if (!ctx) return fail(EC_ERR_ARG, "null argument");
+  cudaSetDevice(ctx->device);
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (ctx->prof) prof_collect(ctx);
+  return check_err(ctx);
+}
+
+extern "C" int ec_profile_enable(ec_ctx* ctx, int on) {
+  if (!ctx) return fail(EC_ERR_ARG, "null argument");
+  cudaSetDevice(ctx->device);
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  prof_collect(ctx);
+  ctx->prof = on != 0;
+  for (int k = 0; k < EC_K_COUNT; k++) {
+    ctx->prof_ms[k] = 0;
+    ctx->prof_n[k] = 0;
+    ctx->prof_bytes[k] = 0;
+  }
+  return EC_OK;
+}
+
+extern "C" int ec_profile_read(ec_ctx* ctx, int kind, double* ms, int* launches, double* bytes) {
+  if (!ctx || kind < 0 || kind >= EC_K_COUNT) return fail(EC_ERR_ARG, "bad argument");
+  cudaSetDevice(ctx->device);
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  prof_collect(ctx);
+  if (ms) *ms = ctx->prof_ms[kind];
+  if (launches) *launches = ctx->prof_n[kind];
+  if (bytes) *bytes = ctx->prof_bytes[kind];
+  return EC_OK;
+}
+
+extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
+  if (!ctx) return 0;
+  const int per_layer = ctx->kv.paged ? 6 : 7;
+  return B * (1 + ctx->c.n_layers * per_layer + 2);
+}
+
+extern "C" int ec_read_state(ec_ctx* ctx, int which, int seq, float* out, size_t n) {
+  if (!ctx || !out || seq < 0 || seq >= ctx->c.max_batch) return fail(EC_ERR_ARG, "bad argument");
+  cudaSetDevice(ctx->device);
+  const ec_model_config& c = ctx->c;
+  const int qkvw = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+  const float* src = nullptr;
+  size_t cnt = 0;
+  switch (which) {
+    case 0: src = ctx->x + (size_t)seq * c.dim; cnt = c.dim; break;
+    case 2: src = ctx->qkvb + (size_t)seq * qkvw; cnt = (size_t)c.n_heads * c.head_dim; break;
+    case 3: src = ctx->qkvb + (size_t)seq * qkvw + c.n_heads * c.head_dim;
+            cnt = (size_t)c.n_kv_heads * c.head_dim; break;
+    case 4: src = ctx->qkvb + (size_t)seq * qkvw + (c.n_heads + c.n_kv_heads) * c.head_dim;
+            cnt = (size_t)c.n_kv_heads * c.head_dim; break;
+    case 5: src = ctx->att + (size_t)seq * c.n_heads * c.head_dim;
+            cnt = (size_t)c.n_heads * c.head_dim; break;
+    case 6: src = ctx->logits + (size_t)seq * c.vocab_size; cnt = c.vocab_size; break;
+    case 7: src = ctx->hbuf + (size_t)seq * c.hidden_dim; cnt = c.hidden_dim; break;
+    case 8: {
+      // attended selection of the last attention launch: [n, ids...] as floats
+      int ns = 0;
+      EC_CUDA_TRY(cudaMemcpy(&ns, ctx->nsel + seq, 4, cudaMemcpyDeviceToHost));
+      std::vector<int> ids(ctx->max_sel);
+      EC_CUDA_TRY(cudaMemcpy(ids.data(), ctx->sel + (size_t)seq * ctx->max_sel,
+                             ctx->max_sel * 4, cudaMemcpyDeviceToHost));
+      if (n < 1) return fail(EC_ERR_ARG, "buffer too small");
+      out[0] = (float)ns;
+      for (int i = 0; i < ns && (size_t)(i + 1) < n; i++) out[i + 1] = (float)ids[i];
+      return EC_OK;
+    }
+    default: return fail(EC_ERR_ARG, "unknown state id");
+  }
+  if (n < cnt) return fail(EC_ERR_ARG, "buffer too small");
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  EC_CUDA_TRY(cudaMemcpy(out, src, cnt * 4, cudaMemcpyDeviceToHost));
+  return EC_OK;
+}
+
+extern "C" int ec_read_lsh(ec_ctx* ctx, int seq, int* n_units, uint32_t* unit_hash,
+                           int* unit_start, int* unit_len, int* heads, int* next) {
+  if (!ctx || seq < 0 || seq >= ctx->c.max_batch) return fail(EC_ERR_ARG, "bad argument");
+  const ec::LshLayout& l = ctx->lsh;
+  if (l.tables <= 0) return fail(EC_ERR_STATE, "LSH disabled");
+  cudaSetDevice(ctx->device);
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  int meta[4];
+  EC_CUDA_TRY(cudaMemcpy(meta, l.meta + seq * 4, 16, cudaMemcpyDeviceToHost));
+  if (n_units) *n_units = meta[2];
+  const size_t mu = l.max_units, tb = (size_t)seq * l.tables;
+  if (unit_hash)
+    EC_CUDA_TRY(cudaMemcpy(unit_hash, l.unit_hash + tb * mu, l.tables * mu * 4, cudaMemcpyDeviceToHost));
+  if (unit_start)
+    EC_CUDA_TRY(cudaMemcpy(unit_start, l.unit_start + seq * mu, mu * 4, cudaMemcpyDeviceToHost));
+  if (unit_len)
+    EC_CUDA_TRY(cudaMemcpy(unit_len, l.unit_len + seq * mu, mu * 4, cudaMemcpyDeviceToHost));
+  if (heads)
+    EC_CUDA_TRY(cudaMemcpy(heads, l.heads + (tb << l.bits), ((size_t)l.tables << l.bits) * 4,
+                           cudaMemcpyDeviceToHost));
+  if (next) EC_CUDA_TRY(cudaMemcpy(next, l.next + tb * mu, l.tables * mu * 4, cudaMemcpyDeviceToHost));
+  return EC_OK;
+}
+
+extern "C" int ec_read_counters(ec_ctx* ctx, int seq, unsigned long long* out2) {
+  if (!ctx || !out2 || seq < 0 || seq >= ctx->c.max_batch) return fail(EC_ERR_ARG, "bad argument");
+  if (ctx->lsh.tables <= 0) {
+    out2[0] = out2[1] = 0;
+    return EC_OK;
+  }
+  cudaSetDevice(ctx->device);
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  EC_CUDA_TRY(cudaMemcpy(out2, ctx->lsh.counters + seq * 2, 16, cudaMemcpyDeviceToHost));
+  return EC_OK;
+}
+
+// ------------------------------------------------------------------------
+// per-op entry points
+// ------------------------------------------------------------------------
+extern "C" int ec_op_gemv(int wkind, const void* w, const float* scale, const float* x, float* y,
+                          int m, int k, void* stream) {
+  if (!w || !x || !y || m <= 0 || k <= 0) return fail(EC_ERR_ARG, "bad argument");
+  if (wkind != EC_W_BF16 && !scale) return fail(EC_ERR_ARG, "scale required");
+  if (k % 32) return fail(EC_ERR_UNSUPPORTED, "k must be a multiple of 32");
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  EC_CUDA_TRY(ec::gemv_prepare());
+  ec::GemvPlan plan;
+  if (!ec::gemv_plan(wkind, m, k, ec::EPI_STORE, nsm, &plan))
+    return fail(EC_ERR_UNSUPPORTED, "no GEMV plan for this shape");
+  ec::GemvParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.scale = scale;
+  p.scale_stride = (wkind == EC_W_INT8) ? 1 : 0;
+  p.x = x;
+  p.y = y;
+  p.N = m;
+  p.K = k;
+  EC_CUDA_TRY(ec::gemv_launch(wkind, ec::PRO_NONE, ec::EPI_STORE, plan, p,
+                              static_cast<cudaStream_t>(stream), false));
+  return EC_OK;
+}
+
+extern "C" int ec_op_rmsnorm(float* out, const float* x, const uint16_t* w, int n, float eps,
+                             void* stream) {
+  if (!out || !x || !w || n <= 0) return fail(EC_ERR_ARG, "bad argument");
+  EC_CUDA_TRY(ec::launch_rmsnorm(out, x, w, n, eps, static_cast<cudaStream_t>(stream)));
+  return EC_OK;
+}
+
+extern "C" int ec_op_rope(float* data, int n_heads, int head_dim, int pos, const float* cos_t,
+                          const float* sin_t, int max_seq, void* stream) {
+  if (!data || !cos_t || !sin_t || head_dim % 2 || n_heads <= 0) return fail(EC_ERR_ARG, "bad argument");
+  EC_CUDA_TRY(ec::launch_rope(data, n_heads, head_dim, pos, cos_t, sin_t, max_seq,
+                              static_cast<cudaStream_t>(stream)));
+  return EC_OK;
+}
+
+extern "C" int ec_op_silu_mul(float* out, const float* gate, const float* up, int n, void* stream) {
+  if (!out || !gate || !up || n <= 0) return fail(EC_ERR_ARG, "bad argument");
+  EC_CUDA_TRY(ec::launch_silu(out, gate, up, n, static_cast<cudaStream_t>(stream)));
+  return EC_OK;
+}
+
+extern "C" int ec_op_quant_int8(int8_t* out, float* scales, const float* in, int rows, int n,
+                                void* stream) {
+  if (!out || !scales || !in || rows <= 0 || n <= 0) return fail(EC_ERR_ARG, "bad argument");
+  EC_CUDA_TRY(ec::launch_quant(out, scales, in, rows, n, static_cast<cudaStream_t>(stream)));
+  return EC_OK;
+}
+
+extern "C" int ec_op_argmax(const float* logits, int n, int B, int* out, void* stream) {
+  if (!logits || !out || n <= 0 || B <= 0) return fail(EC_ERR_ARG, "bad argument");
+  EC_CUDA_TRY(ec::launch_argmax(logits, n, B, out, nullptr, nullptr,
+                                static_cast<cudaStream_t>(stream), false));
+  return EC_OK;
+}
+
+extern "C" int ec_op_paged_append(const ec_paged_view* pv, const float* k, const float* v, int pos,
+                                  void* stream) {
+  (void)pv; (void)k; (void)v; (void)pos; (void)stream;
+  return fail(EC_ERR_UNSUPPORTED, "not built yet");
+}
+
+extern "C" int ec_op_paged_attention(const ec_paged_view* pv, const float* q, float* out,
+                                     int n_heads, int n_tokens, int sparse_blocks_k,
+                                     int* selected_out, int* n_selected_out, void* stream) {
+  (void)pv; (void)q; (void)out; (void)n_heads; (void)n_tokens; (void)sparse_blocks_k;
+  (void)selected_out; (void)n_selected_out; (void)stream;
+  return fail(EC_ERR_UNSUPPORTED, "not built yet");
+}

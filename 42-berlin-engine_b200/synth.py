@@ -157,3 +157,75 @@ def make_model(cfg, seed=1234, kind="int8", pow2=True):
 
 def prompt(cfg, n, seed=99):
     return np.random.default_rng(seed).integers(0, cfg.vocab_size, n).astype(np.int32)
+
+
+class DeviceModel:
+    """A synthetic model generated on a CUDA device with torch (same
+    distributions as make_model), for shapes too large to generate on the
+    host quickly.  torch is used for device memory only."""
+
+    def __init__(self, cfg, seed=1234, device=0, kind="int8"):
+        import torch
+        self.cfg, self.kind, self.seed = cfg, kind, seed
+        self.dev = torch.device("cuda", device)
+        self.torch = torch
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(seed)
+        self._g = g
+
+    def _normal(self, shape, scale):
+        t = self.torch.randn(shape, generator=self._g, device=self.dev, dtype=self.torch.float32)
+        return t.mul_(scale)
+
+    def quant(self, w):
+        """INT8 per row with power-of-two scales (as quant_int8_rows)."""
+        torch = self.torch
+        amax = w.abs().amax(dim=1).clamp_min(1e-30)
+        s = torch.exp2(torch.ceil(torch.log2(amax / 127.0)))
+        q = torch.round(w / s[:, None]).clamp_(-127, 127).to(torch.int8)
+        return q, s.to(torch.float32).contiguous()
+
+    def bf16(self, t):
+        return t.to(self.torch.bfloat16).contiguous()
+
+    def generate(self, sink):
+        """Call sink(kind, layer, name, tensor, scale) for every tensor, one
+        at a time (so only one fp32 matrix is alive)."""
+        cfg = self.cfg
+        shapes = mat_shapes(cfg)
+        emb = self.bf16(self._normal((cfg.vocab_size, cfg.dim), 0.02))
+        sink("emb", -1, "emb", emb, None)
+        del emb
+        for i in range(cfg.n_layers):
+            for n in MATS:
+                q, s = self.quant(self._normal(shapes[n], 0.02))
+                sink("mat", i, n, q, s)
+                del q, s
+            for n in ("attention_norm", "ffn_norm"):
+                sink("norm", i, n, self.bf16(1.0 + self._normal((cfg.dim,), 0.1)), None)
+        sink("norm", -1, "final_norm", self.bf16(1.0 + self._normal((cfg.dim,), 0.1)), None)
+        q, s = self.quant(self._normal((cfg.vocab_size, cfg.dim), 0.02))
+        sink("mat", -1, "lm", q, s)
+
+    def bf16_weights(self):
+        """Host BF16 copies of q * scale (exact) for the reference's path."""
+        torch = self.torch
+        out = {"layers": [dict() for _ in range(self.cfg.n_layers)]}
+
+        def host_bf16(t):
+            return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+        def sink(kind, layer, name, t, s):
+            if kind == "mat":
+                v = host_bf16((t.to(torch.float32) * s[:, None]).to(torch.bfloat16))
+            else:
+                v = host_bf16(t)
+            if layer < 0:
+                out[name] = v
+            else:
+                out["layers"][layer][name] = v
+
+        self.torch.manual_seed(0)
+        self._g.manual_seed(self.seed)
+        self.generate(sink)
+        return out

@@ -1,0 +1,352 @@
+"""Decode throughput of the B200 hot path (BASELINE.json metric: decode tok/s).
+
+Workload: Llama-3-8B-shaped random-init decoder, INT8
+per-channel weights (power-of-two scales), paged INT8 KV cache (the
+reference's default mode), a 2048-token random prompt already in the cache,
+then greedy decode at batch 1 per GPU.  One step = one decode token of every
+sequence.  Multi-GPU: one process per GPU, independent sequences (weak
+scaling, no collective on the data path); value = tokens of all ranks /
+max-over-ranks time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+
+`--impl reference` times the reference engine's own CPU decode
+(oracle/_ref, transformer_forward over BF16 weights equal to the INT8
+weights) on the host cores, rank 0 only.
+"""
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "42-berlin-engine_b200")
+
+
+def _load(name):
+    key = "ec_" + name
+    if key in sys.modules:
+        return sys.modules[key]
+    spec = importlib.util.spec_from_file_location(key, os.path.join(PKG, name + ".py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[key] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+METRIC = "decode tok/s (Llama-3-8B-shaped INT8, b=1 per GPU, 2k context)"
+PROMPT = 2048
+SEED = 1234
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads):
+    """The reference's transformer_forward on the host (oracle/_ref), or the
+    C restatement when the reference was not built here."""
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle  # CPU baseline leg only
+    if oracle.ref_available():
+        m, kind = oracle.RefModel(model_src, use_paged_kv=True, sparse_k=64), "reference"
+    else:
+        m, kind = oracle.PortModel(model_src), "port"
+    toks = _load("synth").prompt(cfg, n_prompt, seed=7)
+    for p in range(n_prompt):
+        lg = m.forward(int(toks[p]), p)
+    tok = int(np.argmax(lg))
+    pos = n_prompt
+    for _ in range(warmup):
+        lg = m.forward(tok, pos)
+        tok, pos = int(np.argmax(lg)), pos + 1
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lg = m.forward(tok, pos)
+        tok, pos = int(np.argmax(lg)), pos + 1
+    dt = time.perf_counter() - t0
+    return steps / dt, kind
+
+
+def run_reference(args):
+    ws, rank, local = dist_setup()
+    if rank != 0:
+        return
+    S = _load("synth")
+    cfg = S.LLAMA3_8B
+    threads = os.cpu_count() or 1
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            raise RuntimeError("no device for weight generation")
+        src = S.DeviceModel(cfg, seed=SEED, device=0)
+        src_model = _HostWeights(cfg, src.bf16_weights())
+        torch.cuda.empty_cache()
+    except Exception as exc:  # generate on the host instead
+        print(f"[bench] device generation unavailable ({exc}); host generation", file=sys.stderr)
+        src_model = S.make_model(cfg, seed=SEED)
+    n_prompt = 16
+    val, kind = cpu_baseline(cfg, src_model, n_prompt, args.steps, args.warmup, threads)
+    sample = (f"{args.steps} decode steps after a {n_prompt}-token prompt (context "
+              f"{n_prompt}..{n_prompt + args.steps + args.warmup} instead of 2k: the step is "
+              f"dominated by the 16 GB of BF16 weight reads either way)")
+    line = {"metric": METRIC, "value": round(val, 4), "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / val, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "llama3-8b-shape decode b=1", "global_batch": 1,
+                       "weights": "bf16 (= int8 * pow2 scale)", "kv": "paged int8"},
+            "cpu_baseline": {"value": round(val, 4), "unit": "tok/s", "cores": threads,
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": round(val, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+class _HostWeights:
+    """Adapter: a config plus precomputed BF16 host weights for RefModel."""
+
+    def __init__(self, cfg, bf):
+        self.cfg, self._bf = cfg, bf
+
+    def bf16_weights(self):
+        return self._bf
+
+
+def run_cuda(args):
+    import torch
+    ws, rank, local = dist_setup()
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    eng = _load("engine")
+    S = _load("synth")
+    cfg = S.LLAMA3_8B
+    B = 1
+    e = eng.Engine(cfg, device=local, max_batch=B)
+    src = S.DeviceModel(cfg, seed=SEED, device=local)
+
+    def sink(kind, layer, name, t, s):
+        if kind == "emb":
+            e.set_weight_device(-1, eng.EC_EMBEDDING, t.data_ptr(), 0)
+        elif kind == "norm":
+            which = {"attention_norm": eng.EC_ATTN_NORM, "ffn_norm": eng.EC_FFN_NORM,
+                     "final_norm": eng.EC_FINAL_NORM}[name]
+            e.set_weight_device(layer, which, t.data_ptr(), 0)
+        else:
+            which = eng.EC_LM_HEAD if layer < 0 else eng.MAT_IDS[name]
+            e.set_weight_device(layer, which, t.data_ptr(), s.data_ptr())
+
+    src.generate(sink)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    # prompt: 2048 random tokens through the decode path (KV cache filled)
+    prompt = S.prompt(cfg, PROMPT, seed=7 + rank)
+    for p in range(PROMPT):
+        _, am = e.step([prompt[p]], [p], want_logits=False)
+    tok = torch.tensor([int(am[0])], dtype=torch.int32, device=f"cuda:{local}")
+    pos = torch.tensor([PROMPT], dtype=torch.int32, device=f"cuda:{local}")
+    stream = torch.cuda.ExternalStream(e.stream())
+
+    def steps(n):
+        for _ in range(n):
+            e.step_device(tok.data_ptr(), pos.data_ptr(), B, True)
+
+    steps(args.warmup)
+    e.sync()
+    if ws > 1:
+        torch.distributed.barrier()
+    with Clocks(local) as clk:
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        steps(args.steps)
+        ev1.record(stream)
+        e.sync()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / args.steps
+    if ws > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    value = ws * B * 1000.0 / ms
+
+    # end to end through the C ABI with host buffers (token/pos in, logits out)
+    cur_tok, cur_pos = int(tok.item()), int(pos.item())
+    host_logits = np.empty((B, cfg.vocab_size), np.float32)
+    for _ in range(2):
+        lg, am = e.step([cur_tok], [cur_pos])
+        cur_tok, cur_pos = int(am[0]), cur_pos + 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lg, am = e.step([cur_tok], [cur_pos])
+        cur_tok, cur_pos = int(am[0]), cur_pos + 1
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+    if ws > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    del host_logits
+
+    # live per-kernel timing (profiling mode: events around each launch)
+    e.profile(True)
+    for _ in range(3):
+        lg, am = e.step([cur_tok], [cur_pos], want_logits=False)
+        cur_tok, cur_pos = int(am[0]), cur_pos + 1
+    prof = e.profile_read()
+    e.profile(False)
+    gemv = [k for k in prof if k.startswith("gemv")]
+    g_ms = sum(prof[k]["ms"] for k in gemv)
+    g_n = sum(prof[k]["launches"] for k in gemv)
+    g_by = sum(prof[k]["bytes"] for k in gemv)
+    tot_ms = sum(v["ms"] for v in prof.values())
+    peak, peak_kind = peaks()
+    achieved = (g_by / g_n) / (g_ms / g_n * 1e-3) / 1e9 if g_n else 0.0
+    weight_bytes = (sum(int(np.prod(s)) for s in S.mat_shapes(cfg).values()) * cfg.n_layers
+                    + cfg.vocab_size * cfg.dim)
+    kv_tok = cfg.n_layers * cfg.n_kv_heads * (cfg.head_dim * 2 + 8)
+    att_tokens = min(PROMPT + args.warmup + args.steps, 64 * 16)
+    step_bytes = weight_bytes + kv_tok * att_tokens
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": "llama3-8b-shape decode b=1 per GPU", "global_batch": ws * B,
+                       "context": PROMPT, "weights": "int8 per-row pow2 scale",
+                       "kv": "paged int8", "parallelism": f"dp{ws} (replicas)",
+                       "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"},
+            "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
+                    "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B * (cfg.vocab_size + 1)},
+            "gpu_launches": e.launches_per_step(B) * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "gemv (all weight-streaming launches)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": peak_kind,
+                         "step_frac": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4),
+                         "step_bytes": step_bytes},
+            "kernel_ms_per_step": {k: round(v["ms"] / 3, 4) for k, v in prof.items()},
+            "kernel_share": {k: round(v["ms"] / tot_ms, 4) for k, v in prof.items() if tot_ms},
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            del src
+            torch.cuda.empty_cache()
+            threads = os.cpu_count() or 1
+            try:
+                src2 = S.DeviceModel(cfg, seed=SEED, device=local)
+                hw = _HostWeights(cfg, src2.bf16_weights())
+                del src2
+                torch.cuda.empty_cache()
+                cps, kind = cpu_baseline(cfg, hw, 16, max(2, min(args.steps, 8)), 1, threads)
+                line["cpu_baseline"] = {
+                    "value": round(cps, 4), "unit": "tok/s", "cores": threads, "kind": kind,
+                    "sample": "8B-shape decode steps after a 16-token prompt (weights-bound)"}
+            except Exception as exc:
+                line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": threads,
+                                        "kind": "reference", "sample": f"failed: {exc}"}
+        print(json.dumps(line), flush=True)
+    e.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+
+
+if __name__ == "__main__":
+    main()

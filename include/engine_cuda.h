@@ -1,0 +1,220 @@
+/*
+** engine_cuda.h -- C ABI of libengine_cuda.so, the B200 (sm_100a) decode hot
+** path for fgroo/42-Berlin-Engine.
+**
+** Plain C: pointers, sizes and status codes; no CUDA, C++ or torch types.
+** Streams are passed as `void *` (a cudaStream_t, NULL = legacy default).
+** Every function returns EC_OK (0) or a negative EC_ERR_* code; it never
+** exits the process.  ec_last_error() gives a human-readable reason.
+**
+** Two layers:
+**   1. The fused decode path (ec_create ... ec_decode_step): one context per
+**      t_transformer owns the device copy of the weights (INT8 per-row or
+**      FP8-E4M3 per-tensor), the KV cache, the RoPE tables and the LSH index,
+**      and runs transformer_forward (src/inference/inference.c:60) for B
+**      independent sequences per call.
+**   2. Per-op entry points (ec_op_*) on caller-owned device buffers, one per
+**      reference op on that path, for hosts that keep their own loop.
+** The file:line after each declaration names the reference interface it
+** replaces.
+*/
+#ifndef ENGINE_CUDA_H
+# define ENGINE_CUDA_H
+# include <stddef.h>
+# include <stdint.h>
+
+# ifdef __cplusplus
+extern "C" {
+# endif
+
+# define EC_OK 0
+# define EC_ERR_ARG (-1)          /* bad argument / shape */
+# define EC_ERR_CUDA (-2)         /* CUDA runtime error */
+# define EC_ERR_OOM (-3)          /* device allocation failed / pool full */
+# define EC_ERR_STATE (-4)        /* call out of order (e.g. weights missing) */
+# define EC_ERR_UNSUPPORTED (-5)  /* shape or mode this build does not run */
+# define EC_ERR_TIMEOUT (-6)      /* a bounded device wait gave up */
+
+/* weight formats */
+# define EC_W_INT8 0   /* int8 [rows][cols] + fp32 scale per row */
+# define EC_W_FP8 1    /* E4M3 [rows][cols] + one fp32 scale per matrix */
+# define EC_W_BF16 2   /* bf16 [rows][cols], no scale (per-op GEMV only) */
+
+/* matrix ids for ec_set_weight (layer >= 0) */
+# define EC_WQ 0
+# define EC_WK 1
+# define EC_WV 2
+# define EC_WO 3
+# define EC_W1 4       /* gate */
+# define EC_W2 5       /* down */
+# define EC_W3 6       /* up */
+# define EC_ATTN_NORM 7
+# define EC_FFN_NORM 8
+/* global tensors (layer = -1) */
+# define EC_EMBEDDING 16
+# define EC_FINAL_NORM 17
+# define EC_LM_HEAD 18
+
+typedef struct ec_model_config
+{
+	int		dim;
+	int		hidden_dim;
+	int		n_layers;
+	int		n_heads;
+	int		n_kv_heads;
+	int		vocab_size;
+	int		seq_len;		/* max positions per sequence (RoPE table rows) */
+	int		head_dim;
+	float	rope_theta;
+	float	norm_eps;
+	int		weight_kind;	/* EC_W_INT8 or EC_W_FP8 */
+	int		use_paged_kv;	/* 1: paged INT8 KV (reference default);
+							** 0: linear BF16 KV with LSH-routed top-K */
+	int		sparse_k;		/* linear mode top-K (SPARSE_K, config.h:67) */
+	int		window;			/* ATTN_WINDOW_SIZE (config.h:79) */
+	int		sparse_blocks_k;/* SPARSE_BLOCKS_K (config.h:73) */
+	int		lsh_tables;		/* 1 in the reference */
+	int		lsh_bits;		/* LSH_NUM_HASHES (ops_lsh.h:33), <= 16 */
+	int		lsh_unit;		/* LSH_BLOCK_SIZE (ops_lsh.h:35): tokens per hash */
+	int		lsh_max_units;	/* LSH_MAX_BLOCKS (ops_lsh.h:36) */
+	int		lsh_radius;		/* LSH_HAMMING_RADIUS (ops_lsh.h:37) */
+	int		lsh_max_cand;	/* candidate units per query (inference.c:300) */
+	int		max_batch;		/* sequences per decode step */
+}	ec_model_config;
+
+typedef struct ec_ctx	ec_ctx;
+
+const char	*ec_last_error(void);
+
+/* Fill `c` with the reference's compile-time defaults (config.h, ops_lsh.h)
+** and the Llama-3-8B shape; callers then override the shape. */
+int		ec_config_default(ec_model_config *c);
+
+/* transformer_init (src/inference/model.c:146): bind a device, allocate the
+** KV pool, upload RoPE tables and LSH hyperplanes computed on the host by
+** the reference's formulas (ops_rope.c:30-96, ops_lsh.c:22-85). */
+int		ec_create(const ec_model_config *c, int device, ec_ctx **out);
+void	ec_destroy(ec_ctx *ctx);
+
+/* Register one tensor (model.c:167-265 weight mapping).  `data` is a host
+** pointer unless `on_device` is nonzero.  Matrices are row-major
+** [out_features][in_features] in the context's weight_kind; `scales` holds
+** one float per row (INT8) or one float (FP8).  Norm weights and the
+** embedding are BF16 and take scales = NULL.  Data is copied. */
+int		ec_set_weight(ec_ctx *ctx, int layer, int which, const void *data,
+			const float *scales, int on_device);
+
+/* Start sequence `seq` fresh (paged_kv_reset, paged.c:297; lsh_index_reset,
+** ops_lsh.c:111). */
+int		ec_reset(ec_ctx *ctx, int seq);
+
+/* transformer_forward (src/inference/inference.c:60) for B sequences:
+** sequence b takes token tokens[b] at position pos[b] (host arrays).
+** logits_host (B * vocab floats) and argmax_host (B ints, the reference's
+** sample_argmax, sampler.c:145) may each be NULL.  Synchronous. */
+int		ec_decode_step(ec_ctx *ctx, const int *tokens, const int *pos, int B,
+			float *logits_host, int *argmax_host);
+
+/* Same step with tokens/positions already in device memory and results left
+** in device memory (ec_logits_device / ec_argmax_device); asynchronous on
+** the context's stream.  `greedy_feedback` != 0 writes each sequence's argmax
+** back into tokens_dev and increments pos_dev, so repeated calls decode
+** greedily without host round trips. */
+int		ec_decode_step_device(ec_ctx *ctx, int *tokens_dev, int *pos_dev, int B,
+			int greedy_feedback);
+float	*ec_logits_device(ec_ctx *ctx);
+int		*ec_argmax_device(ec_ctx *ctx);
+void	*ec_stream(ec_ctx *ctx);
+int		ec_synchronize(ec_ctx *ctx);
+
+/* Tracing: with profiling on, decode steps run without the CUDA graph and
+** every kernel launch is bracketed by CUDA events on the context's stream.
+** ec_profile_read returns, for one kernel kind (EC_K_*), the summed device
+** time in ms, the number of launches and the summed algorithmic bytes. */
+# define EC_K_GEMV_QKV 0
+# define EC_K_GEMV_O 1
+# define EC_K_GEMV_GATEUP 2
+# define EC_K_GEMV_DOWN 3
+# define EC_K_GEMV_LM 4
+# define EC_K_KV_APPEND 5
+# define EC_K_SELECT 6
+# define EC_K_ATTENTION 7
+# define EC_K_EMBED 8
+# define EC_K_ARGMAX 9
+# define EC_K_COUNT 10
+int		ec_profile_enable(ec_ctx *ctx, int on);
+int		ec_profile_read(ec_ctx *ctx, int kind, double *ms, int *launches,
+			double *bytes);
+
+/* Introspection for parity checks (device -> host copies). */
+int		ec_read_state(ec_ctx *ctx, int which, int seq, float *out, size_t n);
+int		ec_read_lsh(ec_ctx *ctx, int seq, int *n_units, uint32_t *unit_hash,
+			int *unit_start, int *unit_len, int *heads, int *next);
+int		ec_read_counters(ec_ctx *ctx, int seq, unsigned long long *out2);
+int		ec_launches_per_step(ec_ctx *ctx, int B);
+
+/* ------------------------------------------------------------------------ */
+/* Per-op entry points on caller-owned device buffers                        */
+/* ------------------------------------------------------------------------ */
+
+/* op_matmul for batch-1 activations (src/compute/ops.h:33,
+** ops_matmul.c:366-392): y[m] = W[m][k] . x[k] in the reference's 32-lane
+** accumulation order, times scale[row] (INT8) / scale[0] (FP8).
+** k must be a multiple of 32. */
+int		ec_op_gemv(int wkind, const void *w, const float *scale, const float *x,
+			float *y, int m, int k, void *stream);
+
+/* op_rmsnorm (src/compute/ops.h:34, ops_norm.c:126); out may alias x. */
+int		ec_op_rmsnorm(float *out, const float *x, const uint16_t *w, int n,
+			float eps, void *stream);
+
+/* rope_apply_multihead_cached (src/compute/ops_rope.h:80) with device copies
+** of the cos/sin tables [max_seq][head_dim/2]. */
+int		ec_op_rope(float *data, int n_heads, int head_dim, int pos,
+			const float *cos_t, const float *sin_t, int max_seq, void *stream);
+
+/* op_silu_mul (src/compute/ops.h:41); out may alias gate. */
+int		ec_op_silu_mul(float *out, const float *gate, const float *up, int n,
+			void *stream);
+
+/* quant_f32_to_int8 (src/compute/ops_quant.c:229) on `rows` vectors of n. */
+int		ec_op_quant_int8(int8_t *out, float *scales, const float *in, int rows,
+			int n, void *stream);
+
+/* sample_argmax (src/compute/sampler.h:19) of B rows of n logits. */
+int		ec_op_argmax(const float *logits, int n, int B, int *out, void *stream);
+
+/* One layer's paged INT8 KV cache in device memory
+** (t_kv_block / t_block_manager, src/memory/paged.h:53-88). */
+typedef struct ec_paged_view
+{
+	int8_t		*k;			/* [blocks][n_kv_heads][16][head_dim] */
+	int8_t		*v;
+	float		*k_scale;	/* [blocks][n_kv_heads][16] */
+	float		*v_scale;
+	float		*centroid;	/* [blocks][head_dim], KV head 0 mean */
+	const int	*page_table;/* [max_logical] logical -> physical block */
+	int			n_kv_heads;
+	int			head_dim;
+}	ec_paged_view;
+
+/* paged_kv_append (src/memory/paged.h:143) of one token at `pos`: quantise
+** k, v (F32 [n_kv_heads*head_dim], device) and store; computes the block
+** centroid when the block fills (calc_block_centroid_int8, paged.c:350). */
+int		ec_op_paged_append(const ec_paged_view *pv, const float *k,
+			const float *v, int pos, void *stream);
+
+/* op_paged_attention (ops_attention.h:75) over logical blocks
+** [0, n_tokens/16] with n_tokens cached tokens, or, when n_blocks >
+** sparse_blocks_k, score_blocks + select_top_k_blocks +
+** op_paged_attention_sparse (paged.h:200-212, ops_attention.h:82) as
+** inference.c:447-489 drives them.  selected_out (optional, device,
+** sparse_blocks_k ints) receives the logical blocks attended. */
+int		ec_op_paged_attention(const ec_paged_view *pv, const float *q,
+			float *out, int n_heads, int n_tokens, int sparse_blocks_k,
+			int *selected_out, int *n_selected_out, void *stream);
+
+# ifdef __cplusplus
+}
+# endif
+#endif
