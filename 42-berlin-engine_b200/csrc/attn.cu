@@ -21,6 +21,31 @@ namespace ec {
 
 constexpr int kBlk = 16;  // tokens per KV block (KV_BLOCK_SIZE, paged.h:35)
 
+// Paged K rows are stored rotated: 16-byte piece p of token t (within its
+// block) sits at piece (p + t) mod (hd/16), so threads scoring consecutive
+// tokens read different banks.  Byte offset of element d:
+__device__ __forceinline__ int kswz(int t, int d, int hd) {
+  return ((((d >> 4) + t) & ((hd >> 4) - 1)) << 4) | (d & 15);
+}
+
+// Phase timestamps for performance work (build with -DEC_PHASE_TIMING):
+// slot s of g_phase_ts gets %globaltimer when one thread passes mark s.
+#ifdef EC_PHASE_TIMING
+__device__ long long g_phase_ts[64];
+#define PHASE_MARK(cond, s)                                                 \
+  do {                                                                      \
+    if (cond) {                                                             \
+      long long t_;                                                         \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));               \
+      g_phase_ts[s] = t_;                                                   \
+    }                                                                       \
+  } while (0)
+#else
+#define PHASE_MARK(cond, s) \
+  do {                      \
+  } while (0)
+#endif
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -29,7 +54,7 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // quant_f32_to_int8 (ops_quant.c:229-273) of one vector of n <= 256 floats by
 // one warp.  Returns the scale.
-__device__ float warp_quant_int8(const float* in, int8_t* out, int n, int lane) {
+__device__ float warp_quant_int8(const float* in, int8_t* out, int n, int lane, int rot = -1) {
   float mx = 0.0f;
   for (int i = lane; i < n; i += 32) mx = fmaxf(mx, fabsf(in[i]));
   mx = warp_max(mx);
@@ -44,7 +69,7 @@ __device__ float warp_quant_int8(const float* in, int8_t* out, int n, int lane) 
   for (int i = lane; i < n; i += 32) {
     int v = (int)roundf(__fmul_rn(in[i], inv));
     v = v > 127 ? 127 : (v < -127 ? -127 : v);
-    out[i] = (int8_t)v;
+    out[rot >= 0 ? kswz(rot, i, n) : i] = (int8_t)v;
   }
   return scale;
 }
@@ -52,17 +77,24 @@ __device__ float warp_quant_int8(const float* in, int8_t* out, int n, int lane) 
 // ------------------------------------------------------------------------
 // KV append: one CTA per sequence.
 // ------------------------------------------------------------------------
+__device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int layer, int b);
+
 __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout lsh, StepBuffers sb,
                                                         int layer) {
-  const int b = blockIdx.x;
+  const int b = blockIdx.y;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim, half = hd >> 1;
   pdl_launch_dependents();
   pdl_wait();
+  if (blockIdx.x == 1) {
+    paged_select_cta(kv, sb, layer, b);
+    return;
+  }
   const int pos = sb.pos[b];
-  float* q = sb.qkv + (long)b * (H + 2 * KV) * hd;
-  float* k = q + H * hd;
+  const float* q = sb.qkv + (long)b * (H + 2 * KV) * hd;
+  float* qo = sb.qrot + (long)b * H * hd;
+  float* k = sb.qkv + (long)b * (H + 2 * KV) * hd + H * hd;
   float* v = k + KV * hd;
 
   // RoPE (rope_apply_multihead_cached, ops_rope.c:192-231); no-op past the table
@@ -71,11 +103,14 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
     const float* sr = sb.rope_sin + (long)pos * half;
     for (int i = tid; i < (H + KV) * half; i += blockDim.x) {
       const int head = i / half, j = i - head * half;
-      float* p = (head < H) ? q + head * hd : k + (head - H) * hd;
-      const float c = cr[j], s = sr[j], v0 = p[j], v1 = p[j + half];
-      p[j] = __fmaf_rn(v0, c, -__fmul_rn(v1, s));
-      p[j + half] = __fmaf_rn(v0, s, __fmul_rn(v1, c));
+      const float* src = (head < H) ? q + head * hd : k + (head - H) * hd;
+      float* dst = (head < H) ? qo + head * hd : k + (head - H) * hd;
+      const float c = cr[j], s = sr[j], v0 = src[j], v1 = src[j + half];
+      dst[j] = __fmaf_rn(v0, c, -__fmul_rn(v1, s));
+      dst[j + half] = __fmaf_rn(v0, s, __fmul_rn(v1, c));
     }
+  } else {
+    for (int i = tid; i < H * hd; i += blockDim.x) qo[i] = q[i];
   }
   __syncthreads();
 
@@ -88,7 +123,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
         const bool isv = h >= KV;
         const int kh = isv ? h - KV : h;
         int8_t* dst = (isv ? kv.vq : kv.kq) + ((blk * KV + kh) * kBlk + off) * hd;
-        const float sc = warp_quant_int8((isv ? v : k) + kh * hd, dst, hd, lane);
+        const float sc = warp_quant_int8((isv ? v : k) + kh * hd, dst, hd, lane, isv ? -1 : off);
         if (lane == 0) (isv ? kv.vs : kv.ks)[(blk * KV + kh) * kBlk + off] = sc;
       }
       __syncthreads();
@@ -97,7 +132,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
         for (int d = tid; d < hd; d += blockDim.x) {
           float c = 0.0f;
           for (int t = 0; t < kBlk; t++)
-            c = __fadd_rn(c, __fmul_rn((float)kv.kq[((blk * KV) * kBlk + t) * hd + d],
+            c = __fadd_rn(c, __fmul_rn((float)kv.kq[((blk * KV) * kBlk + t) * hd + kswz(t, d, hd)],
                                        kv.ks[(blk * KV) * kBlk + t]));
           kv.centroid[blk * hd + d] = __fmul_rn(c, __fdiv_rn(1.0f, (float)kBlk));
         }
@@ -187,35 +222,58 @@ __device__ __forceinline__ float dot_bf16_ref(const uint16_t* a, const float* b,
   return s;
 }
 
-// min-heap primitives on shared arrays (ops_heap.h:40-100)
-__device__ void heap_sift_up(float* hs, int* hi, int i) {
-  while (i > 0) {
-    const int p = (i - 1) >> 1;
-    if (hs[p] <= hs[i]) break;
-    float ts = hs[i]; hs[i] = hs[p]; hs[p] = ts;
-    int ti = hi[i]; hi[i] = hi[p]; hi[p] = ti;
-    i = p;
+// Min-heap replay of heap_push (ops_heap.h:40-100) on shared arrays.
+// Stored 1-based (node n at [n], children 2n, 2n+1 adjacent) so a level of
+// sift-down reads both children with one 8-byte load; the element being
+// placed is carried in registers ("hole" sifting).  Comparisons are the
+// reference's: sift-up stops when parent <= value; sift-down picks the left
+// child unless the right one is strictly smaller, and moves on only while the
+// chosen child is strictly smaller than the value.
+__device__ __forceinline__ void heap_up(float* hs, int* hi, int n, float v, int vi) {
+  while (n > 1) {
+    const int p = n >> 1;
+    const float ps = hs[p];
+    if (ps <= v) break;
+    hs[n] = ps;
+    hi[n] = hi[p];
+    n = p;
   }
+  hs[n] = v;
+  hi[n] = vi;
 }
 
-__device__ void heap_sift_down(float* hs, int* hi, int size, int i) {
+__device__ __forceinline__ void heap_down(float* hs, int* hi, int size, float v, int vi) {
+  int n = 1;
   for (;;) {
-    int s = i;
-    const int l = 2 * i + 1, r = 2 * i + 2;
-    if (l < size && hs[l] < hs[s]) s = l;
-    if (r < size && hs[r] < hs[s]) s = r;
-    if (s == i) break;
-    float ts = hs[i]; hs[i] = hs[s]; hs[s] = ts;
-    int ti = hi[i]; hi[i] = hi[s]; hi[s] = ti;
-    i = s;
+    const int l = 2 * n;
+    if (l > size) break;
+    int c = l;
+    float cs;
+    if (l + 1 <= size) {
+      const float2 pr = *reinterpret_cast<const float2*>(hs + l);
+      cs = pr.x;
+      if (pr.y < pr.x) {
+        c = l + 1;
+        cs = pr.y;
+      }
+    } else {
+      cs = hs[l];
+    }
+    if (!(cs < v)) break;
+    hs[n] = cs;
+    hi[n] = hi[c];
+    n = c;
   }
+  hs[n] = v;
+  hi[n] = vi;
 }
 
 // Replays heap_push over (score[i], idx[i]) i < n with capacity cap, by one
 // warp: a ballot drops candidates that cannot beat the current root (the
-// root only grows), lane 0 performs the pushes that can.  Result in heap
-// array order.  Returns the heap size.
-// idx == nullptr means candidate i carries index i + idx_base.
+// root only grows), lane 0 performs the pushes that can.  hs/hi hold cap + 2
+// entries (1-based, hs 8-byte aligned).  The result, in the reference's heap
+// array order, is hi[1 .. size].  idx == nullptr means candidate i carries
+// index i + idx_base.
 __device__ int warp_heap_topk(const float* score, const int* idx, int n, int cap, float* hs,
                               int* hi, int lane, int idx_base = 0) {
   int size = 0;
@@ -231,19 +289,14 @@ __device__ int warp_heap_topk(const float* score, const int* idx, int n, int cap
       const float sL = __shfl_sync(0xffffffffu, sv, L);
       const int iL = __shfl_sync(0xffffffffu, iv, L);
       if (lane == 0) {
-        if (size < cap) {
-          hs[size] = sL;
-          hi[size] = iL;
-          heap_sift_up(hs, hi, size);
-        } else if (sL > hs[0]) {
-          hs[0] = sL;
-          hi[0] = iL;
-          heap_sift_down(hs, hi, size, 0);
-        }
+        if (size < cap)
+          heap_up(hs, hi, size + 1, sL, iL);
+        else if (sL > hs[1])
+          heap_down(hs, hi, size, sL, iL);
       }
       __syncwarp();
       if (size < cap) size++;
-      root = hs[0];
+      root = hs[1];
       pend &= ~(1u << L);
       if (size >= cap) pend &= __ballot_sync(0xffffffffu, sv > root);
     }
@@ -259,9 +312,9 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;  // candidate capacity
   int* cand = reinterpret_cast<int*>(smem);               // [cap_c]
   float* cscore = reinterpret_cast<float*>(cand + cap_c);  // [cap_c]
-  float* hs = cscore + cap_c;                             // [sparse_k]
-  int* hi = reinterpret_cast<int*>(hs + sb.sparse_k);     // [sparse_k]
-  float* qm = reinterpret_cast<float*>(hi + sb.sparse_k);  // [hd]
+  float* hs = cscore + cap_c;                             // [sparse_k + 2], 1-based
+  int* hi = reinterpret_cast<int*>(hs + sb.sparse_k + 2);  // [sparse_k + 2]
+  float* qm = reinterpret_cast<float*>(hi + sb.sparse_k + 2);  // [hd]
   __shared__ uint32_t s_code[16];
   __shared__ int s_units[64];
   __shared__ int s_nu, s_nc, s_wcount;
@@ -270,7 +323,7 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
   pdl_wait();
   const int pos = sb.pos[b];
   const int kv_len = min(pos + 1, kv.seq_len);
-  const float* q = sb.qkv + (long)b * (H + 2 * KV) * hd;
+  const float* q = sb.qrot + (long)b * H * hd;
   if (!(sb.sparse_k > 0 && kv_len > sb.sparse_k)) {
     if (tid == 0) sb.nsel[b] = -1;  // dense attention over [0, kv_len)
     return;
@@ -370,7 +423,7 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
     const int cap = nc < sb.sparse_k ? nc : sb.sparse_k;
     const int size = warp_heap_topk(cscore, cand, nc, cap, hs, hi, lane);
     int* out = sb.sel + (long)b * sb.max_sel;
-    for (int i = lane; i < size; i += 32) out[i] = hi[i];
+    for (int i = lane; i < size; i += 32) out[i] = hi[i + 1];
     if (lane == 0) {
       sb.nsel[b] = size;
       lsh.counters[b * 2] += 1ull;
@@ -379,27 +432,148 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
   }
 }
 
+// heap_push over score[0..n) (indices i + idx_base) with capacity cap, by
+// one thread; result hi[1..size] in the reference's heap array order.
+__device__ int heap_topk_seq(const float* score, int n, int cap, float* hs, int* hi,
+                             int idx_base) {
+  int size = 0;
+  int i = 0;
+  for (; i < n && size < cap; i++) heap_up(hs, hi, ++size, score[i], i + idx_base);
+  float root = size ? hs[1] : 0.0f;
+#pragma unroll 4
+  for (; i < n; i++) {
+    const float s = score[i];
+    if (s > root) {
+      heap_down(hs, hi, size, s, i + idx_base);
+      root = hs[1];
+    }
+  }
+  return size;
+}
+
+// ------------------------------------------------------------------------
+// Paged block selection (inference.c:447-469): with more than
+// SPARSE_BLOCKS_K blocks, score_blocks (paged.c:401-431, query head 0 .
+// centroid) and select_top_k_blocks (paged.c:439-495: first, last, then
+// heap_push of blocks 1..nb-2, heap array order).  Only full middle blocks
+// are scored, so this runs concurrently with this step's append.  Writes
+// sel[b] / nsel[b] (nsel = -1: attend to every block).
+// ------------------------------------------------------------------------
+__device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int layer, int b) {
+  constexpr int kChunkBlocks = 32;  // centroids staged per round (16 KB at hd 128)
+  __shared__ __align__(16) float s_q[256];
+  __shared__ __align__(16) float s_c[2 * kChunkBlocks * 128];
+  __shared__ int s_nsel;
+  __shared__ __align__(16) float s_bsc[2048];
+  __shared__ __align__(16) float s_hs[68];
+  __shared__ int s_hi[68];
+  __shared__ __align__(8) uint64_t s_bar[2];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim, half = hd >> 1;
+  if (!kv.paged) return;
+  const int pos = sb.pos[b];
+  const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
+  const int nb = (n_tok + kBlk - 1) / kBlk;
+  if (nb <= sb.sparse_blocks_k || nb > 2048 || hd > 128) {
+    if (tid == 0) sb.nsel[b] = -1;
+    return;
+  }
+  PHASE_MARK(tid == 0 && layer == 1, 0);
+  if (tid == 0) {
+    mbar_init(&s_bar[0], 1);
+    mbar_init(&s_bar[1], 1);
+    fence_mbar_init();
+  }
+  // query head 0, rotated here (the append CTA rotates its own copy)
+  const float* q = sb.qkv + (long)b * (H + 2 * KV) * hd;
+  for (int j = tid; j < half; j += blockDim.x) {
+    const float v0 = q[j], v1 = q[j + half];
+    if (pos < kv.seq_len) {
+      const float c = sb.rope_cos[(long)pos * half + j], s = sb.rope_sin[(long)pos * half + j];
+      s_q[j] = __fmaf_rn(v0, c, -__fmul_rn(v1, s));
+      s_q[j + half] = __fmaf_rn(v0, s, __fmul_rn(v1, c));
+    } else {
+      s_q[j] = v0;
+      s_q[j + half] = v1;
+    }
+  }
+  __syncthreads();
+  const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
+  const int* pt = kv.page_table + base;
+  // score_blocks over the middle blocks 1 .. nb-2: centroids staged in rounds
+  // of kChunkBlocks (double-buffered); 8 threads per block run the 8 lanes of
+  // simd_dot_f32_f32 and combine them in its horizontal-sum order
+  const int nmid = nb - 2;
+  const int nround = (nmid + kChunkBlocks - 1) / kChunkBlocks;
+  auto issue = [&](int r) {
+    const int c0 = 1 + r * kChunkBlocks;
+    const int cn = min(kChunkBlocks, nb - 1 - c0);
+    float* dst = s_c + (r & 1) * kChunkBlocks * 128;
+    if (lane == 0) mbar_expect_tx(&s_bar[r & 1], (uint32_t)(cn * hd * 4));
+    __syncwarp();
+    for (int i = lane; i < cn; i += 32)
+      bulk_g2s(dst + i * hd, kv.centroid + (base + pt[c0 + i]) * hd, hd * 4, &s_bar[r & 1]);
+  };
+  if (warp == 0) issue(0);
+  bool ok = true;
+  for (int r = 0; r < nround; r++) {
+    if (warp == 0 && r + 1 < nround) issue(r + 1);
+    if (ok) ok = mbar_wait(&s_bar[r & 1], (r >> 1) & 1, sb.err);
+    const int c0 = 1 + r * kChunkBlocks;
+    const int cn = min(kChunkBlocks, nb - 1 - c0);
+    const float* cb = s_c + (r & 1) * kChunkBlocks * 128;
+    const int blk = tid >> 3, l = tid & 7;
+    float acc = 0.0f;
+    if (blk < cn && ok)
+      for (int d = l; d < hd; d += 8) acc = __fmaf_rn(s_q[d], cb[blk * hd + d], acc);
+    // ((c0+c4)+(c1+c5)) + ((c2+c6)+(c3+c7))
+    const float h4 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+    const float t2 = __fadd_rn(h4, __shfl_xor_sync(0xffffffffu, h4, 1));
+    const float sum = __fadd_rn(t2, __shfl_xor_sync(0xffffffffu, t2, 2));
+    if (blk < cn && l == 0) s_bsc[c0 + blk] = sum;
+    __syncthreads();
+  }
+  int m = sb.sparse_blocks_k - 2;
+  if (m > nb - 2) m = nb - 2;
+  if (m > 62) m = 62;
+  PHASE_MARK(tid == 0 && layer == 1, 1);
+  if (tid == 0) {
+    const int size = heap_topk_seq(s_bsc + 1, nmid, m, s_hs, s_hi, 1);
+    PHASE_MARK(true && layer == 1, 2);
+    s_nsel = size;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int size = s_nsel;
+    int* out = sb.sel + (long)b * sb.max_sel;
+    if (lane == 0) {
+      out[0] = 0;
+      out[1] = nb - 1;
+      sb.nsel[b] = 2 + size;
+    }
+    for (int i = lane; i < size; i += 32) out[2 + i] = s_hi[1 + i];
+  }
+}
+
 // ------------------------------------------------------------------------
 // Attention: one CTA per (query head, sequence).
-//   1. selection: paged blocks (dense, or centroid scores + min-heap replay in
-//      the reference's order) or the linear-mode position list;
-//   2. the selected K rows land in shared memory by bulk copies issued by
-//      one warp; scores in the reference's dot order;
-//   3. running max by a max-scan, both exponentials per token in parallel;
-//   4. V rows land in the same buffer; threads 0..hd-1 run the output
+//   1. the selected K rows (paged blocks in selection order, or linear-mode
+//      positions) land in shared memory by bulk copies issued by one warp;
+//      scores in the reference's dot order;
+//   2. running max by a max-scan, both exponentials per token in parallel;
+//   3. V rows land in the same buffer; threads 0..hd-1 run the output
 //      recurrence for one dimension each, the next warp the denominator.
 // ------------------------------------------------------------------------
-constexpr int kAttnThreads = 160;
+constexpr int kAttnThreads = 512;
 constexpr int kMaxSel = 68;  // SPARSE_BLOCKS_K + 2, rounded
 
 struct AttnSmemLayout {
-  size_t kv, sc, sf, tks, tvs, lpos, bsc, bsel, boff, bphys, bfill, ksb, vsb, total;
+  size_t kv, sc, sf, tks, tvs, lpos, boff, bphys, bfill, ksb, vsb, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-__host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int esize,
-                                                      int max_blocks) {
+__host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int esize) {
   AttnSmemLayout L;
   size_t o = 256 * 4;  // q head
   L.kv = o;
@@ -414,10 +588,6 @@ __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int e
   o += (size_t)max_tok * 4;
   L.lpos = o;
   o += (size_t)max_tok * 4;
-  L.bsc = o;
-  o += ((size_t)max_blocks + 128) * 4;
-  L.bsel = o;
-  o += ((size_t)max_blocks + kMaxSel) * 4;
   L.boff = o;
   o += kMaxSel * 4;
   L.bphys = o;
@@ -433,6 +603,11 @@ __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int e
   return L;
 }
 
+// stored int8 byte -> exact float of its signed value
+__device__ __forceinline__ float s8_to_f32(uint32_t byte) {
+  return __fsub_rn(__uint_as_float(byte ^ 0x4B000080u), 8388736.0f);
+}
+
 template <bool PAGED>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, StepBuffers sb,
                                                                  int layer, int max_tok) {
@@ -441,7 +616,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim;
   const int kvh = h / (H / KV);
-  const AttnSmemLayout Ly = attn_layout(max_tok, hd, ES, kv.max_blocks);
+  const AttnSmemLayout Ly = attn_layout(max_tok, hd, ES);
   float* qs = reinterpret_cast<float*>(smem);
   uint8_t* kvb = smem + Ly.kv;
   float* sc = reinterpret_cast<float*>(smem + Ly.sc);
@@ -449,8 +624,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   float* tks = reinterpret_cast<float*>(smem + Ly.tks);
   float* tvs = reinterpret_cast<float*>(smem + Ly.tvs);
   int* lpos = reinterpret_cast<int*>(smem + Ly.lpos);
-  float* bsc = reinterpret_cast<float*>(smem + Ly.bsc);
-  int* bsel = reinterpret_cast<int*>(smem + Ly.bsel);
+  uint8_t* ttok = reinterpret_cast<uint8_t*>(lpos);  // paged: token index within its block
   int* boff = reinterpret_cast<int*>(smem + Ly.boff);
   int* bphys = reinterpret_cast<int*>(smem + Ly.bphys);
   int* bfill = reinterpret_cast<int*>(smem + Ly.bfill);
@@ -467,49 +641,26 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   }
   pdl_launch_dependents();
   pdl_wait();
+  const bool mk = (h == 0 && b == 0 && layer == 1);
+  (void)mk;
+  PHASE_MARK(mk && tid == 0, 8);
   const int pos = sb.pos[b];
-  const float* qg = sb.qkv + (long)b * (H + 2 * KV) * hd;
+  const float* qg = sb.qrot + (long)b * H * hd;
   for (int d = tid; d < hd; d += blockDim.x) qs[d] = qg[h * hd + d];
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  __syncthreads();
   bool ok = true;
 
-  // ---------------------------------------------------------- selection
+  // ------------------------------------------ selected blocks / positions
   if constexpr (PAGED) {
     const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
     const int nb = (n_tok + kBlk - 1) / kBlk;
     const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
     const int* pt = kv.page_table + base;
-    if (nb > sb.sparse_blocks_k) {
-      // score_blocks (paged.c:401-431) with query head 0
-      for (int i = tid; i < nb; i += blockDim.x)
-        bsc[i] = dot8_f32(qg, kv.centroid + (base + pt[i]) * hd, hd);
-      __syncthreads();
-      // select_top_k_blocks (paged.c:439-495): first, last, then heap_push of
-      // blocks 1..nb-2 with capacity m, in the reference's heap array order
-      int m = sb.sparse_blocks_k - 2;
-      if (m > nb - 2) m = nb - 2;
-      if (m > 62) m = 62;
-      if (warp == 0) {
-        float* hs = bsc + kv.max_blocks;  // [64]
-        int* hi = reinterpret_cast<int*>(hs + 64);
-        const int size = warp_heap_topk(bsc + 1, nullptr, nb - 2, m, hs, hi, lane, 1);
-        if (lane == 0) {
-          bsel[0] = 0;
-          bsel[1] = nb - 1;
-          s_nsel = 2 + size;
-        }
-        __syncwarp();
-        for (int i = lane; i < size; i += 32) bsel[2 + i] = hi[i];
-      }
-    } else {
-      for (int i = tid; i < nb; i += blockDim.x) bsel[i] = i;
-      if (tid == 0) s_nsel = nb;
-    }
-    __syncthreads();
-    const int nsel = s_nsel;
+    const int ns = sb.nsel[b];
+    const int* sel = sb.sel + (long)b * sb.max_sel;
+    const int nsel = ns > 0 ? ns : nb;  // selection order, or every block in order
     for (int k = tid; k < nsel; k += blockDim.x) {
-      const int lb = bsel[k];
+      const int lb = ns > 0 ? sel[k] : k;
       bphys[k] = (int)(base + pt[lb]);
       bfill[k] = (lb == nb - 1) ? n_tok - lb * kBlk : kBlk;
     }
@@ -521,10 +672,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
         n += bfill[k];
       }
       s_ntok = n;
-      if (h == 0 && sb.nsel) {
-        for (int i = 0; i < nsel; i++) sb.sel[(long)b * sb.max_sel + i] = bsel[i];
-        sb.nsel[b] = nsel;
-      }
+      s_nsel = nsel;
     }
     __syncthreads();
     const int T = s_ntok;
@@ -541,11 +689,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
       }
     }
     ok = mbar_wait(&bar[0], 0, sb.err);
-    for (int k = tid; k < nsel; k += blockDim.x)
-      for (int t = 0; t < bfill[k]; t++) {
-        tks[boff[k] + t] = ksb[k * 16 + t];
-        tvs[boff[k] + t] = vsb[k * 16 + t];
+    for (int j = tid; j < nsel * kBlk; j += blockDim.x) {
+      const int k = j >> 4, t = j & 15;
+      if (t < bfill[k]) {
+        tks[boff[k] + t] = ksb[j];
+        tvs[boff[k] + t] = vsb[j];
+        ttok[boff[k] + t] = (uint8_t)t;
       }
+    }
   } else {
     const int kv_len = min(pos + 1, kv.seq_len);
     const int ns = sb.nsel[b];
@@ -567,23 +718,32 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   }
   __syncthreads();
   const int T = s_ntok;
+  PHASE_MARK(mk && tid == 0, 9);
 
   // ------------------------------------------------------------- scores
   for (int i = tid; i < T && ok; i += blockDim.x) {
     float s;
     if constexpr (PAGED) {
-      const int8_t* kr = reinterpret_cast<const int8_t*>(kvb) + (size_t)i * hd;
+      // piece c of this token's row sits at (c + t) mod np (stored rotated)
+      const uint8_t* kr = kvb + (size_t)i * hd;
+      const int t = ttok[i];
       const float ksc = tks[i];
+      const int np = hd >> 4;
       float acc[8];
 #pragma unroll
       for (int l = 0; l < 8; l++) acc[l] = 0.0f;
-      for (int d = 0; d < hd; d += 8) {
-        const uint2 u = *reinterpret_cast<const uint2*>(kr + d);
-        float w[8];
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        if (c >= np) break;
+        const uint4 u = *reinterpret_cast<const uint4*>(kr + (((c + t) & (np - 1)) << 4));
+        float w[16];
         dec_i8x4(u.x, w);
         dec_i8x4(u.y, w + 4);
+        dec_i8x4(u.z, w + 8);
+        dec_i8x4(u.w, w + 12);
 #pragma unroll
-        for (int l = 0; l < 8; l++) acc[l] = __fmaf_rn(qs[d + l], __fmul_rn(w[l], ksc), acc[l]);
+        for (int l = 0; l < 16; l++)
+          acc[l & 7] = __fmaf_rn(qs[16 * c + l], __fmul_rn(w[l], ksc), acc[l & 7]);
       }
       s = hsum8(acc);
     } else {
@@ -592,6 +752,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
     sc[i] = __fmul_rn(s, scale);
   }
   __syncthreads();
+  PHASE_MARK(mk && tid == 0, 10);
   // V rows into the same buffer (K is no longer needed)
   if (warp == 0 && ok) {
     if constexpr (PAGED) {
@@ -638,38 +799,105 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
     }
   }
   __syncthreads();
+  // flag per 8 tokens: every scale factor is 1 (the running max did not move)
+  int* ones = reinterpret_cast<int*>(tks);  // K scales are no longer needed
+  for (int g = tid; g < (T >> 3); g += blockDim.x) {
+    bool a1 = true;
+#pragma unroll
+    for (int u = 0; u < 8; u++) a1 = a1 && (sf[8 * g + u] == 1.0f);
+    ones[g] = a1;
+  }
+  __syncthreads();
+  PHASE_MARK(mk && tid == 0, 11);
   if (ok) ok = mbar_wait(&bar[1], 0, sb.err);
+  PHASE_MARK(mk && tid == 0, 12);
 
   // -------------------------------------------------------- recurrences
+  // out_t = fma(re_t, v_t, out_{t-1} * sf_t); with sf_t == 1 the multiply is
+  // the identity and runs of eight such steps skip it.
   const int cw = (hd + 31) >> 5;  // chain warps
   if (warp == cw) {
     if (lane == 0) {
       float sum = 0.0f;
-      for (int i = 0; i < T; i++) sum = __fmaf_rn(sum, sf[i], sc[i]);
+      int i = 0;
+      for (; i + 8 <= T; i += 8) {
+        const float4 f0 = *reinterpret_cast<const float4*>(sf + i);
+        const float4 f1 = *reinterpret_cast<const float4*>(sf + i + 4);
+        const float4 r0 = *reinterpret_cast<const float4*>(sc + i);
+        const float4 r1 = *reinterpret_cast<const float4*>(sc + i + 4);
+        sum = __fmaf_rn(sum, f0.x, r0.x);
+        sum = __fmaf_rn(sum, f0.y, r0.y);
+        sum = __fmaf_rn(sum, f0.z, r0.z);
+        sum = __fmaf_rn(sum, f0.w, r0.w);
+        sum = __fmaf_rn(sum, f1.x, r1.x);
+        sum = __fmaf_rn(sum, f1.y, r1.y);
+        sum = __fmaf_rn(sum, f1.z, r1.z);
+        sum = __fmaf_rn(sum, f1.w, r1.w);
+      }
+      for (; i < T; i++) sum = __fmaf_rn(sum, sf[i], sc[i]);
       s_sum = sum;
     }
   } else if (tid < hd && ok) {
     const int d = tid;
     float o = 0.0f;
-    if constexpr (PAGED) {
-      const int8_t* vb = reinterpret_cast<const int8_t*>(kvb) + d;
-#pragma unroll 4
-      for (int i = 0; i < T; i++) {
-        const float vv = __fmul_rn((float)vb[(size_t)i * hd], tvs[i]);
-        const float f = sf[i];
-        o = (f == 1.0f) ? __fmaf_rn(sc[i], vv, o) : __fmaf_rn(sc[i], vv, __fmul_rn(o, f));
+    // one group of 8 tokens: raw exps, dequantised values, all-ones flag;
+    // the next group is loaded before the current one's FMA chain runs
+    auto load = [&](int i, float* r, float* vv, int& fl) {
+      const float4 r0 = *reinterpret_cast<const float4*>(sc + i);
+      const float4 r1 = *reinterpret_cast<const float4*>(sc + i + 4);
+      r[0] = r0.x; r[1] = r0.y; r[2] = r0.z; r[3] = r0.w;
+      r[4] = r1.x; r[5] = r1.y; r[6] = r1.z; r[7] = r1.w;
+      if constexpr (PAGED) {
+        const float4 s0 = *reinterpret_cast<const float4*>(tvs + i);
+        const float4 s1 = *reinterpret_cast<const float4*>(tvs + i + 4);
+        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int u = 0; u < 8; u++) vv[u] = __fmul_rn(s8_to_f32(kvb[(size_t)(i + u) * hd + d]), sv[u]);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          vv[u] = bf16_to_f32(reinterpret_cast<const uint16_t*>(kvb)[(size_t)(i + u) * hd + d]);
       }
-    } else {
-      const uint16_t* vb = reinterpret_cast<const uint16_t*>(kvb) + d;
-#pragma unroll 4
-      for (int i = 0; i < T; i++) {
-        const float vv = bf16_to_f32(vb[(size_t)i * hd]);
-        const float f = sf[i];
-        o = (f == 1.0f) ? __fmaf_rn(sc[i], vv, o) : __fmaf_rn(sc[i], vv, __fmul_rn(o, f));
+      fl = ones[i >> 3];
+    };
+    int i = 0;
+    if (T >= 8) {
+      float rn[8], vn[8];
+      int fn;
+      load(0, rn, vn, fn);
+      for (; i + 8 <= T; i += 8) {
+        float r[8], vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          r[u] = rn[u];
+          vv[u] = vn[u];
+        }
+        const int fl = fn;
+        if (i + 16 <= T) load(i + 8, rn, vn, fn);
+        if (fl) {
+#pragma unroll
+          for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], o);
+        } else {
+          const float4 f0 = *reinterpret_cast<const float4*>(sf + i);
+          const float4 f1 = *reinterpret_cast<const float4*>(sf + i + 4);
+          const float f[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+#pragma unroll
+          for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], __fmul_rn(o, f[u]));
+        }
       }
     }
+    for (; i < T; i++) {
+      float vv;
+      if constexpr (PAGED)
+        vv = __fmul_rn(s8_to_f32(kvb[(size_t)i * hd + d]), tvs[i]);
+      else
+        vv = bf16_to_f32(reinterpret_cast<const uint16_t*>(kvb)[(size_t)i * hd + d]);
+      o = __fmaf_rn(sc[i], vv, __fmul_rn(o, sf[i]));
+    }
     qs[d] = o;  // q no longer needed
+    PHASE_MARK(mk && d == 0, 13);
   }
+  PHASE_MARK(mk && warp == cw && lane == 0, 14);
   __syncthreads();
   if (tid < hd) {
     float o = qs[tid];
@@ -686,7 +914,7 @@ static int attn_max_tok(const KvLayout& kv, const StepBuffers& sb) {
 
 static size_t attn_smem(const KvLayout& kv, const StepBuffers& sb, int max_tok) {
   (void)sb;
-  return attn_layout(max_tok, kv.head_dim, kv.paged ? 1 : 2, kv.max_blocks).total;
+  return attn_layout(max_tok, kv.head_dim, kv.paged ? 1 : 2).total;
 }
 
 template <typename K, typename... Args>
@@ -705,6 +933,12 @@ static cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaS
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+#ifdef EC_PHASE_TIMING
+extern "C" int ec_debug_phase_times(long long* out) {
+  return cudaMemcpyFromSymbol(out, g_phase_ts, sizeof(g_phase_ts)) == cudaSuccess ? 0 : -2;
+}
+#endif
+
 cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb) {
   const int max_tok = attn_max_tok(kv, sb);
   const int smem = (int)attn_smem(kv, sb, max_tok);
@@ -715,7 +949,7 @@ cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuf
     e = cudaFuncSetAttribute(attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;
-  const int ssel = cap_c * 8 + sb.sparse_k * 8 + 256 * 4;
+  const int ssel = cap_c * 8 + (sb.sparse_k + 2) * 8 + 256 * 4;
   if (!e && ssel <= 227 * 1024)
     e = cudaFuncSetAttribute(linear_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ssel);
@@ -724,13 +958,14 @@ cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuf
 
 cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                              int layer, int B, cudaStream_t s, bool pdl) {
-  return launch_ex(kv_append_kernel, dim3(B), dim3(256), 0, s, pdl, kv, lsh, sb, layer);
+  return launch_ex(kv_append_kernel, dim3(kv.paged ? 2 : 1, B), dim3(256), 0, s, pdl, kv, lsh, sb,
+                   layer);
 }
 
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                                  int layer, int B, cudaStream_t s, bool pdl) {
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;
-  const size_t smem = (size_t)cap_c * 8 + (size_t)sb.sparse_k * 8 + 256 * 4;
+  const size_t smem = (size_t)cap_c * 8 + (size_t)(sb.sparse_k + 2) * 8 + 256 * 4;
   return launch_ex(linear_select_kernel, dim3(B), dim3(256), smem, s, pdl, kv, lsh, sb, layer);
 }
 

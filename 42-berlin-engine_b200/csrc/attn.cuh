@@ -38,7 +38,8 @@ struct LshLayout {
 
 struct StepBuffers {
   const int* pos;       // [B]
-  float* qkv;           // [B][(H + 2KV) * hd]  (q rotated in place)
+  float* qkv;           // [B][(H + 2KV) * hd] projections (k rotated in place)
+  float* qrot;          // [B][H * hd] rotated queries
   float* att;           // [B][H * hd]
   int* sel;             // [B][L?] per-sequence selection scratch: [B][max_sel]
   int* nsel;            // [B]
@@ -51,6 +52,9 @@ struct StepBuffers {
 
 // Shared-memory attributes for the current device (outside stream capture).
 cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb);
+// Per layer, before attention: one CTA appends the token (RoPE, INT8 or BF16
+// store, centroid, LSH update); in paged mode a second CTA selects the
+// blocks to attend (it only reads blocks that this step does not change).
 cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                              int layer, int B, cudaStream_t s, bool pdl);
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,

@@ -48,7 +48,8 @@ struct ec_ctx {
   // state
   ec::KvLayout kv{};
   ec::LshLayout lsh{};
-  float *x = nullptr, *qkvb = nullptr, *att = nullptr, *hbuf = nullptr, *logits = nullptr;
+  float *x = nullptr, *qkvb = nullptr, *qrot = nullptr, *att = nullptr, *hbuf = nullptr,
+        *logits = nullptr;
   int *argmax = nullptr, *tokens = nullptr, *pos = nullptr, *sel = nullptr, *nsel = nullptr;
   int* err = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
@@ -192,9 +193,9 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   if (!cfg || !out) return fail(EC_ERR_ARG, "null argument");
   const ec_model_config& c = *cfg;
   if (c.dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
-      c.n_heads % c.n_kv_heads || c.head_dim % 32 || c.head_dim > 128 || c.dim % 32 ||
+      c.n_heads % c.n_kv_heads || (c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128) || c.dim % 32 ||
       c.hidden_dim % 32 || c.vocab_size <= 0 || c.seq_len <= 0 || c.max_batch <= 0)
-    return fail(EC_ERR_UNSUPPORTED, "unsupported model shape (head_dim <= 128, dims % 32)");
+    return fail(EC_ERR_UNSUPPORTED, "unsupported model shape (head_dim 32, 64 or 128; dims % 32)");
   if (c.weight_kind != EC_W_INT8 && c.weight_kind != EC_W_FP8)
     return fail(EC_ERR_ARG, "weight_kind must be EC_W_INT8 or EC_W_FP8");
   if (c.lsh_tables < 0 || c.lsh_tables > 16 || c.lsh_bits < 1 || c.lsh_bits > 16 ||
@@ -202,6 +203,8 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     return fail(EC_ERR_UNSUPPORTED, "LSH settings out of range");
   if (c.sparse_blocks_k < 1 || c.sparse_blocks_k > 64)
     return fail(EC_ERR_UNSUPPORTED, "sparse_blocks_k must be in 1..64 (select_top_k_blocks)");
+  if (c.use_paged_kv && c.seq_len > 32768)
+    return fail(EC_ERR_UNSUPPORTED, "paged KV supports seq_len <= 32768 (2048 blocks)");
   if (!c.use_paged_kv && c.sparse_k <= 0)
     return fail(EC_ERR_UNSUPPORTED, "linear KV mode needs sparse_k > 0");
   cudaError_t e = cudaSetDevice(device);
@@ -253,6 +256,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   TRY(dalloc(ctx, &ctx->x, (size_t)S * D));
   TRY(dalloc(ctx, &ctx->qkvb, (size_t)S * (H + 2 * KV) * hd));
   TRY(dalloc(ctx, &ctx->att, (size_t)S * H * hd));
+  TRY(dalloc(ctx, &ctx->qrot, (size_t)S * H * hd));
   TRY(dalloc(ctx, &ctx->hbuf, (size_t)S * F));
   TRY(dalloc(ctx, &ctx->logits, (size_t)S * V));
   TRY(dalloc(ctx, &ctx->argmax, (size_t)S));
@@ -509,6 +513,7 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
     float* x = ctx->x + (size_t)b * D;
     sb.pos = pos + b;
     sb.qkv = ctx->qkvb + (size_t)b * (H + 2 * KV) * hd;
+    sb.qrot = ctx->qrot + (size_t)b * H * hd;
     sb.att = ctx->att + (size_t)b * H * hd;
     sb.sel = ctx->sel + (size_t)b * ctx->max_sel;
     sb.nsel = ctx->nsel + b;
@@ -720,7 +725,8 @@ extern "C" int ec_read_state(ec_ctx* ctx, int which, int seq, float* out, size_t
   size_t cnt = 0;
   switch (which) {
     case 0: src = ctx->x + (size_t)seq * c.dim; cnt = c.dim; break;
-    case 2: src = ctx->qkvb + (size_t)seq * qkvw; cnt = (size_t)c.n_heads * c.head_dim; break;
+    case 2: src = ctx->qrot + (size_t)seq * c.n_heads * c.head_dim;
+            cnt = (size_t)c.n_heads * c.head_dim; break;
     case 3: src = ctx->qkvb + (size_t)seq * qkvw + c.n_heads * c.head_dim;
             cnt = (size_t)c.n_kv_heads * c.head_dim; break;
     case 4: src = ctx->qkvb + (size_t)seq * qkvw + (c.n_heads + c.n_kv_heads) * c.head_dim;
