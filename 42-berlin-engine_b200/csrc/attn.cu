@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
     paged_select_cta(kv, sb, layer, b);
     return;
   }
-  const int pos = sb.pos[b];
+  const int pos = step_pos(sb, b);
   const float* q = sb.qkv + (long)b * (H + 2 * KV) * hd;
   float* qo = sb.qrot + (long)b * H * hd;
   float* k = sb.qkv + (long)b * (H + 2 * KV) * hd + H * hd;
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
   __shared__ unsigned s_seen[4096 / 32];
   pdl_launch_dependents();
   pdl_wait();
-  const int pos = sb.pos[b];
+  const int pos = step_pos(sb, b);
   const int kv_len = min(pos + 1, kv.seq_len);
   const float* q = sb.qrot + (long)b * H * hd;
   if (!(sb.sparse_k > 0 && kv_len > sb.sparse_k)) {
@@ -471,11 +471,17 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim, half = hd >> 1;
   if (!kv.paged) return;
-  const int pos = sb.pos[b];
+  const int pos = step_pos(sb, b);
   const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
   const int nb = (n_tok + kBlk - 1) / kBlk;
   if (nb <= sb.sparse_blocks_k || nb > 2048 || hd > 128) {
-    if (tid == 0) sb.nsel[b] = -1;
+    // every block in order (listed explicitly when asked to, same result)
+    const bool list = sb.list_dense && nb <= sb.max_sel;
+    if (list) {
+      int* out = sb.sel + (long)b * sb.max_sel;
+      for (int i = tid; i < nb; i += blockDim.x) out[i] = i;
+    }
+    if (tid == 0) sb.nsel[b] = list ? nb : -1;
     return;
   }
   PHASE_MARK(tid == 0 && layer == 1, 0);
@@ -485,10 +491,10 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
     fence_mbar_init();
   }
   // query head 0, rotated here (the append CTA rotates its own copy)
-  const float* q = sb.qkv + (long)b * (H + 2 * KV) * hd;
+  const float* q = sb.q_rotated ? sb.qrot + (long)b * H * hd : sb.qkv + (long)b * (H + 2 * KV) * hd;
   for (int j = tid; j < half; j += blockDim.x) {
     const float v0 = q[j], v1 = q[j + half];
-    if (pos < kv.seq_len) {
+    if (pos < kv.seq_len && !sb.q_rotated) {
       const float c = sb.rope_cos[(long)pos * half + j], s = sb.rope_sin[(long)pos * half + j];
       s_q[j] = __fmaf_rn(v0, c, -__fmul_rn(v1, s));
       s_q[j + half] = __fmaf_rn(v0, s, __fmul_rn(v1, c));
@@ -575,6 +581,7 @@ __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a -
 
 __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int esize) {
   AttnSmemLayout L;
+  const int nblk = max_tok / 16 + 4;  // selected blocks (partial last block included)
   size_t o = 256 * 4;  // q head
   L.kv = o;
   o = align_up(o + (size_t)max_tok * hd * esize, 16);
@@ -589,16 +596,16 @@ __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int e
   L.lpos = o;
   o += (size_t)max_tok * 4;
   L.boff = o;
-  o += kMaxSel * 4;
+  o += nblk * 4;
   L.bphys = o;
-  o += kMaxSel * 4;
+  o += nblk * 4;
   L.bfill = o;
-  o += kMaxSel * 4;
+  o += nblk * 4;
   o = align_up(o, 16);
   L.ksb = o;
-  o += kMaxSel * 16 * 4;
+  o += nblk * 16 * 4;
   L.vsb = o;
-  o += kMaxSel * 16 * 4;
+  o += nblk * 16 * 4;
   L.total = o;
   return L;
 }
@@ -644,7 +651,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   const bool mk = (h == 0 && b == 0 && layer == 1);
   (void)mk;
   PHASE_MARK(mk && tid == 0, 8);
-  const int pos = sb.pos[b];
+  const int pos = step_pos(sb, b);
   const float* qg = sb.qrot + (long)b * H * hd;
   for (int d = tid; d < hd; d += blockDim.x) qs[d] = qg[h * hd + d];
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
@@ -933,27 +940,93 @@ static cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaS
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// paged_kv_append of one token into a one-layer view (k, v already rotated).
+__global__ void __launch_bounds__(256) paged_append_view_kernel(KvLayout kv, const float* k,
+                                                                const float* v, int pos) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int KV = kv.n_kv_heads, hd = kv.head_dim;
+  const int lb = pos / kBlk, off = pos - lb * kBlk;
+  if (lb >= kv.max_blocks) return;
+  const long blk = kv.page_table[lb];
+  for (int h = warp; h < 2 * KV; h += nwarps) {
+    const bool isv = h >= KV;
+    const int kh = isv ? h - KV : h;
+    int8_t* dst = (isv ? kv.vq : kv.kq) + ((blk * KV + kh) * kBlk + off) * hd;
+    const float sc = warp_quant_int8((isv ? v : k) + kh * hd, dst, hd, lane, isv ? -1 : off);
+    if (lane == 0) (isv ? kv.vs : kv.ks)[(blk * KV + kh) * kBlk + off] = sc;
+  }
+  __syncthreads();
+  if (off == kBlk - 1) {
+    for (int d = tid; d < hd; d += blockDim.x) {
+      float c = 0.0f;
+      for (int t = 0; t < kBlk; t++)
+        c = __fadd_rn(c, __fmul_rn((float)kv.kq[((blk * KV) * kBlk + t) * hd + kswz(t, d, hd)],
+                                   kv.ks[(blk * KV) * kBlk + t]));
+      kv.centroid[blk * hd + d] = __fmul_rn(c, __fdiv_rn(1.0f, (float)kBlk));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) paged_select_kernel(KvLayout kv, StepBuffers sb) {
+  paged_select_cta(kv, sb, 0, blockIdx.y);
+}
+
 #ifdef EC_PHASE_TIMING
 extern "C" int ec_debug_phase_times(long long* out) {
   return cudaMemcpyFromSymbol(out, g_phase_ts, sizeof(g_phase_ts)) == cudaSuccess ? 0 : -2;
 }
 #endif
 
+// Opt a kernel into the largest dynamic shared memory it can take: the
+// per-block limit less its own static shared memory.
+template <typename K>
+cudaError_t opt_in_max_smem(K kernel) {
+  cudaFuncAttributes a;
+  cudaError_t e = cudaFuncGetAttributes(&a, kernel);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              227 * 1024 - (int)a.sharedSizeBytes);
+}
+
 cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb) {
   const int max_tok = attn_max_tok(kv, sb);
   const int smem = (int)attn_smem(kv, sb, max_tok);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(attention_kernel<true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (!e)
-    e = cudaFuncSetAttribute(attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem);
+  // the largest opt-in: per-op calls share these kernels with other sizes
+  cudaError_t e = opt_in_max_smem(attention_kernel<true>);
+  if (!e) e = opt_in_max_smem(attention_kernel<false>);
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;
   const int ssel = cap_c * 8 + (sb.sparse_k + 2) * 8 + 256 * 4;
   if (!e && ssel <= 227 * 1024)
     e = cudaFuncSetAttribute(linear_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ssel);
   return e;
+}
+
+cudaError_t launch_paged_append_view(const KvLayout& kv, const float* k, const float* v, int pos,
+                                     int* err, cudaStream_t s) {
+  (void)err;
+  paged_append_view_kernel<<<1, 256, 0, s>>>(kv, k, v, pos);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_select(const KvLayout& kv, const StepBuffers& sb, cudaStream_t s) {
+  paged_select_kernel<<<dim3(1, 1), 256, 0, s>>>(kv, sb);
+  return cudaGetLastError();
+}
+
+size_t attention_smem_bytes(int max_tok, int hd, bool paged) {
+  return attn_layout(max_tok, hd, paged ? 1 : 2).total;
+}
+
+cudaError_t launch_attention_n(const KvLayout& kv, const StepBuffers& sb, int max_tok,
+                               cudaStream_t s) {
+  const size_t smem = attention_smem_bytes(max_tok, kv.head_dim, kv.paged != 0);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  cudaError_t e = opt_in_max_smem(attention_kernel<true>);
+  if (e != cudaSuccess) return e;
+  return launch_ex(attention_kernel<true>, dim3(kv.n_heads, 1), dim3(kAttnThreads), smem, s, false,
+                   kv, sb, 0, max_tok);
 }
 
 cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,

@@ -48,7 +48,14 @@ struct StepBuffers {
   const float* rope_sin;
   int sparse_k, window, sparse_blocks_k;
   int* err;
+  int pos_fixed;        // position when pos == nullptr (per-op entry points)
+  int q_rotated;        // selection reads qrot (already rotated) instead of qkv
+  int list_dense;       // selection also lists every block when attending all
 };
+
+inline __host__ __device__ int step_pos(const StepBuffers& sb, int b) {
+  return sb.pos ? sb.pos[b] : sb.pos_fixed;
+}
 
 // Shared-memory attributes for the current device (outside stream capture).
 cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb);
@@ -61,5 +68,14 @@ cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const
                                  int layer, int B, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
                              cudaStream_t s, bool pdl);
+
+// Per-op entry points on one layer (a KvLayout with n_layers = 1):
+// append one token, select blocks (sb.q_rotated), attention with max_tok.
+cudaError_t launch_paged_append_view(const KvLayout& kv, const float* k, const float* v, int pos,
+                                     int* err, cudaStream_t s);
+cudaError_t launch_paged_select(const KvLayout& kv, const StepBuffers& sb, cudaStream_t s);
+cudaError_t launch_attention_n(const KvLayout& kv, const StepBuffers& sb, int max_tok,
+                               cudaStream_t s);
+size_t attention_smem_bytes(int max_tok, int hd, bool paged);
 
 }  // namespace ec

@@ -854,16 +854,107 @@ extern "C" int ec_op_argmax(const float* logits, int n, int B, int* out, void* s
   return EC_OK;
 }
 
+namespace {
+
+// KvLayout of a caller's one-layer view.
+bool view_layout(const ec_paged_view* pv, ec::KvLayout* kv) {
+  if (!pv || !pv->k || !pv->v || !pv->k_scale || !pv->v_scale || !pv->centroid ||
+      !pv->page_table || pv->n_kv_heads <= 0 || pv->max_blocks <= 0 ||
+      (pv->head_dim != 32 && pv->head_dim != 64 && pv->head_dim != 128))
+    return false;
+  *kv = ec::KvLayout{};
+  kv->n_layers = 1;
+  kv->n_kv_heads = pv->n_kv_heads;
+  kv->head_dim = pv->head_dim;
+  kv->max_blocks = pv->max_blocks;
+  kv->seq_len = pv->max_blocks * 16;
+  kv->paged = 1;
+  kv->kq = pv->k;
+  kv->vq = pv->v;
+  kv->ks = pv->k_scale;
+  kv->vs = pv->v_scale;
+  kv->centroid = pv->centroid;
+  kv->page_table = const_cast<int*>(pv->page_table);
+  return true;
+}
+
+}  // namespace
+
 extern "C" int ec_op_paged_append(const ec_paged_view* pv, const float* k, const float* v, int pos,
                                   void* stream) {
-  (void)pv; (void)k; (void)v; (void)pos; (void)stream;
-  return fail(EC_ERR_UNSUPPORTED, "not built yet");
+  ec::KvLayout kv;
+  if (!view_layout(pv, &kv) || !k || !v) return fail(EC_ERR_ARG, "bad paged view or vectors");
+  if (pos < 0 || pos >= pv->max_blocks * 16) return fail(EC_ERR_ARG, "position beyond the view");
+  EC_CUDA_TRY(ec::launch_paged_append_view(kv, k, v, pos, nullptr, static_cast<cudaStream_t>(stream)));
+  return EC_OK;
 }
+
+namespace {
+
+// Shared body of the per-op paged attention: `scratch` holds
+// [sel: max_sel ints][nsel][err], max_sel = paged_attention_max_sel(...).
+int paged_attention_run(const ec_paged_view* pv, const float* q, float* out, int n_heads,
+                        int n_tokens, int sparse_blocks_k, int* selected_out,
+                        int* n_selected_out, int* scratch, int max_sel, cudaStream_t s) {
+  ec::KvLayout kv;
+  view_layout(pv, &kv);
+  kv.n_heads = n_heads;
+  ec::StepBuffers sb{};
+  sb.pos = nullptr;
+  sb.pos_fixed = n_tokens - 1;
+  sb.qrot = const_cast<float*>(q);
+  sb.att = out;
+  sb.sel = scratch;
+  sb.nsel = scratch + max_sel;
+  sb.err = scratch + max_sel + 1;
+  sb.max_sel = max_sel;
+  sb.sparse_blocks_k = sparse_blocks_k > 0 ? sparse_blocks_k : 1 << 30;
+  sb.q_rotated = 1;
+  sb.list_dense = 1;
+  const int nb = (n_tokens + 15) / 16;
+  const int max_tok = (sparse_blocks_k > 0 && nb > sparse_blocks_k) ? 16 * sparse_blocks_k
+                                                                   : ((n_tokens + 15) & ~15);
+  EC_CUDA_TRY(cudaMemsetAsync(sb.err, 0, sizeof(int), s));
+  EC_CUDA_TRY(ec::launch_paged_select(kv, sb, s));
+  EC_CUDA_TRY(ec::launch_attention_n(kv, sb, max_tok, s));
+  if (selected_out)
+    EC_CUDA_TRY(cudaMemcpyAsync(selected_out, sb.sel, (size_t)(sparse_blocks_k > 0 && nb > sparse_blocks_k ? sparse_blocks_k : nb) * 4,
+                                cudaMemcpyDeviceToDevice, s));
+  if (n_selected_out)
+    EC_CUDA_TRY(cudaMemcpyAsync(n_selected_out, sb.nsel, 4, cudaMemcpyDeviceToDevice, s));
+  return EC_OK;
+}
+
+int paged_attention_check(const ec_paged_view* pv, const float* q, float* out, int n_heads,
+                          int n_tokens, int sparse_blocks_k) {
+  ec::KvLayout kv;
+  if (!view_layout(pv, &kv) || !q || !out) return fail(EC_ERR_ARG, "bad paged view or vectors");
+  if (n_heads <= 0 || n_heads % pv->n_kv_heads) return fail(EC_ERR_ARG, "n_heads");
+  if (n_tokens <= 0 || n_tokens > pv->max_blocks * 16) return fail(EC_ERR_ARG, "n_tokens");
+  if (sparse_blocks_k < 0 || sparse_blocks_k > 64)
+    return fail(EC_ERR_UNSUPPORTED, "sparse_blocks_k must be 0..64");
+  const int nb = (n_tokens + 15) / 16;
+  if (nb > 2048) return fail(EC_ERR_UNSUPPORTED, "at most 2048 blocks");
+  const bool dense = !(sparse_blocks_k > 0 && nb > sparse_blocks_k);
+  if (dense && (long)((n_tokens + 15) & ~15) * pv->head_dim > 131072)
+    return fail(EC_ERR_UNSUPPORTED, "dense attention over more than 131072 K bytes");
+  return EC_OK;
+}
+
+}  // namespace
 
 extern "C" int ec_op_paged_attention(const ec_paged_view* pv, const float* q, float* out,
                                      int n_heads, int n_tokens, int sparse_blocks_k,
                                      int* selected_out, int* n_selected_out, void* stream) {
-  (void)pv; (void)q; (void)out; (void)n_heads; (void)n_tokens; (void)sparse_blocks_k;
-  (void)selected_out; (void)n_selected_out; (void)stream;
-  return fail(EC_ERR_UNSUPPORTED, "not built yet");
+  int rc = paged_attention_check(pv, q, out, n_heads, n_tokens, sparse_blocks_k);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nb = (n_tokens + 15) / 16;
+  const int max_sel = nb > 66 ? nb : 66;
+  int* scratch = nullptr;
+  EC_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&scratch), (size_t)(max_sel + 2) * 4, s));
+  rc = paged_attention_run(pv, q, out, n_heads, n_tokens, sparse_blocks_k, selected_out,
+                           n_selected_out, scratch, max_sel, s);
+  cudaFreeAsync(scratch, s);
+  return rc;
 }

@@ -53,7 +53,7 @@ class Transformer(C.Structure):
 class PagedView(C.Structure):
     _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("k_scale", C.c_void_p),
                 ("v_scale", C.c_void_p), ("centroid", C.c_void_p), ("page_table", C.c_void_p),
-                ("n_kv_heads", C.c_int), ("head_dim", C.c_int)]
+                ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("max_blocks", C.c_int)]
 
 
 _lib = None

@@ -185,7 +185,10 @@ int		ec_op_quant_int8(int8_t *out, float *scales, const float *in, int rows,
 int		ec_op_argmax(const float *logits, int n, int B, int *out, void *stream);
 
 /* One layer's paged INT8 KV cache in device memory
-** (t_kv_block / t_block_manager, src/memory/paged.h:53-88). */
+** (t_kv_block / t_block_manager, src/memory/paged.h:53-88).  Blocks hold 16
+** tokens; within a block K rows are stored rotated by 16-byte pieces (piece p
+** of token t at piece (p + t) mod (head_dim / 16)), so fill the view only
+** with ec_op_paged_append.  head_dim is 32, 64 or 128. */
 typedef struct ec_paged_view
 {
 	int8_t		*k;			/* [blocks][n_kv_heads][16][head_dim] */
@@ -193,23 +196,31 @@ typedef struct ec_paged_view
 	float		*k_scale;	/* [blocks][n_kv_heads][16] */
 	float		*v_scale;
 	float		*centroid;	/* [blocks][head_dim], KV head 0 mean */
-	const int	*page_table;/* [max_logical] logical -> physical block */
+	const int	*page_table;/* [max_blocks] logical -> physical block */
 	int			n_kv_heads;
 	int			head_dim;
+	int			max_blocks;	/* logical blocks the page table maps */
 }	ec_paged_view;
 
 /* paged_kv_append (src/memory/paged.h:143) of one token at `pos`: quantise
-** k, v (F32 [n_kv_heads*head_dim], device) and store; computes the block
-** centroid when the block fills (calc_block_centroid_int8, paged.c:350). */
+** k, v (F32 [n_kv_heads*head_dim], device, already rotated) and store;
+** computes the block centroid when the block fills
+** (calc_block_centroid_int8, paged.c:350). */
 int		ec_op_paged_append(const ec_paged_view *pv, const float *k,
 			const float *v, int pos, void *stream);
 
-/* op_paged_attention (ops_attention.h:75) over logical blocks
-** [0, n_tokens/16] with n_tokens cached tokens, or, when n_blocks >
-** sparse_blocks_k, score_blocks + select_top_k_blocks +
-** op_paged_attention_sparse (paged.h:200-212, ops_attention.h:82) as
-** inference.c:447-489 drives them.  selected_out (optional, device,
-** sparse_blocks_k ints) receives the logical blocks attended. */
+/* Decode attention of one token over the first n_tokens cached tokens, q =
+** rotated queries [n_heads * head_dim] (device), out likewise.
+** sparse_blocks_k == 0: op_paged_attention (ops_attention.h:75), every block
+** in order (n_tokens * head_dim <= 131072).  sparse_blocks_k in 1..64: as
+** inference.c:436-496 drives it -- dense while the blocks number at most
+** sparse_blocks_k, else score_blocks + select_top_k_blocks (paged.h:200-212,
+** query head 0) and op_paged_attention_sparse (ops_attention.h:82) over
+** first, last and the heap-ordered rest.  selected_out (device, optional,
+** sparse_blocks_k ints; with sparse_blocks_k == 0, n_tokens/16 + 1) receives
+** the logical blocks in the order attended, n_selected_out (device,
+** optional) their number.  Uses a small scratch buffer that it allocates
+** and frees on `stream` (stream-ordered allocator). */
 int		ec_op_paged_attention(const ec_paged_view *pv, const float *q,
 			float *out, int n_heads, int n_tokens, int sparse_blocks_k,
 			int *selected_out, int *n_selected_out, void *stream);

@@ -215,3 +215,79 @@ def test_host_transformer_api(eng, torch, tiny_model):
         lg = t.forward(toks[pos], pos)
         assert digest(lg) == dg[pos]
     t.close()
+
+
+def paged_view(eng, torch, kv_heads, hd, max_blocks, seed=5):
+    """A paged cache in torch-allocated device memory whose page table is a
+    seeded permutation (logical block b lives in physical block perm[b])."""
+    perm = np.random.default_rng(seed).permutation(max_blocks).astype(np.int32)
+    bufs = dict(
+        k=torch.zeros(max_blocks * kv_heads * 16 * hd, dtype=torch.int8, device="cuda"),
+        v=torch.zeros(max_blocks * kv_heads * 16 * hd, dtype=torch.int8, device="cuda"),
+        ks=torch.zeros(max_blocks * kv_heads * 16, dtype=torch.float32, device="cuda"),
+        vs=torch.zeros(max_blocks * kv_heads * 16, dtype=torch.float32, device="cuda"),
+        c=torch.zeros(max_blocks * hd, dtype=torch.float32, device="cuda"),
+        pt=dev(torch, perm))
+    pv = eng.PagedView(bufs["k"].data_ptr(), bufs["v"].data_ptr(), bufs["ks"].data_ptr(),
+                       bufs["vs"].data_ptr(), bufs["c"].data_ptr(), bufs["pt"].data_ptr(),
+                       kv_heads, hd, max_blocks)
+    return pv, bufs
+
+
+def golden_paged_view(eng, torch):
+    """The golden paged cache (KV=2, hd=64, 1100 tokens of seed 31) filled
+    through ec_op_paged_append."""
+    import ctypes as C
+    from make_golden import paged_inputs
+    KV, hd, T = 2, 64, 1100
+    pv, bufs = paged_view(eng, torch, KV, hd, 128)
+    kk, vv = paged_inputs(T, KV * hd)
+    dk, dv = dev(torch, kk), dev(torch, vv)
+    L = eng.lib()
+    for p in range(T):
+        eng.check(L.ec_op_paged_append(C.byref(pv), dk[p].data_ptr(), dv[p].data_ptr(), p, None))
+    bufs["kk"], bufs["vv"] = dk, dv
+    return pv, bufs
+
+
+def test_paged_ops_match_reference(eng, torch):
+    """ec_op_paged_append + ec_op_paged_attention on a permuted page table:
+    dense (op_paged_attention) and block-sparse (score, heap top-K, sparse
+    attention) outputs and the selected logical blocks, bit-identical to the
+    reference engine's (tests/golden)."""
+    import ctypes as C
+    H, hd, T = 8, 64, 1100
+    pv, bufs = golden_paged_view(eng, torch)
+    L = eng.lib()
+    q = dev(torch, G["paged_q"])
+    out = torch.zeros(H * hd, dtype=torch.float32, device="cuda")
+    sel = torch.full((80,), -7, dtype=torch.int32, device="cuda")
+    ns = torch.zeros(1, dtype=torch.int32, device="cuda")
+    eng.check(L.ec_op_paged_attention(C.byref(pv), q.data_ptr(), out.data_ptr(), H, T, 0,
+                                      sel.data_ptr(), ns.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(out.cpu().numpy()), bits(G["paged_dense"]))
+    nb = (T + 15) // 16
+    assert int(ns.item()) == nb
+    assert np.array_equal(sel.cpu().numpy()[:nb], np.arange(nb))
+    out.zero_()
+    eng.check(L.ec_op_paged_attention(C.byref(pv), q.data_ptr(), out.data_ptr(), H, T, 64,
+                                      sel.data_ptr(), ns.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(out.cpu().numpy()), bits(G["paged_sparse"]))
+    want = G["paged_sel"]
+    assert int(ns.item()) == want.size
+    assert np.array_equal(sel.cpu().numpy()[:want.size], want)
+
+
+def test_paged_ops_argument_errors(eng, torch):
+    import ctypes as C
+    L = eng.lib()
+    pv, bufs = paged_view(eng, torch, 2, 64, 8)
+    x = torch.zeros(512, dtype=torch.float32, device="cuda")
+    assert L.ec_op_paged_append(C.byref(pv), x.data_ptr(), x.data_ptr(), 8 * 16, None) == \
+        eng.EC_ERR_ARG
+    assert L.ec_op_paged_attention(C.byref(pv), x.data_ptr(), x.data_ptr(), 3, 16, 0,
+                                   None, None, None) == eng.EC_ERR_ARG
+    assert L.ec_op_paged_attention(C.byref(pv), x.data_ptr(), x.data_ptr(), 8, 16, 65,
+                                   None, None, None) == eng.EC_ERR_UNSUPPORTED
