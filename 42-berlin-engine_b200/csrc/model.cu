@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "attn.cuh"
@@ -957,4 +958,67 @@ extern "C" int ec_op_paged_attention(const ec_paged_view* pv, const float* q, fl
                            n_selected_out, scratch, max_sel, s);
   cudaFreeAsync(scratch, s);
   return rc;
+}
+
+// ---------------------------------------------------------------------------
+// ec_op_paged_attention_static: the same operation for callers that cannot
+// allocate device memory -- code running inside another runtime's memory
+// pool or allocator hooks, code that is forbidden to call cudaMalloc after
+// start-up, or hosts whose own allocator owns the whole device.  Its scratch
+// (the selected-block list, its count and an error word) is a fixed array in
+// this library's device memory instead of a stream-ordered allocation.
+
+namespace {
+
+// Largest context the fixed scratch serves: 2048 blocks of 16 tokens.
+constexpr int kStaticMaxBlocks = 2048;
+constexpr int kStaticMaxSel = kStaticMaxBlocks;  // >= 66 for the sparse path
+
+// [sel: kStaticMaxSel][nsel][err].  Every device that loads the library holds
+// one copy (about 8 KB) until the process exits.  Host code may not use this
+// name as a device address; it takes the address from cudaGetSymbolAddress.
+static __device__ __align__(256) int g_paged_scratch[kStaticMaxSel + 2];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+int* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_paged_scratch on the current device, looked up once per
+// device (the first call on each device does it).
+int static_scratch(int** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(EC_ERR_UNSUPPORTED, "device ordinal too large");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_paged_scratch);
+    if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+    g_scratch_addr[dev] = static_cast<int*>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return EC_OK;
+}
+
+}  // namespace
+
+extern "C" int ec_op_paged_attention_static(const ec_paged_view* pv, const float* q, float* out,
+                                            int n_heads, int n_tokens, int sparse_blocks_k,
+                                            int* selected_out, int* n_selected_out,
+                                            void* stream) {
+  if (n_tokens > kStaticMaxBlocks * 16)
+    return fail(EC_ERR_UNSUPPORTED,
+                "n_tokens beyond the fixed scratch of ec_op_paged_attention_static "
+                "(at most 32768 tokens = 2048 blocks)");
+  int rc = paged_attention_check(pv, q, out, n_heads, n_tokens, sparse_blocks_k);
+  if (rc) return rc;
+  int* scratch = nullptr;
+  rc = static_scratch(&scratch);
+  if (rc) return rc;
+  // paged_attention_run zeroes the error word; the list and count are always
+  // written by the selection before the attention reads them.
+  return paged_attention_run(pv, q, out, n_heads, n_tokens, sparse_blocks_k, selected_out,
+                             n_selected_out, scratch, kStaticMaxSel,
+                             static_cast<cudaStream_t>(stream));
 }

@@ -27,7 +27,7 @@ EXPORTS = [
     "ec_argmax_device", "ec_stream", "ec_synchronize", "ec_read_state", "ec_read_lsh",
     "ec_read_counters", "ec_launches_per_step", "ec_op_gemv", "ec_op_rmsnorm", "ec_op_rope",
     "ec_op_silu_mul", "ec_op_quant_int8", "ec_op_argmax", "ec_op_paged_append",
-    "ec_op_paged_attention", "ec_transformer_init", "ec_transformer_set_tensor",
+    "ec_op_paged_attention", "ec_op_paged_attention_static", "ec_transformer_init", "ec_transformer_set_tensor",
     "ec_transformer_forward", "ec_transformer_argmax", "ec_transformer_reset",
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read",
 ]
@@ -91,6 +91,8 @@ def lib():
             "ec_op_argmax": (i, [vp, i, i, vp, vp]),
             "ec_op_paged_append": (i, [C.POINTER(PagedView), vp, vp, i, vp]),
             "ec_op_paged_attention": (i, [C.POINTER(PagedView), vp, vp, i, i, i, vp, vp, vp]),
+            "ec_op_paged_attention_static": (i, [C.POINTER(PagedView), vp, vp, i, i, i, vp, vp,
+                                                 vp]),
             "ec_transformer_init": (i, [C.POINTER(Transformer), C.POINTER(ModelConfig), i]),
             "ec_transformer_set_tensor": (i, [C.POINTER(Transformer), C.c_char_p, vp, vp]),
             "ec_transformer_forward": (C.POINTER(C.c_float), [C.POINTER(Transformer), i, i]),

@@ -225,6 +225,22 @@ int		ec_op_paged_attention(const ec_paged_view *pv, const float *q,
 			float *out, int n_heads, int n_tokens, int sparse_blocks_k,
 			int *selected_out, int *n_selected_out, void *stream);
 
+/* ec_op_paged_attention without any allocation, for callers that cannot
+** allocate device memory (code running under another runtime's allocator or
+** memory pool, or required not to call cudaMalloc once started).  It has no
+** counterpart in the reference, whose CPU engine allocates nothing on a GPU.
+** Same arguments, checks and results as ec_op_paged_attention, with
+** n_tokens <= 32768 (2048 blocks); larger contexts are rejected with
+** EC_ERR_UNSUPPORTED.  Its scratch is a fixed 8 KB array in the library's
+** device memory, one per device, held until the process exits.  The first
+** call on a device looks up that array's address (with that device
+** current), so make it before any stream capture.  All calls on a device
+** share the array: calls that may overlap on the GPU (other streams, other
+** threads) race and must be serialised by the caller. */
+int		ec_op_paged_attention_static(const ec_paged_view *pv, const float *q,
+			float *out, int n_heads, int n_tokens, int sparse_blocks_k,
+			int *selected_out, int *n_selected_out, void *stream);
+
 # ifdef __cplusplus
 }
 # endif
