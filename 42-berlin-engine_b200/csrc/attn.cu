@@ -571,7 +571,6 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
 //      recurrence for one dimension each, the next warp the denominator.
 // ------------------------------------------------------------------------
 constexpr int kAttnThreads = 512;
-constexpr int kMaxSel = 68;  // SPARSE_BLOCKS_K + 2, rounded
 
 struct AttnSmemLayout {
   size_t kv, sc, sf, tks, tvs, lpos, boff, bphys, bfill, ksb, vsb, total;

@@ -58,30 +58,6 @@ __device__ __forceinline__ void decode4(const uint8_t* p, float* f) {
   }
 }
 
-// RMSNorm of xs[0..K) in place (consumer threads only; `nc` of them).
-__device__ __forceinline__ void rmsnorm_smem(float* xs, const uint16_t* __restrict__ w, int K,
-                                             float eps, float* red, int ct, int nc) {
-  if (ct < 8) {
-    float acc = 0.0f;
-    int j = ct;
-    const int k8 = K & ~7;
-#pragma unroll 8
-    for (; j < k8; j += 8) acc = __fmaf_rn(xs[j], xs[j], acc);
-    red[ct] = acc;
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(nc));
-  if (ct == 0) {
-    float ss = hsum8(red);
-    for (int j = K & ~7; j < K; j++) ss = __fmaf_rn(xs[j], xs[j], ss);
-    ss = __fdiv_rn(ss, (float)K);
-    red[8] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(nc));
-  const float inv = red[8];
-  for (int j = ct; j < K; j += nc) xs[j] = __fmul_rn(__fmul_rn(xs[j], inv), bf16_to_f32(w[j]));
-  asm volatile("bar.sync 1, %0;" ::"r"(nc));
-}
-
 template <int WK, int PRO, int EPI>
 __global__ void __launch_bounds__(32 + 8 * kMaxRg, 1) gemv_kernel(GemvParams p) {
   constexpr int ES = WTraits<WK>::esize;

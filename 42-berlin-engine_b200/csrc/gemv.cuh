@@ -22,6 +22,7 @@ struct GemvParams {
   int kcb;                 // bytes of one row streamed per pipeline stage
   int silu_vec_limit;      // SWIGLU: outputs below this index use the vector form
   int* err;
+  int stages;              // packed kernel: pipeline stages (set from the plan)
 };
 
 // Host-side launch description for one GEMV shape.
@@ -42,5 +43,30 @@ cudaError_t gemv_prepare();
 // Launch (PDL attribute set when `pdl` is true).
 cudaError_t gemv_launch(int wkind, int pro, int epi, const GemvPlan& plan, const GemvParams& p,
                         cudaStream_t stream, bool pdl);
+
+// ---------------------------------------------------------------------------
+// Packed-layout GEMV (gemv_packed.cu): the decode step's weight matrices are
+// repacked once at upload into [chunk][row quad][32-column piece][4 rows][32 B]
+// so that one bulk copy fills each pipeline stage.
+struct PackedPlan {
+  int grid;
+  int warps;            // consumer warps (block = 32 * (warps + 1))
+  int rows_per_thread;  // 1 or 2
+  int kce;              // columns per chunk: 512 or 32
+  int stages;
+  int smem;
+};
+
+int packed_kce(int K);
+size_t packed_bytes(int N, int K);
+// force_r: 0 = choose, 1 or 2 = rows per thread.
+bool packed_plan(int wkind, int N, int K, int n_sm, int force_r, PackedPlan* plan);
+cudaError_t packed_prepare();
+cudaError_t packed_launch(int wkind, int pro, int epi, const PackedPlan& plan,
+                          const GemvParams& p, cudaStream_t stream, bool pdl);
+// Pack nr row-major rows of K bytes (device) into packed rows
+// row_base + row_stride * i of an N-row packed matrix (device).
+cudaError_t packed_pack(const uint8_t* src, uint8_t* dst, int N, int K, int nr, int row_base,
+                        int row_stride, cudaStream_t stream);
 
 }  // namespace ec

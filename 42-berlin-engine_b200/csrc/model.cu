@@ -25,7 +25,7 @@ extern "C" const char* ec_last_error(void) { return g_err; }
 namespace {
 
 struct Mat {
-  uint8_t* w = nullptr;
+  uint8_t* w = nullptr;  // packed layout (gemv_packed.cu), rows padded to a multiple of 4
   float* scale = nullptr;  // per row (INT8 and FP8 alike, FP8 expanded)
   int rows = 0, cols = 0;
 };
@@ -55,7 +55,7 @@ struct ec_ctx {
   int* err = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
   int max_sel = 0;
-  ec::GemvPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_lm{};
+  ec::PackedPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_lm{};
   // graph cache
   cudaGraphExec_t gexec = nullptr;
   int g_B = -1, g_fb = -1;
@@ -92,6 +92,12 @@ float rand_gaussian(unsigned* seed) {
   float u2 = (float)((*seed >> 16) & 0x7FFF) / 32767.0f;
   if (u1 < 1e-6f) u1 = 1e-6f;
   return sqrtf(-2.0f * logf(u1)) * cosf(2.0f * 3.14159265f * u2);
+}
+
+// EC_GEMV_ROWS_PER_THREAD=1|2 overrides the GEMV plans' choice (tuning).
+int gemv_force_r() {
+  const char* v = getenv("EC_GEMV_ROWS_PER_THREAD");
+  return v ? atoi(v) : 0;
 }
 
 int fail(int code, const char* msg) {
@@ -241,7 +247,8 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     for (int i = 0; i < 4; i++) {
       ms[i]->rows = rows[i];
       ms[i]->cols = cols[i];
-      TRY(dalloc(ctx, &ms[i]->w, (size_t)rows[i] * cols[i]));
+      TRY(dalloc(ctx, &ms[i]->w, ec::packed_bytes(rows[i], cols[i])));
+      TRY(cudaMemset(ms[i]->w, 0, ec::packed_bytes(rows[i], cols[i])));
       TRY(dalloc(ctx, &ms[i]->scale, (size_t)rows[i]));
     }
     TRY(dalloc(ctx, &ctx->attn_norm[l], (size_t)D));
@@ -249,7 +256,8 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   }
   ctx->lm.rows = V;
   ctx->lm.cols = D;
-  TRY(dalloc(ctx, &ctx->lm.w, (size_t)V * D));
+  TRY(dalloc(ctx, &ctx->lm.w, ec::packed_bytes(V, D)));
+  TRY(cudaMemset(ctx->lm.w, 0, ec::packed_bytes(V, D)));
   TRY(dalloc(ctx, &ctx->lm.scale, (size_t)V));
   TRY(dalloc(ctx, &ctx->emb, (size_t)V * D));
   TRY(dalloc(ctx, &ctx->final_norm, (size_t)D));
@@ -347,11 +355,12 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   }
   // GEMV plans
   const int wk = c.weight_kind;
-  if (!ec::gemv_plan(wk, (H + 2 * KV) * hd, D, ec::EPI_STORE, ctx->n_sm, &ctx->p_qkv) ||
-      !ec::gemv_plan(wk, D, H * hd, ec::EPI_RESID, ctx->n_sm, &ctx->p_o) ||
-      !ec::gemv_plan(wk, 2 * F, D, ec::EPI_SWIGLU, ctx->n_sm, &ctx->p_w13) ||
-      !ec::gemv_plan(wk, D, F, ec::EPI_RESID, ctx->n_sm, &ctx->p_w2) ||
-      !ec::gemv_plan(wk, V, D, ec::EPI_STORE, ctx->n_sm, &ctx->p_lm)) {
+  const int fr = gemv_force_r();
+  if (!ec::packed_plan(wk, (H + 2 * KV) * hd, D, ctx->n_sm, fr, &ctx->p_qkv) ||
+      !ec::packed_plan(wk, D, H * hd, ctx->n_sm, fr, &ctx->p_o) ||
+      !ec::packed_plan(wk, 2 * F, D, ctx->n_sm, fr, &ctx->p_w13) ||
+      !ec::packed_plan(wk, D, F, ctx->n_sm, fr, &ctx->p_w2) ||
+      !ec::packed_plan(wk, V, D, ctx->n_sm, fr, &ctx->p_lm)) {
     ec_destroy(ctx);
     return fail(EC_ERR_UNSUPPORTED, "no GEMV plan for this shape");
   }
@@ -361,6 +370,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     sb.window = c.window;
     sb.sparse_blocks_k = c.sparse_blocks_k;
     TRY(ec::gemv_prepare());
+    TRY(ec::packed_prepare());
     TRY(ec::attn_prepare(ctx->kv, ctx->lsh, sb));
   }
 #undef TRY
@@ -388,6 +398,28 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
     std::vector<float> v(rows, s);
     return cudaMemcpy2D(dst, stride * 4, v.data(), 4, 4, rows, cudaMemcpyHostToDevice);
   };
+  // nr row-major rows of m.cols bytes -> packed rows row_base + row_stride*i
+  auto put_rows = [&](Mat& m, const void* src, int nr, int row_base, int row_stride) -> cudaError_t {
+    const size_t bytes = (size_t)nr * m.cols;
+    const uint8_t* d = static_cast<const uint8_t*>(src);
+    void* tmp = nullptr;
+    cudaError_t e2;
+    if (!on_device) {
+      if ((e2 = cudaMalloc(&tmp, bytes)) != cudaSuccess) return e2;
+      // same stream as the pack: a pageable cudaMemcpy may return before its
+      // DMA has landed, and ctx->stream does not wait for the legacy stream
+      if ((e2 = cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, ctx->stream)) !=
+          cudaSuccess) {
+        cudaFree(tmp);
+        return e2;
+      }
+      d = static_cast<const uint8_t*>(tmp);
+    }
+    e2 = ec::packed_pack(d, m.w, m.rows, m.cols, nr, row_base, row_stride, ctx->stream);
+    if (e2 == cudaSuccess) e2 = cudaStreamSynchronize(ctx->stream);
+    if (tmp) cudaFree(tmp);
+    return e2;
+  };
   cudaError_t e = cudaSuccess;
   if (layer < 0) {
     switch (which) {
@@ -398,12 +430,13 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
         e = cudaMemcpy(ctx->final_norm, data, (size_t)D * 2, kind);
         break;
       case EC_LM_HEAD:
-        e = cudaMemcpy(ctx->lm.w, data, (size_t)c.vocab_size * D, kind);
+        e = put_rows(ctx->lm, data, c.vocab_size, 0, 1);
         if (e == cudaSuccess) e = put_scales(ctx->lm.scale, c.vocab_size, 1);
         break;
       default:
         return fail(EC_ERR_ARG, "unknown global tensor id");
     }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
     ctx->have_global |= 1u << (which - EC_EMBEDDING);
     return EC_OK;
@@ -414,24 +447,24 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
       const int r0 = which == EC_WQ ? 0 : (which == EC_WK ? H * hd : (H + KV) * hd);
       const int nr = which == EC_WQ ? H * hd : KV * hd;
       Mat& m = ctx->qkv[layer];
-      e = cudaMemcpy(m.w + (size_t)r0 * D, data, (size_t)nr * D, kind);
+      e = put_rows(m, data, nr, r0, 1);
       if (e == cudaSuccess) e = put_scales(m.scale + r0, nr, 1);
       break;
     }
     case EC_WO:
-      e = cudaMemcpy(ctx->wo[layer].w, data, (size_t)D * H * hd, kind);
+      e = put_rows(ctx->wo[layer], data, D, 0, 1);
       if (e == cudaSuccess) e = put_scales(ctx->wo[layer].scale, D, 1);
       break;
     case EC_W1: case EC_W3: {
       // interleave: row 2i = gate i, row 2i+1 = up i
       Mat& m = ctx->w13[layer];
       const int off = which == EC_W1 ? 0 : 1;
-      e = cudaMemcpy2D(m.w + (size_t)off * D, 2 * (size_t)D, data, D, D, F, kind);
+      e = put_rows(m, data, F, off, 2);
       if (e == cudaSuccess) e = put_scales(m.scale + off, F, 2);
       break;
     }
     case EC_W2:
-      e = cudaMemcpy(ctx->w2[layer].w, data, (size_t)D * F, kind);
+      e = put_rows(ctx->w2[layer], data, D, 0, 1);
       if (e == cudaSuccess) e = put_scales(ctx->w2[layer].scale, D, 1);
       break;
     case EC_ATTN_NORM:
@@ -443,6 +476,8 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
     default:
       return fail(EC_ERR_ARG, "unknown layer tensor id");
   }
+  // every copy above complete before the decode stream can read it
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
   ctx->have[layer] |= 1u << which;
   return EC_OK;
@@ -471,7 +506,7 @@ extern "C" int ec_reset(ec_ctx* ctx, int seq) {
 
 namespace {
 
-cudaError_t gemv(ec_ctx* ctx, int kind, const Mat& m, const ec::GemvPlan& plan, int pro,
+cudaError_t gemv(ec_ctx* ctx, int kind, const Mat& m, const ec::PackedPlan& plan, int pro,
                  int epi, const float* x, const uint16_t* nw, float* y) {
   // algorithmic bytes: weights + row scales + x (+ norm weight) + y (+ y read)
   const double by = (double)m.rows * m.cols + 4.0 * m.rows + 4.0 * m.cols +
@@ -492,7 +527,7 @@ cudaError_t gemv(ec_ctx* ctx, int kind, const Mat& m, const ec::GemvPlan& plan, 
   p.silu_vec_limit = (m.rows / 2) & ~7;
   p.err = ctx->err;
   ctx->launches++;
-  return ec::gemv_launch(ctx->c.weight_kind, pro, epi, plan, p, ctx->stream, true);
+  return ec::packed_launch(ctx->c.weight_kind, pro, epi, plan, p, ctx->stream, true);
 }
 
 // Enqueue one decode step for B sequences (tokens/pos in device memory).
@@ -817,6 +852,46 @@ extern "C" int ec_op_gemv(int wkind, const void* w, const float* scale, const fl
   p.K = k;
   EC_CUDA_TRY(ec::gemv_launch(wkind, ec::PRO_NONE, ec::EPI_STORE, plan, p,
                               static_cast<cudaStream_t>(stream), false));
+  return EC_OK;
+}
+
+extern "C" size_t ec_gemv_packed_bytes(int m, int k) {
+  return (m > 0 && k > 0) ? ec::packed_bytes(m, k) : 0;
+}
+
+extern "C" int ec_gemv_pack(const void* w_rowmajor, void* w_packed, int m, int k, void* stream) {
+  if (!w_rowmajor || !w_packed || m <= 0 || k <= 0) return fail(EC_ERR_ARG, "bad argument");
+  if (k % 32) return fail(EC_ERR_UNSUPPORTED, "k must be a multiple of 32");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // padding rows of the last quad read as zero
+  EC_CUDA_TRY(cudaMemsetAsync(w_packed, 0, ec::packed_bytes(m, k), s));
+  EC_CUDA_TRY(ec::packed_pack(static_cast<const uint8_t*>(w_rowmajor),
+                              static_cast<uint8_t*>(w_packed), m, k, m, 0, 1, s));
+  return EC_OK;
+}
+
+extern "C" int ec_op_gemv_packed(int wkind, const void* w, const float* scale, const float* x,
+                                 float* y, int m, int k, void* stream) {
+  if (!w || !x || !y || !scale || m <= 0 || k <= 0) return fail(EC_ERR_ARG, "bad argument");
+  if (wkind != EC_W_INT8 && wkind != EC_W_FP8) return fail(EC_ERR_ARG, "INT8 or FP8 weights");
+  if (k % 32) return fail(EC_ERR_UNSUPPORTED, "k must be a multiple of 32");
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  EC_CUDA_TRY(ec::packed_prepare());
+  ec::PackedPlan plan;
+  if (!ec::packed_plan(wkind, m, k, nsm, gemv_force_r(), &plan))
+    return fail(EC_ERR_UNSUPPORTED, "no GEMV plan for this shape");
+  ec::GemvParams p{};
+  p.w = static_cast<const uint8_t*>(w);
+  p.scale = scale;
+  p.scale_stride = (wkind == EC_W_INT8) ? 1 : 0;
+  p.x = x;
+  p.y = y;
+  p.N = m;
+  p.K = k;
+  EC_CUDA_TRY(ec::packed_launch(wkind, ec::PRO_NONE, ec::EPI_STORE, plan, p,
+                                static_cast<cudaStream_t>(stream), false));
   return EC_OK;
 }
 

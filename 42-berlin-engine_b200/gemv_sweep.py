@@ -60,9 +60,20 @@ def run_case(torch, eng, kind, n, k, args, peak):
     y = torch.empty(n, device=dev)
     sptr = sc.data_ptr() if sc is not None else None
 
+    op = L.ec_op_gemv
+    if args.layout == "packed" and kind != "bf16":
+        # the decode step's layout: repack each copy once, outside the timing
+        op = L.ec_op_gemv_packed
+        pk = []
+        for w_ in ws:
+            dst = torch.empty(L.ec_gemv_packed_bytes(n, k), dtype=torch.uint8, device=dev)
+            eng.check(L.ec_gemv_pack(w_.data_ptr(), dst.data_ptr(), n, k, stream.cuda_stream))
+            pk.append(dst)
+        ws = pk
+
     def run(i):
-        eng.check(L.ec_op_gemv(wk, ws[i % copies].data_ptr(), sptr, x.data_ptr(), y.data_ptr(),
-                               n, k, stream.cuda_stream))
+        eng.check(op(wk, ws[i % copies].data_ptr(), sptr, x.data_ptr(), y.data_ptr(),
+                     n, k, stream.cuda_stream))
 
     for i in range(args.warmup):
         run(i)
@@ -76,7 +87,7 @@ def run_case(torch, eng, kind, n, k, args, peak):
     us = ev[0].elapsed_time(ev[1]) * 1e3 / args.iters
     algo = wbytes + (4 * n if kind == "int8" else 4) + 4 * k + 4 * n
     gbs = algo / (us * 1e-6) / 1e9
-    return {"kernel": "gemv", "kind": kind, "N": n, "K": k, "batch": 1, "us": round(us, 2),
+    return {"kernel": "gemv", "layout": args.layout, "kind": kind, "N": n, "K": k, "batch": 1, "us": round(us, 2),
             "algo_bytes": algo, "GBps": round(gbs, 1), "frac_of_measured_peak": round(gbs / peak, 4),
             "l2": f"{copies} rotating weight copies"}
 
@@ -88,6 +99,8 @@ def main():
     ap.add_argument("--shapes", default=",".join(f"{n}x{k}" for n, k in SHAPES))
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--layout", default="packed", choices=["packed", "rowmajor"],
+                    help="packed: the decode step's kernel; rowmajor: ec_op_gemv")
     ap.add_argument("--l2-bytes", type=float, default=512e6, help="bytes of weight copies rotated")
     args = ap.parse_args()
     eng = _load("engine")

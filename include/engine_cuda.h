@@ -164,6 +164,18 @@ int		ec_launches_per_step(ec_ctx *ctx, int B);
 int		ec_op_gemv(int wkind, const void *w, const float *scale, const float *x,
 			float *y, int m, int k, void *stream);
 
+/* The same op_matmul over weights held in the layout the decode step streams
+** (rows in groups of 4, interleaved by 32-byte pieces within chunks of 512
+** or 32 columns; see gemv_packed.cu).  ec_gemv_packed_bytes gives the size of
+** a packed m x k matrix, ec_gemv_pack fills it from row-major device weights
+** (INT8 or FP8 bytes), and ec_op_gemv_packed computes y = W . x, bit-identical
+** to ec_op_gemv on the row-major matrix.  k must be a multiple of 32. */
+size_t	ec_gemv_packed_bytes(int m, int k);
+int		ec_gemv_pack(const void *w_rowmajor, void *w_packed, int m, int k,
+			void *stream);
+int		ec_op_gemv_packed(int wkind, const void *w_packed, const float *scale,
+			const float *x, float *y, int m, int k, void *stream);
+
 /* op_rmsnorm (src/compute/ops.h:34, ops_norm.c:126); out may alias x. */
 int		ec_op_rmsnorm(float *out, const float *x, const uint16_t *w, int n,
 			float eps, void *stream);

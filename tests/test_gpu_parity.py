@@ -75,6 +75,39 @@ def test_gemv(eng, torch, synth, oracle, kind, m, k):
     assert np.array_equal(bits(dy.cpu().numpy()), bits(y))
 
 
+@pytest.mark.parametrize("rows_per_thread", ["0", "1", "2"])
+@pytest.mark.parametrize("kind", ["int8", "fp8"])
+@pytest.mark.parametrize("m,k", [(37, 64), (6, 1024), (300, 512), (4096, 4096), (1000, 14336),
+                                 (2816, 1408), (130, 4096), (6144, 4096)])
+def test_gemv_packed(eng, torch, synth, oracle, monkeypatch, rows_per_thread, kind, m, k):
+    """The decode step's GEMV (packed weight layout, chunks of 512 or 32
+    columns, 1 or 2 rows per thread, ragged last row quad) == the
+    restatement of op_matmul, bit for bit."""
+    monkeypatch.setenv("EC_GEMV_ROWS_PER_THREAD", rows_per_thread)
+    rng = np.random.default_rng(m * 11 + k)
+    w = rng.standard_normal((m, k), dtype=np.float32) * np.float32(0.02)
+    x = rng.standard_normal(k, dtype=np.float32)
+    y = np.zeros(m, np.float32)
+    P = oracle.port()
+    if kind == "int8":
+        q, s = synth.quant_int8_rows(w, pow2=False)
+        P.port_gemv_q8(y, q, s, x, m, k)
+        wk = eng.EC_W_INT8
+    else:
+        q, s = synth.quant_fp8_tensor(w)
+        P.port_gemv_fp8(y, q, np.float32(s[0]), x, m, k)
+        wk = eng.EC_W_FP8
+    L = eng.lib()
+    dq, dx, ds = dev(torch, q), dev(torch, x), dev(torch, s)
+    packed = torch.full((L.ec_gemv_packed_bytes(m, k),), 7, dtype=torch.uint8, device="cuda")
+    eng.check(L.ec_gemv_pack(dq.data_ptr(), packed.data_ptr(), m, k, None))
+    dy = torch.full((m,), float("nan"), dtype=torch.float32, device="cuda")
+    eng.check(L.ec_op_gemv_packed(wk, packed.data_ptr(), ds.data_ptr(), dx.data_ptr(),
+                                  dy.data_ptr(), m, k, None))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(dy.cpu().numpy()), bits(y))
+
+
 def test_small_ops(eng, torch):
     L = eng.lib()
     # RMSNorm
