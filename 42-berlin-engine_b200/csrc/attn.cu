@@ -222,84 +222,86 @@ __device__ __forceinline__ float dot_bf16_ref(const uint16_t* a, const float* b,
   return s;
 }
 
-// Min-heap replay of heap_push (ops_heap.h:40-100) on shared arrays.
-// Stored 1-based (node n at [n], children 2n, 2n+1 adjacent) so a level of
-// sift-down reads both children with one 8-byte load; the element being
-// placed is carried in registers ("hole" sifting).  Comparisons are the
-// reference's: sift-up stops when parent <= value; sift-down picks the left
-// child unless the right one is strictly smaller, and moves on only while the
-// chosen child is strictly smaller than the value.
-__device__ __forceinline__ void heap_up(float* hs, int* hi, int n, float v, int vi) {
+// Exact replay of heap_push (ops_heap.h:40-100): a min-heap of at most `cap`
+// entries; while not full a value is appended at position size+1 and sifted
+// up past every ancestor strictly greater than it; once full, a value
+// strictly greater than the root replaces it and is sifted down (the left
+// child unless the right one is strictly smaller, while that child is
+// strictly smaller than the value).  The result, in the reference's heap
+// array order, is the index half of hp[1 .. size].
+//
+// Nodes are packed (score bits, index) pairs, 1-based, so a sibling pair is
+// one 16-byte load; positions beyond `size` hold +inf, so a sift-down of
+// fixed depth D (2^D > cap) needs no bound checks: an +inf child is never
+// taken.  One warp: a ballot skips every candidate that cannot beat the
+// current root (the root only grows), lane 0 runs the operations.
+__device__ __forceinline__ void hnode_up(uint2* hp, int n, float v, int vi) {
   while (n > 1) {
     const int p = n >> 1;
-    const float ps = hs[p];
-    if (ps <= v) break;
-    hs[n] = ps;
-    hi[n] = hi[p];
+    const uint2 pn = hp[p];
+    if (__uint_as_float(pn.x) <= v) break;
+    hp[n] = pn;
     n = p;
   }
-  hs[n] = v;
-  hi[n] = vi;
+  hp[n] = make_uint2(__float_as_uint(v), (unsigned)vi);
 }
 
-__device__ __forceinline__ void heap_down(float* hs, int* hi, int size, float v, int vi) {
+template <int D>
+__device__ __forceinline__ void hnode_down(uint2* hp, float v, int vi) {
   int n = 1;
-  for (;;) {
+  bool go = true;
+#pragma unroll
+  for (int lv = 0; lv < D; lv++) {
     const int l = 2 * n;
-    if (l > size) break;
-    int c = l;
-    float cs;
-    if (l + 1 <= size) {
-      const float2 pr = *reinterpret_cast<const float2*>(hs + l);
-      cs = pr.x;
-      if (pr.y < pr.x) {
-        c = l + 1;
-        cs = pr.y;
-      }
-    } else {
-      cs = hs[l];
+    const uint4 pr = *reinterpret_cast<const uint4*>(hp + l);
+    const bool right = __uint_as_float(pr.z) < __uint_as_float(pr.x);
+    const uint2 cn = right ? make_uint2(pr.z, pr.w) : make_uint2(pr.x, pr.y);
+    go = go && (__uint_as_float(cn.x) < v);
+    if (go) {
+      hp[n] = cn;
+      n = l + right;
     }
-    if (!(cs < v)) break;
-    hs[n] = cs;
-    hi[n] = hi[c];
-    n = c;
   }
-  hs[n] = v;
-  hi[n] = vi;
+  hp[n] = make_uint2(__float_as_uint(v), (unsigned)vi);
 }
 
-// Replays heap_push over (score[i], idx[i]) i < n with capacity cap, by one
-// warp: a ballot drops candidates that cannot beat the current root (the
-// root only grows), lane 0 performs the pushes that can.  hs/hi hold cap + 2
-// entries (1-based, hs 8-byte aligned).  The result, in the reference's heap
-// array order, is hi[1 .. size].  idx == nullptr means candidate i carries
-// index i + idx_base.
-__device__ int warp_heap_topk(const float* score, const int* idx, int n, int cap, float* hs,
-                              int* hi, int lane, int idx_base = 0) {
-  int size = 0;
-  float root = -FLT_MAX;
+// hp holds 2^(D+1) nodes.  `ready(j)` (whole warp, j non-decreasing) returns
+// once score[0..j] may be read, or false to give up.  idx == nullptr:
+// candidate i carries index i + idx_base.  Candidates go by windows of 32: a
+// ballot against the root at the window's start drops those that cannot be
+// taken (the root only grows); lane 0 runs the rest in order.
+template <int D, typename Ready>
+__device__ int warp_heap_select(const float* score, const int* idx, int idx_base, int n, int cap,
+                                uint2* hp, int lane, Ready ready) {
+  for (int i = lane; i < (2 << D); i += 32) hp[i] = make_uint2(0x7F800000u, 0u);
+  __syncwarp();
+  if (cap <= 0) return 0;
+  int size = 0;      // lane 0's copy is authoritative; broadcast per window
+  float root = 0.0f;
   for (int base = 0; base < n; base += 32) {
+    if (!ready(min(base + 31, n - 1))) return 0;
     const int i = base + lane;
-    const float sv = (i < n) ? score[i] : 0.0f;
-    const int iv = (i < n) ? (idx ? idx[i] : i + idx_base) : 0;
-    unsigned pend = __ballot_sync(0xffffffffu, i < n);
-    if (size >= cap) pend &= __ballot_sync(0xffffffffu, sv > root);
-    while (pend) {
-      const int L = __ffs(pend) - 1;
-      const float sL = __shfl_sync(0xffffffffu, sv, L);
-      const int iL = __shfl_sync(0xffffffffu, iv, L);
-      if (lane == 0) {
-        if (size < cap)
-          heap_up(hs, hi, size + 1, sL, iL);
-        else if (sL > hs[1])
-          heap_down(hs, hi, size, sL, iL);
+    const bool full = size >= cap;
+    const float sv = i < n ? score[i] : 0.0f;
+    unsigned pend = __ballot_sync(0xffffffffu, i < n && (!full || sv > root));
+    if (lane == 0) {
+      while (pend) {
+        const int k = base + __ffs(pend) - 1;
+        pend &= pend - 1;
+        const float v = score[k];
+        const int vi = idx ? idx[k] : k + idx_base;
+        if (size < cap) {
+          hnode_up(hp, ++size, v, vi);
+          if (size == cap) root = __uint_as_float(hp[1].x);
+        } else if (v > root) {
+          hnode_down<D>(hp, v, vi);
+          root = __uint_as_float(hp[1].x);
+        }
       }
-      __syncwarp();
-      if (size < cap) size++;
-      root = hs[1];
-      pend &= ~(1u << L);
-      if (size >= cap) pend &= __ballot_sync(0xffffffffu, sv > root);
     }
+    size = __shfl_sync(0xffffffffu, size, 0);
+    root = __shfl_sync(0xffffffffu, root, 0);
+    __syncwarp();
   }
   return size;
 }
@@ -312,9 +314,8 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;  // candidate capacity
   int* cand = reinterpret_cast<int*>(smem);               // [cap_c]
   float* cscore = reinterpret_cast<float*>(cand + cap_c);  // [cap_c]
-  float* hs = cscore + cap_c;                             // [sparse_k + 2], 1-based
-  int* hi = reinterpret_cast<int*>(hs + sb.sparse_k + 2);  // [sparse_k + 2]
-  float* qm = reinterpret_cast<float*>(hi + sb.sparse_k + 2);  // [hd]
+  uint2* hp = reinterpret_cast<uint2*>(cscore + cap_c);  // [1024] heap nodes, 1-based
+  float* qm = reinterpret_cast<float*>(hp + 1024);         // [hd]
   __shared__ uint32_t s_code[16];
   __shared__ int s_units[64];
   __shared__ int s_nu, s_nc, s_wcount;
@@ -421,34 +422,17 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
   __syncthreads();
   if (warp == 0) {
     const int cap = nc < sb.sparse_k ? nc : sb.sparse_k;
-    const int size = warp_heap_topk(cscore, cand, nc, cap, hs, hi, lane);
+    auto all = [](int) { return true; };
+    const int size = cap < 64 ? warp_heap_select<6>(cscore, cand, 0, nc, cap, hp, lane, all)
+                              : warp_heap_select<9>(cscore, cand, 0, nc, cap, hp, lane, all);
     int* out = sb.sel + (long)b * sb.max_sel;
-    for (int i = lane; i < size; i += 32) out[i] = hi[i + 1];
+    for (int i = lane; i < size; i += 32) out[i] = (int)hp[i + 1].y;
     if (lane == 0) {
       sb.nsel[b] = size;
       lsh.counters[b * 2] += 1ull;
       lsh.counters[b * 2 + 1] += (unsigned long long)size;
     }
   }
-}
-
-// heap_push over score[0..n) (indices i + idx_base) with capacity cap, by
-// one thread; result hi[1..size] in the reference's heap array order.
-__device__ int heap_topk_seq(const float* score, int n, int cap, float* hs, int* hi,
-                             int idx_base) {
-  int size = 0;
-  int i = 0;
-  for (; i < n && size < cap; i++) heap_up(hs, hi, ++size, score[i], i + idx_base);
-  float root = size ? hs[1] : 0.0f;
-#pragma unroll 4
-  for (; i < n; i++) {
-    const float s = score[i];
-    if (s > root) {
-      heap_down(hs, hi, size, s, i + idx_base);
-      root = hs[1];
-    }
-  }
-  return size;
 }
 
 // ------------------------------------------------------------------------
@@ -458,16 +442,21 @@ __device__ int heap_topk_seq(const float* score, int n, int cap, float* hs, int*
 // heap_push of blocks 1..nb-2, heap array order).  Only full middle blocks
 // are scored, so this runs concurrently with this step's append.  Writes
 // sel[b] / nsel[b] (nsel = -1: attend to every block).
+//
+// Warps 1..7 stage centroids in rounds of kChunk blocks (double-buffered bulk
+// copies) and score them, publishing how many are done; warp 0 replays the
+// heap over the scores as they arrive.  256 threads.
 // ------------------------------------------------------------------------
 __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int layer, int b) {
-  constexpr int kChunkBlocks = 32;  // centroids staged per round (16 KB at hd 128)
-  __shared__ __align__(16) float s_q[256];
-  __shared__ __align__(16) float s_c[2 * kChunkBlocks * 128];
-  __shared__ int s_nsel;
+  constexpr int kChunk = 32;  // centroids per staging round (16 KB at hd 128)
+  constexpr int kScorers = 224;
+  __shared__ __align__(16) float s_q[128];
+  __shared__ __align__(16) float s_c[2 * kChunk * 128];
   __shared__ __align__(16) float s_bsc[2048];
-  __shared__ __align__(16) float s_hs[68];
-  __shared__ int s_hi[68];
+  __shared__ __align__(16) uint2 s_hp[128];
   __shared__ __align__(8) uint64_t s_bar[2];
+  __shared__ int s_ready;  // middle-block scores [0, s_ready) are written
+  __shared__ int s_nsel;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim, half = hd >> 1;
   if (!kv.paged) return;
@@ -489,6 +478,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
     mbar_init(&s_bar[0], 1);
     mbar_init(&s_bar[1], 1);
     fence_mbar_init();
+    s_ready = 0;
   }
   // query head 0, rotated here (the append CTA rotates its own copy)
   const float* q = sb.q_rotated ? sb.qrot + (long)b * H * hd : sb.qkv + (long)b * (H + 2 * KV) * hd;
@@ -506,47 +496,70 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
   __syncthreads();
   const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
   const int* pt = kv.page_table + base;
-  // score_blocks over the middle blocks 1 .. nb-2: centroids staged in rounds
-  // of kChunkBlocks (double-buffered); 8 threads per block run the 8 lanes of
-  // simd_dot_f32_f32 and combine them in its horizontal-sum order
   const int nmid = nb - 2;
-  const int nround = (nmid + kChunkBlocks - 1) / kChunkBlocks;
-  auto issue = [&](int r) {
-    const int c0 = 1 + r * kChunkBlocks;
-    const int cn = min(kChunkBlocks, nb - 1 - c0);
-    float* dst = s_c + (r & 1) * kChunkBlocks * 128;
-    if (lane == 0) mbar_expect_tx(&s_bar[r & 1], (uint32_t)(cn * hd * 4));
-    __syncwarp();
-    for (int i = lane; i < cn; i += 32)
-      bulk_g2s(dst + i * hd, kv.centroid + (base + pt[c0 + i]) * hd, hd * 4, &s_bar[r & 1]);
-  };
-  if (warp == 0) issue(0);
-  bool ok = true;
-  for (int r = 0; r < nround; r++) {
-    if (warp == 0 && r + 1 < nround) issue(r + 1);
-    if (ok) ok = mbar_wait(&s_bar[r & 1], (r >> 1) & 1, sb.err);
-    const int c0 = 1 + r * kChunkBlocks;
-    const int cn = min(kChunkBlocks, nb - 1 - c0);
-    const float* cb = s_c + (r & 1) * kChunkBlocks * 128;
-    const int blk = tid >> 3, l = tid & 7;
-    float acc = 0.0f;
-    if (blk < cn && ok)
-      for (int d = l; d < hd; d += 8) acc = __fmaf_rn(s_q[d], cb[blk * hd + d], acc);
-    // ((c0+c4)+(c1+c5)) + ((c2+c6)+(c3+c7))
-    const float h4 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
-    const float t2 = __fadd_rn(h4, __shfl_xor_sync(0xffffffffu, h4, 1));
-    const float sum = __fadd_rn(t2, __shfl_xor_sync(0xffffffffu, t2, 2));
-    if (blk < cn && l == 0) s_bsc[c0 + blk] = sum;
-    __syncthreads();
-  }
   int m = sb.sparse_blocks_k - 2;
-  if (m > nb - 2) m = nb - 2;
+  if (m > nmid) m = nmid;
   if (m > 62) m = 62;
-  PHASE_MARK(tid == 0 && layer == 1, 1);
-  if (tid == 0) {
-    const int size = heap_topk_seq(s_bsc + 1, nmid, m, s_hs, s_hi, 1);
-    PHASE_MARK(true && layer == 1, 2);
-    s_nsel = size;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ heap
+    auto ready = [&](int j) -> bool {
+      for (uint32_t it = 0; it < kWaitLimit; it++) {
+        if (*reinterpret_cast<volatile int*>(&s_ready) > j) {
+          __threadfence_block();
+          return true;
+        }
+      }
+      if (lane == 0) atomicCAS(sb.err, 0, EC_ERR_TIMEOUT);
+      return false;
+    };
+    const int size = warp_heap_select<6>(s_bsc, nullptr, 1, nmid, m, s_hp, lane, ready);
+    PHASE_MARK(lane == 0 && layer == 1, 2);
+    if (lane == 0) s_nsel = size;
+  } else {
+    // -------------------------------------------- score_blocks, in rounds
+    // 8 threads per block run the 8 lanes of simd_dot_f32_f32 and combine
+    // them in its horizontal-sum order
+    const int ct = tid - 32;
+    const int nround = (nmid + kChunk - 1) / kChunk;
+    auto issue = [&](int r) {
+      const int c0 = 1 + r * kChunk;
+      const int cn = min(kChunk, nb - 1 - c0);
+      float* dst = s_c + (r & 1) * kChunk * 128;
+      if (lane == 0) mbar_expect_tx(&s_bar[r & 1], (uint32_t)(cn * hd * 4));
+      __syncwarp();
+      for (int i = lane; i < cn; i += 32)
+        bulk_g2s(dst + i * hd, kv.centroid + (base + pt[c0 + i]) * hd, hd * 4, &s_bar[r & 1]);
+    };
+    if (warp == 1) {
+      issue(0);
+      if (nround > 1) issue(1);
+    }
+    bool ok = true;
+    for (int r = 0; r < nround; r++) {
+      if (ok) ok = mbar_wait(&s_bar[r & 1], (r >> 1) & 1, sb.err);
+      const int c0 = r * kChunk;  // middle index of the round's first block
+      const int cn = min(kChunk, nmid - c0);
+      const float* cb = s_c + (r & 1) * kChunk * 128;
+      for (int bb = 0; bb < cn; bb += kScorers / 8) {
+        const int blk = bb + (ct >> 3), l = ct & 7;
+        float acc = 0.0f;
+        if (blk < cn && ok)
+          for (int d = l; d < hd; d += 8) acc = __fmaf_rn(s_q[d], cb[blk * hd + d], acc);
+        // ((c0+c4)+(c1+c5)) + ((c2+c6)+(c3+c7))
+        const float h4 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+        const float t2 = __fadd_rn(h4, __shfl_xor_sync(0xffffffffu, h4, 1));
+        const float sum = __fadd_rn(t2, __shfl_xor_sync(0xffffffffu, t2, 2));
+        if (blk < cn && l == 0) s_bsc[c0 + blk] = sum;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(kScorers));  // scores written, buffer free
+      if (ct == 0) {
+        __threadfence_block();
+        *reinterpret_cast<volatile int*>(&s_ready) = c0 + cn;
+      }
+      if (warp == 1 && r + 2 < nround) issue(r + 2);
+    }
+    PHASE_MARK(ct == 0 && layer == 1, 1);
   }
   __syncthreads();
   if (warp == 0) {
@@ -557,7 +570,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
       out[1] = nb - 1;
       sb.nsel[b] = 2 + size;
     }
-    for (int i = lane; i < size; i += 32) out[2 + i] = s_hi[1 + i];
+    for (int i = lane; i < size; i += 32) out[2 + i] = (int)s_hp[1 + i].y;
   }
 }
 
@@ -571,9 +584,11 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
 //      recurrence for one dimension each, the next warp the denominator.
 // ------------------------------------------------------------------------
 constexpr int kAttnThreads = 512;
+constexpr int kRingTok = 32;  // V tokens per ring chunk
+constexpr int kRing = 3;      // ring chunks
 
 struct AttnSmemLayout {
-  size_t kv, sc, sf, tks, tvs, lpos, boff, bphys, bfill, ksb, vsb, total;
+  size_t kv, sc, sf, tks, tvs, lpos, boff, bphys, bfill, ksb, vsb, ring, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -585,15 +600,15 @@ __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int e
   L.kv = o;
   o = align_up(o + (size_t)max_tok * hd * esize, 16);
   L.sc = o;
-  o += (size_t)max_tok * 4;
+  o += (size_t)(max_tok + 8) * 4;
   L.sf = o;
-  o += (size_t)max_tok * 4;
+  o += (size_t)(max_tok + 8) * 4;
   L.tks = o;
-  o += (size_t)max_tok * 4;
+  o += (size_t)(max_tok + 8) * 4;
   L.tvs = o;
-  o += (size_t)max_tok * 4;
+  o += (size_t)(max_tok + 8) * 4;
   L.lpos = o;
-  o += (size_t)max_tok * 4;
+  o += (size_t)(max_tok + 8) * 4;
   L.boff = o;
   o += nblk * 4;
   L.bphys = o;
@@ -601,10 +616,9 @@ __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int e
   L.bfill = o;
   o += nblk * 4;
   o = align_up(o, 16);
-  L.ksb = o;
-  o += nblk * 16 * 4;
-  L.vsb = o;
-  o += nblk * 16 * 4;
+  L.ksb = L.vsb = o;  // unused
+  L.ring = o;
+  o += (size_t)kRing * kRingTok * hd * 4;
   L.total = o;
   return L;
 }
@@ -614,6 +628,21 @@ __device__ __forceinline__ float s8_to_f32(uint32_t byte) {
   return __fsub_rn(__uint_as_float(byte ^ 0x4B000080u), 8388736.0f);
 }
 
+// Attention for one (query head, sequence): op_paged_attention(_sparse)
+// (ops_attention.c:292-461) over the selected paged blocks in selection
+// order, or attention_head_sparse (ops_attention.c:131-170) over linear-mode
+// positions.  Phases:
+//   1. the selected K rows (and per-token scales) land in shared memory by
+//      bulk copies; block offsets come from a warp prefix sum;
+//   2. scores s_t = dot(q, k_t) * (1/sqrt(hd)) in the reference's 8-lane
+//      order (paired f32x2 arithmetic, same roundings);
+//   3. the running max m_t = max(m_{t-1}, s_t) by a block-wide max-scan, then
+//      both exponentials of every token in parallel (fast_expf);
+//   4. V rows land in the same buffer; spare warps dequantise them into a
+//      ring of float chunks; threads 0..hd-1 run the output recurrence
+//      o_t = fma(e_t, v_t, o_{t-1} * f_t) for one dimension each (the multiply
+//      skipped over runs where every f_t is 1), one more warp the
+//      denominator; out = o / sum.
 template <bool PAGED>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, StepBuffers sb,
                                                                  int layer, int max_tok) {
@@ -630,19 +659,24 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   float* tks = reinterpret_cast<float*>(smem + Ly.tks);
   float* tvs = reinterpret_cast<float*>(smem + Ly.tvs);
   int* lpos = reinterpret_cast<int*>(smem + Ly.lpos);
-  uint8_t* ttok = reinterpret_cast<uint8_t*>(lpos);  // paged: token index within its block
   int* boff = reinterpret_cast<int*>(smem + Ly.boff);
   int* bphys = reinterpret_cast<int*>(smem + Ly.bphys);
   int* bfill = reinterpret_cast<int*>(smem + Ly.bfill);
-  float* ksb = reinterpret_cast<float*>(smem + Ly.ksb);
-  float* vsb = reinterpret_cast<float*>(smem + Ly.vsb);
+  float* ring = reinterpret_cast<float*>(smem + Ly.ring);
   __shared__ __align__(8) uint64_t bar[2];
+  __shared__ __align__(8) uint64_t rfull[kRing], rempty[kRing];
   __shared__ int s_ntok, s_nsel;
   __shared__ float s_wmax[kAttnThreads / 32];
   __shared__ float s_sum;
+  const int cw = (hd + 31) >> 5;                   // chain warps
+  const int npw = kAttnThreads / 32 - cw - 1;      // ring producer warps
   if (tid == 0) {
     mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    mbar_init(&bar[1], kAttnThreads);  // one cp.async arrival per thread
+    for (int k = 0; k < kRing; k++) {
+      mbar_init(&rfull[k], npw);
+      mbar_init(&rempty[k], cw);
+    }
     fence_mbar_init();
   }
   pdl_launch_dependents();
@@ -657,6 +691,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   bool ok = true;
 
   // ------------------------------------------ selected blocks / positions
+  int* trow = lpos;  // paged: K/V row of token i, (block * KV + kvh) * 16 + t
+  const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;  // linear mode
   if constexpr (PAGED) {
     const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
     const int nb = (n_tok + kBlk - 1) / kBlk;
@@ -665,42 +701,43 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
     const int ns = sb.nsel[b];
     const int* sel = sb.sel + (long)b * sb.max_sel;
     const int nsel = ns > 0 ? ns : nb;  // selection order, or every block in order
-    for (int k = tid; k < nsel; k += blockDim.x) {
-      const int lb = ns > 0 ? sel[k] : k;
-      bphys[k] = (int)(base + pt[lb]);
-      bfill[k] = (lb == nb - 1) ? n_tok - lb * kBlk : kBlk;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      int n = 0;
-      for (int k = 0; k < nsel; k++) {
-        boff[k] = n;
-        n += bfill[k];
-      }
-      s_ntok = n;
-      s_nsel = nsel;
-    }
-    __syncthreads();
-    const int T = s_ntok;
-    // K rows and both scale vectors of every selected block
     if (warp == 0) {
-      if (lane == 0) mbar_expect_tx(&bar[0], (uint32_t)(T * hd + nsel * 2 * 64));
-      __syncwarp();
-      for (int k = lane; k < nsel; k += 32) {
-        const long blk = bphys[k];
-        bulk_g2s(kvb + (size_t)boff[k] * hd, kv.kq + ((blk * KV + kvh) * kBlk) * hd,
-                 bfill[k] * hd, &bar[0]);
-        bulk_g2s(ksb + k * 16, kv.ks + (blk * KV + kvh) * kBlk, 64, &bar[0]);
-        bulk_g2s(vsb + k * 16, kv.vs + (blk * KV + kvh) * kBlk, 64, &bar[0]);
+      // block table and offsets (exclusive prefix sum of the fills)
+      int carry = 0;
+      for (int k0 = 0; k0 < nsel; k0 += 32) {
+        const int k = k0 + lane;
+        int fill = 0;
+        if (k < nsel) {
+          const int lb = ns > 0 ? sel[k] : k;
+          bphys[k] = (int)(base + pt[lb]);
+          fill = (lb == nb - 1) ? n_tok - lb * kBlk : kBlk;
+          bfill[k] = fill;
+        }
+        int incl = fill;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        if (k < nsel) boff[k] = carry + incl - fill;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
       }
+      if (lane == 0) {
+        s_ntok = carry;
+        s_nsel = nsel;
+      }
+      PHASE_MARK(mk && lane == 0, 15);
     }
-    ok = mbar_wait(&bar[0], 0, sb.err);
-    for (int j = tid; j < nsel * kBlk; j += blockDim.x) {
+    __syncthreads();
+    const int nsl = s_nsel;
+    for (int j = tid; j < nsl * kBlk; j += blockDim.x) {
       const int k = j >> 4, t = j & 15;
       if (t < bfill[k]) {
-        tks[boff[k] + t] = ksb[j];
-        tvs[boff[k] + t] = vsb[j];
-        ttok[boff[k] + t] = (uint8_t)t;
+        const int i = boff[k] + t;
+        const int row = (bphys[k] * KV + kvh) * kBlk + t;
+        trow[i] = row;
+        tks[i] = kv.ks[row];
+        tvs[i] = kv.vs[row];
       }
     }
   } else {
@@ -711,72 +748,74 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
     const int T = sparse ? ns : kv_len;
     for (int i = tid; i < T; i += blockDim.x) lpos[i] = sparse ? sel[i] : i;
     if (tid == 0) s_ntok = T;
-    __syncthreads();
-    const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;
-    if (warp == 0) {
-      if (lane == 0) mbar_expect_tx(&bar[0], (uint32_t)(T * hd * 2));
-      __syncwarp();
-      for (int i = lane; i < T; i += 32)
-        bulk_g2s(kvb + (size_t)i * hd * 2, kv.lk + ((lrow + lpos[i]) * KV + kvh) * hd, hd * 2,
-                 &bar[0]);
-    }
-    ok = mbar_wait(&bar[0], 0, sb.err);
   }
   __syncthreads();
   const int T = s_ntok;
+  // V rows -> shared memory by 16-byte asynchronous copies from every thread,
+  // completing on bar[1] (counted per thread); they land while scores run
+  {
+    const int rowb = hd * ES;
+    const int lgp = 31 - __clz(rowb >> 4);  // 16-byte pieces per row (power of 2)
+    for (int e = tid; e < (T << lgp); e += blockDim.x) {
+      const int i = e >> lgp, pc = e & ((1 << lgp) - 1);
+      const uint8_t* src;
+      if constexpr (PAGED)
+        src = reinterpret_cast<const uint8_t*>(kv.vq) + (size_t)trow[i] * hd + pc * 16;
+      else
+        src = reinterpret_cast<const uint8_t*>(kv.lv + ((lrow + lpos[i]) * KV + kvh) * hd) + pc * 16;
+      cp_async16(kvb + (size_t)i * rowb + pc * 16, src);
+    }
+    cp_async_arrive(&bar[1]);
+  }
   PHASE_MARK(mk && tid == 0, 9);
 
   // ------------------------------------------------------------- scores
-  for (int i = tid; i < T && ok; i += blockDim.x) {
+  // K rows straight from global memory (16-byte read-only loads)
+  for (int i = tid; i < T; i += blockDim.x) {
     float s;
     if constexpr (PAGED) {
-      // piece c of this token's row sits at (c + t) mod np (stored rotated)
-      const uint8_t* kr = kvb + (size_t)i * hd;
-      const int t = ttok[i];
+      // piece c of this token's row sits at (c + t) mod np (stored rotated);
+      // acc[l & 7] += q[16c + l] * (k[16c + l] * scale_t), l = 0..15
+      const int row = trow[i];
+      const uint8_t* kr = reinterpret_cast<const uint8_t*>(kv.kq) + (size_t)row * hd;
+      const int t = row & (kBlk - 1);
       const float ksc = tks[i];
+      const uint64_t ks2 = pack2(__float_as_uint(ksc), __float_as_uint(ksc));
       const int np = hd >> 4;
-      float acc[8];
+      uint4 u[8];
 #pragma unroll
-      for (int l = 0; l < 8; l++) acc[l] = 0.0f;
+      for (int c = 0; c < 8; c++)
+        if (c < np) u[c] = ldg_nc16(kr + (((c + t) & (np - 1)) << 4));
+      uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int c = 0; c < 8; c++) {
         if (c >= np) break;
-        const uint4 u = *reinterpret_cast<const uint4*>(kr + (((c + t) & (np - 1)) << 4));
-        float w[16];
-        dec_i8x4(u.x, w);
-        dec_i8x4(u.y, w + 4);
-        dec_i8x4(u.z, w + 8);
-        dec_i8x4(u.w, w + 12);
+        const ulonglong2* q2 = reinterpret_cast<const ulonglong2*>(qs + 16 * c);
+        const uint32_t wv[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
 #pragma unroll
-        for (int l = 0; l < 16; l++)
-          acc[l & 7] = __fmaf_rn(qs[16 * c + l], __fmul_rn(w[l], ksc), acc[l & 7]);
+        for (int g = 0; g < 4; g++) {
+          uint64_t w01, w23;
+          decode_pairs<EC_W_INT8>(wv[g], w01, w23);
+          const ulonglong2 qq = q2[g];
+          // elements 4g..4g+3 -> accumulator pairs (2g)&3 and (2g+1)&3
+          fma2(acc[(2 * g) & 3], mul2(w01, ks2), qq.x);
+          fma2(acc[(2 * g + 1) & 3], mul2(w23, ks2), qq.y);
+        }
       }
-      s = hsum8(acc);
+      float a8[8];
+#pragma unroll
+      for (int l = 0; l < 4; l++) {
+        a8[2 * l] = lo_f(acc[l]);
+        a8[2 * l + 1] = hi_f(acc[l]);
+      }
+      s = hsum8(a8);
     } else {
-      s = dot_bf16_ref(reinterpret_cast<const uint16_t*>(kvb) + (size_t)i * hd, qs, hd);
+      s = dot_bf16_ref(kv.lk + ((lrow + lpos[i]) * KV + kvh) * hd, qs, hd);
     }
     sc[i] = __fmul_rn(s, scale);
   }
   __syncthreads();
   PHASE_MARK(mk && tid == 0, 10);
-  // V rows into the same buffer (K is no longer needed)
-  if (warp == 0 && ok) {
-    if constexpr (PAGED) {
-      const int nsel = s_nsel;
-      if (lane == 0) mbar_expect_tx(&bar[1], (uint32_t)(T * hd));
-      __syncwarp();
-      for (int k = lane; k < nsel; k += 32)
-        bulk_g2s(kvb + (size_t)boff[k] * hd, kv.vq + (((long)bphys[k] * KV + kvh) * kBlk) * hd,
-                 bfill[k] * hd, &bar[1]);
-    } else {
-      const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;
-      if (lane == 0) mbar_expect_tx(&bar[1], (uint32_t)(T * hd * 2));
-      __syncwarp();
-      for (int i = lane; i < T; i += 32)
-        bulk_g2s(kvb + (size_t)i * hd * 2, kv.lv + ((lrow + lpos[i]) * KV + kvh) * hd, hd * 2,
-                 &bar[1]);
-    }
-  }
   // running max m_t = max(m_{t-1}, s_t) (exact), then the two exponentials
   {
     const int per = (T + blockDim.x - 1) / blockDim.x;
@@ -791,8 +830,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
     }
     if (lane == 31) s_wmax[warp] = incl;
     __syncthreads();
-    float pre = -INFINITY;
-    for (int w = 0; w < warp; w++) pre = (s_wmax[w] > pre) ? s_wmax[w] : pre;
+    if (warp == 0) {
+      // exclusive max-prefix over the warps
+      const int nw = blockDim.x >> 5;
+      float w = lane < nw ? s_wmax[lane] : -INFINITY;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float t = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w = (t > w) ? t : w;
+      }
+      const float ex = __shfl_up_sync(0xffffffffu, w, 1);
+      __syncwarp();
+      if (lane < nw) s_wmax[lane] = lane == 0 ? -INFINITY : ex;
+    }
+    __syncthreads();
+    const float pre = s_wmax[warp];
     float excl = __shfl_up_sync(0xffffffffu, incl, 1);
     if (lane == 0) excl = -INFINITY;
     float run = (excl > pre) ? excl : pre;
@@ -807,22 +859,18 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   __syncthreads();
   // flag per 8 tokens: every scale factor is 1 (the running max did not move)
   int* ones = reinterpret_cast<int*>(tks);  // K scales are no longer needed
-  for (int g = tid; g < (T >> 3); g += blockDim.x) {
+  for (int g = tid; g < (T + 7) >> 3; g += blockDim.x) {
     bool a1 = true;
-#pragma unroll
-    for (int u = 0; u < 8; u++) a1 = a1 && (sf[8 * g + u] == 1.0f);
+    for (int u = 0; u < 8 && 8 * g + u < T; u++) a1 = a1 && (sf[8 * g + u] == 1.0f);
     ones[g] = a1;
   }
   __syncthreads();
   PHASE_MARK(mk && tid == 0, 11);
-  if (ok) ok = mbar_wait(&bar[1], 0, sb.err);
-  PHASE_MARK(mk && tid == 0, 12);
 
   // -------------------------------------------------------- recurrences
-  // out_t = fma(re_t, v_t, out_{t-1} * sf_t); with sf_t == 1 the multiply is
-  // the identity and runs of eight such steps skip it.
-  const int cw = (hd + 31) >> 5;  // chain warps
+  const int nchunk = (T + kRingTok - 1) / kRingTok;
   if (warp == cw) {
+    // denominator: sum_t = fma(sum_{t-1}, f_t, e_t)
     if (lane == 0) {
       float sum = 0.0f;
       int i = 0;
@@ -843,62 +891,79 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
       for (; i < T; i++) sum = __fmaf_rn(sum, sf[i], sc[i]);
       s_sum = sum;
     }
-  } else if (tid < hd && ok) {
+  } else if (warp > cw) {
+    // ring producers: chunk c of V rows -> floats ring[c % kRing][t][d]
+    const int pt = tid - (cw + 1) * 32, np = npw * 32;
+    if (ok) ok = mbar_wait(&bar[1], 0, sb.err);
+    for (int c = 0; c < nchunk; c++) {
+      const int slot = c % kRing;
+      if (c >= kRing && ok) ok = mbar_wait(&rempty[slot], ((c / kRing) - 1) & 1, sb.err);
+      float* dst = ring + (size_t)slot * kRingTok * hd;
+      const int t0 = c * kRingTok;
+      const int nt = min(kRingTok, T - t0);
+      // four consecutive elements of one token per step: v * scale_t, exact
+      const int lg = 31 - __clz(hd) - 2;  // hd / 4 groups per token
+      for (int e4 = pt; e4 < (nt * hd >> 2) && ok; e4 += np) {
+        const int t = e4 >> lg, d = (e4 & ((hd >> 2) - 1)) << 2;
+        uint4 out;
+        if constexpr (PAGED) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(kvb + (size_t)(t0 + t) * hd + d);
+          const float ts = tvs[t0 + t];
+          const uint64_t s2 = pack2(__float_as_uint(ts), __float_as_uint(ts));
+          uint64_t p01, p23;
+          decode_pairs<EC_W_INT8>(w, p01, p23);
+          p01 = mul2(p01, s2);
+          p23 = mul2(p23, s2);
+          out = make_uint4((uint32_t)p01, (uint32_t)(p01 >> 32), (uint32_t)p23,
+                           (uint32_t)(p23 >> 32));
+        } else {
+          const uint2 w = *reinterpret_cast<const uint2*>(
+              reinterpret_cast<const uint16_t*>(kvb) + (size_t)(t0 + t) * hd + d);
+          out = make_uint4(w.x << 16, w.x & 0xFFFF0000u, w.y << 16, w.y & 0xFFFF0000u);
+        }
+        *reinterpret_cast<uint4*>(dst + (size_t)t * hd + d) = out;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rfull[slot]);
+    }
+  } else if (tid < hd) {
+    // out_t = fma(e_t, v_t, out_{t-1} * f_t); with f_t == 1 the multiply is
+    // the identity and runs of eight such steps skip it
     const int d = tid;
     float o = 0.0f;
-    // one group of 8 tokens: raw exps, dequantised values, all-ones flag;
-    // the next group is loaded before the current one's FMA chain runs
-    auto load = [&](int i, float* r, float* vv, int& fl) {
-      const float4 r0 = *reinterpret_cast<const float4*>(sc + i);
-      const float4 r1 = *reinterpret_cast<const float4*>(sc + i + 4);
-      r[0] = r0.x; r[1] = r0.y; r[2] = r0.z; r[3] = r0.w;
-      r[4] = r1.x; r[5] = r1.y; r[6] = r1.z; r[7] = r1.w;
-      if constexpr (PAGED) {
-        const float4 s0 = *reinterpret_cast<const float4*>(tvs + i);
-        const float4 s1 = *reinterpret_cast<const float4*>(tvs + i + 4);
-        const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    for (int c = 0; c < nchunk; c++) {
+      const int slot = c % kRing;
+      if (ok) ok = mbar_wait(&rfull[slot], (c / kRing) & 1, sb.err);
+      const float* src = ring + (size_t)slot * kRingTok * hd + d;
+      const int t0 = c * kRingTok;
+      const int nt = min(kRingTok, T - t0);
+      if (ok && nt == kRingTok) {
 #pragma unroll
-        for (int u = 0; u < 8; u++) vv[u] = __fmul_rn(s8_to_f32(kvb[(size_t)(i + u) * hd + d]), sv[u]);
-      } else {
+        for (int g = 0; g < kRingTok / 8; g++) {
+          const int i = t0 + 8 * g;
+          float vv[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++)
-          vv[u] = bf16_to_f32(reinterpret_cast<const uint16_t*>(kvb)[(size_t)(i + u) * hd + d]);
-      }
-      fl = ones[i >> 3];
-    };
-    int i = 0;
-    if (T >= 8) {
-      float rn[8], vn[8];
-      int fn;
-      load(0, rn, vn, fn);
-      for (; i + 8 <= T; i += 8) {
-        float r[8], vv[8];
+          for (int u = 0; u < 8; u++) vv[u] = src[(8 * g + u) * hd];
+          const float4 r0 = *reinterpret_cast<const float4*>(sc + i);
+          const float4 r1 = *reinterpret_cast<const float4*>(sc + i + 4);
+          const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+          if (ones[i >> 3]) {
 #pragma unroll
-        for (int u = 0; u < 8; u++) {
-          r[u] = rn[u];
-          vv[u] = vn[u];
+            for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], o);
+          } else {
+            const float4 f0 = *reinterpret_cast<const float4*>(sf + i);
+            const float4 f1 = *reinterpret_cast<const float4*>(sf + i + 4);
+            const float f[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+#pragma unroll
+            for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], __fmul_rn(o, f[u]));
+          }
         }
-        const int fl = fn;
-        if (i + 16 <= T) load(i + 8, rn, vn, fn);
-        if (fl) {
-#pragma unroll
-          for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], o);
-        } else {
-          const float4 f0 = *reinterpret_cast<const float4*>(sf + i);
-          const float4 f1 = *reinterpret_cast<const float4*>(sf + i + 4);
-          const float f[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-#pragma unroll
-          for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], __fmul_rn(o, f[u]));
-        }
+      } else if (ok) {
+        for (int t = 0; t < nt; t++)
+          o = __fmaf_rn(sc[t0 + t], src[t * hd], __fmul_rn(o, sf[t0 + t]));
       }
-    }
-    for (; i < T; i++) {
-      float vv;
-      if constexpr (PAGED)
-        vv = __fmul_rn(s8_to_f32(kvb[(size_t)i * hd + d]), tvs[i]);
-      else
-        vv = bf16_to_f32(reinterpret_cast<const uint16_t*>(kvb)[(size_t)i * hd + d]);
-      o = __fmaf_rn(sc[i], vv, __fmul_rn(o, sf[i]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[slot]);
     }
     qs[d] = o;  // q no longer needed
     PHASE_MARK(mk && d == 0, 13);
@@ -995,7 +1060,7 @@ cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuf
   cudaError_t e = opt_in_max_smem(attention_kernel<true>);
   if (!e) e = opt_in_max_smem(attention_kernel<false>);
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;
-  const int ssel = cap_c * 8 + (sb.sparse_k + 2) * 8 + 256 * 4;
+  const int ssel = cap_c * 8 + 1024 * 8 + 256 * 4;
   if (!e && ssel <= 227 * 1024)
     e = cudaFuncSetAttribute(linear_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              ssel);
@@ -1037,7 +1102,7 @@ cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const Ste
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                                  int layer, int B, cudaStream_t s, bool pdl) {
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;
-  const size_t smem = (size_t)cap_c * 8 + (size_t)(sb.sparse_k + 2) * 8 + 256 * 4;
+  const size_t smem = (size_t)cap_c * 8 + 1024 * 8 + 256 * 4;
   return launch_ex(linear_select_kernel, dim3(B), dim3(256), smem, s, pdl, kv, lsh, sb, layer);
 }
 

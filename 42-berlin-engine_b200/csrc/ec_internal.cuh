@@ -147,6 +147,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
 // dst, src and bytes must be multiples of 16.
+// 16-byte asynchronous copy global -> shared through L2 (cp.async.cg).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed
+// (the arrival is not counted up front: init the barrier with the number of
+// arriving threads).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 16-byte read-only global load that skips L1.
+__device__ __forceinline__ uint4 ldg_nc16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(
@@ -162,6 +185,52 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ------------------------------------------------ paired f32 arithmetic --
+// add/mul/fma.rn.f32x2 (sm_100): two independent IEEE operations, the same
+// rounding as the scalar forms.
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ void fma2(uint64_t& acc, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// Four weight bytes -> two float pairs (elements 0,1 and 2,3), exact.
+template <int WK>
+__device__ __forceinline__ void decode_pairs(uint32_t w, uint64_t& p01, uint64_t& p23) {
+  if constexpr (WK == EC_W_INT8) {
+    // 0x4B0000xx with xx = v ^ 0x80 is 2^23 + 128 + v
+    const uint32_t u = w ^ 0x80808080u;
+    const uint64_t bias = pack2(__float_as_uint(-8388736.0f), __float_as_uint(-8388736.0f));
+    p01 = add2(pack2(__byte_perm(u, 0x4B000000u, 0x7540), __byte_perm(u, 0x4B000000u, 0x7541)),
+               bias);
+    p23 = add2(pack2(__byte_perm(u, 0x4B000000u, 0x7542), __byte_perm(u, 0x4B000000u, 0x7543)),
+               bias);
+  } else {
+    // E4M3 with the reference's semantics (fp8_to_float, ops_quant.c:27-50):
+    // byte k moved to the top byte, an arithmetic shift by 4 leaves the sign
+    // in bit 31 and the 7 magnitude bits at 20..26; times 2^120 exactly
+    auto bits = [](uint32_t t) { return (uint32_t)(((int)t) >> 4) & 0x87F00000u; };
+    const uint64_t s120 = pack2(__float_as_uint(0x1p120f), __float_as_uint(0x1p120f));
+    p01 = mul2(pack2(bits(w << 24), bits(w << 16)), s120);
+    p23 = mul2(pack2(bits(w << 8), bits(w)), s120);
+  }
+}
 
 // RMSNorm of xs[0..K) in place (consumer threads only; `nc` of them).
 __device__ __forceinline__ void rmsnorm_smem(float* xs, const uint16_t* __restrict__ w, int K,

@@ -59,8 +59,10 @@ struct PackedPlan {
 
 int packed_kce(int K);
 size_t packed_bytes(int N, int K);
-// force_r: 0 = choose, 1 or 2 = rows per thread.
-bool packed_plan(int wkind, int N, int K, int n_sm, int force_r, PackedPlan* plan);
+// force_r: 0 = choose, 1 or 2 = rows per thread.  co_resident: at most
+// about half an SM (shared memory, threads), so the next kernel fits beside.
+bool packed_plan(int wkind, int N, int K, int n_sm, int force_r, bool co_resident,
+                 PackedPlan* plan);
 cudaError_t packed_prepare();
 cudaError_t packed_launch(int wkind, int pro, int epi, const PackedPlan& plan,
                           const GemvParams& p, cudaStream_t stream, bool pdl);

@@ -22,6 +22,8 @@
 // become floats with one byte permute each (2^23 + 128 + v, exact) and a
 // paired subtraction; products accumulate with paired FMAs (fma.rn.f32x2:
 // two independent fma.rn, the same rounding as the scalar form).
+#include <cstdlib>
+
 #include "ec_internal.cuh"
 #include "gemv.cuh"
 
@@ -31,49 +33,6 @@ namespace {
 
 constexpr int kMaxStages = 8;
 constexpr int kMaxWarps = 16;  // consumer warps
-
-__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
-  uint64_t d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
-  return d;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ void fma2(uint64_t& acc, uint64_t a, uint64_t b) {
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
-}
-__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float((uint32_t)v); }
-__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
-
-// Four weight bytes -> two float pairs (elements 0,1 and 2,3), exact.
-template <int WK>
-__device__ __forceinline__ void decode_pairs(uint32_t w, uint64_t& p01, uint64_t& p23) {
-  if constexpr (WK == EC_W_INT8) {
-    // 0x4B0000xx with xx = v ^ 0x80 is 2^23 + 128 + v
-    const uint32_t u = w ^ 0x80808080u;
-    const uint64_t bias = pack2(__float_as_uint(-8388736.0f), __float_as_uint(-8388736.0f));
-    p01 = add2(pack2(__byte_perm(u, 0x4B000000u, 0x7540), __byte_perm(u, 0x4B000000u, 0x7541)),
-               bias);
-    p23 = add2(pack2(__byte_perm(u, 0x4B000000u, 0x7542), __byte_perm(u, 0x4B000000u, 0x7543)),
-               bias);
-  } else {
-    // E4M3 with the reference's semantics (fp8_to_float, ops_quant.c:27-50):
-    // byte k moved to the top byte, an arithmetic shift by 4 leaves the sign
-    // in bit 31 and the 7 magnitude bits at 20..26; times 2^120 exactly
-    auto bits = [](uint32_t t) { return (uint32_t)(((int)t) >> 4) & 0x87F00000u; };
-    const uint64_t s120 = pack2(__float_as_uint(0x1p120f), __float_as_uint(0x1p120f));
-    p01 = mul2(pack2(bits(w << 24), bits(w << 16)), s120);
-    p23 = mul2(pack2(bits(w << 8), bits(w)), s120);
-  }
-}
 
 template <int WK, int PRO, int EPI, int R, int KCE>
 __global__ void __launch_bounds__(32 + 32 * kMaxWarps, 1) gemv_packed_kernel(GemvParams p) {
@@ -306,20 +265,30 @@ int packed_kce(int K) { return (K % 512 == 0) ? 512 : 32; }
 
 size_t packed_bytes(int N, int K) { return (size_t)((N + 3) / 4) * 4 * (size_t)K; }
 
-bool packed_plan(int wkind, int N, int K, int n_sm, int force_r, PackedPlan* plan) {
+bool packed_plan(int wkind, int N, int K, int n_sm, int force_r, bool co_resident,
+                 PackedPlan* plan) {
   if ((wkind != EC_W_INT8 && wkind != EC_W_FP8) || N <= 0 || K <= 0 || K % 32 != 0) return false;
   const int kce = packed_kce(K);
   const int nq = (N + 3) / 4;
   const int grid = nq < n_sm ? nq : n_sm;
   const int qpc = (nq + grid - 1) / grid;  // quads of the busiest CTA
-  int R = (qpc * 4 >= 256) ? 2 : 1;
+  // co_resident: leave room on every SM for the next kernel's CTA (shared
+  // memory, threads and registers), so that under programmatic dependent
+  // launch it starts streaming its own weights while this one drains
+  int R = (!co_resident && qpc * 4 >= 256) ? 2 : 1;
   if (force_r == 1 || force_r == 2) R = force_r;
-  // spread the CTA's quads evenly over the fewest groups of <= kMaxWarps*R
-  const int ngroups = (qpc + kMaxWarps * R - 1) / (kMaxWarps * R);
+  const int max_warps = co_resident ? kMaxWarps - 1 : kMaxWarps;
+  // spread the CTA's quads evenly over the fewest groups of <= max_warps*R
+  const int ngroups = (qpc + max_warps * R - 1) / (max_warps * R);
   const int qs = (qpc + ngroups - 1) / ngroups;
   int warps = (qs + R - 1) / R;
   const int fixed = (2 * kMaxStages + 2) * 8 + 16 * 4 + K * 4;
-  const int budget = 220 * 1024;
+  int budget = 220 * 1024;
+  if (co_resident) {
+    const char* v = getenv("EC_GEMV_SMEM_KB");
+    budget = (v ? atoi(v) : 110) * 1024;
+    if (budget < fixed + 2 * 4 * kce) budget = fixed + 2 * 4 * kce;
+  }
   int stages = 0;
   for (;;) {
     const int sb = warps * R * 4 * kce;

@@ -212,8 +212,8 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     return fail(EC_ERR_UNSUPPORTED, "sparse_blocks_k must be in 1..64 (select_top_k_blocks)");
   if (c.use_paged_kv && c.seq_len > 32768)
     return fail(EC_ERR_UNSUPPORTED, "paged KV supports seq_len <= 32768 (2048 blocks)");
-  if (!c.use_paged_kv && c.sparse_k <= 0)
-    return fail(EC_ERR_UNSUPPORTED, "linear KV mode needs sparse_k > 0");
+  if (!c.use_paged_kv && (c.sparse_k <= 0 || c.sparse_k > 511))
+    return fail(EC_ERR_UNSUPPORTED, "linear KV mode needs sparse_k in 1..511");
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
   ec_ctx* ctx = new ec_ctx();
@@ -356,11 +356,14 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   // GEMV plans
   const int wk = c.weight_kind;
   const int fr = gemv_force_r();
-  if (!ec::packed_plan(wk, (H + 2 * KV) * hd, D, ctx->n_sm, fr, &ctx->p_qkv) ||
-      !ec::packed_plan(wk, D, H * hd, ctx->n_sm, fr, &ctx->p_o) ||
-      !ec::packed_plan(wk, 2 * F, D, ctx->n_sm, fr, &ctx->p_w13) ||
-      !ec::packed_plan(wk, D, F, ctx->n_sm, fr, &ctx->p_w2) ||
-      !ec::packed_plan(wk, V, D, ctx->n_sm, fr, &ctx->p_lm)) {
+  // co-resident plans measured slower (the block scheduler may place two CTAs
+  // of one GEMV on an SM whose previous CTA has finished): opt-in only
+  const bool co = getenv("EC_GEMV_SMEM_KB") != nullptr;
+  if (!ec::packed_plan(wk, (H + 2 * KV) * hd, D, ctx->n_sm, fr, co, &ctx->p_qkv) ||
+      !ec::packed_plan(wk, D, H * hd, ctx->n_sm, fr, co, &ctx->p_o) ||
+      !ec::packed_plan(wk, 2 * F, D, ctx->n_sm, fr, co, &ctx->p_w13) ||
+      !ec::packed_plan(wk, D, F, ctx->n_sm, fr, co, &ctx->p_w2) ||
+      !ec::packed_plan(wk, V, D, ctx->n_sm, fr, false, &ctx->p_lm)) {
     ec_destroy(ctx);
     return fail(EC_ERR_UNSUPPORTED, "no GEMV plan for this shape");
   }
@@ -880,7 +883,7 @@ extern "C" int ec_op_gemv_packed(int wkind, const void* w, const float* scale, c
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   EC_CUDA_TRY(ec::packed_prepare());
   ec::PackedPlan plan;
-  if (!ec::packed_plan(wkind, m, k, nsm, gemv_force_r(), &plan))
+  if (!ec::packed_plan(wkind, m, k, nsm, gemv_force_r(), false, &plan))
     return fail(EC_ERR_UNSUPPORTED, "no GEMV plan for this shape");
   ec::GemvParams p{};
   p.w = static_cast<const uint8_t*>(w);
@@ -1012,7 +1015,9 @@ int paged_attention_check(const ec_paged_view* pv, const float* q, float* out, i
   const int nb = (n_tokens + 15) / 16;
   if (nb > 2048) return fail(EC_ERR_UNSUPPORTED, "at most 2048 blocks");
   const bool dense = !(sparse_blocks_k > 0 && nb > sparse_blocks_k);
-  if (dense && (long)((n_tokens + 15) & ~15) * pv->head_dim > 131072)
+  const int max_tok = dense ? ((n_tokens + 15) & ~15) : 16 * sparse_blocks_k;
+  if ((dense && (long)max_tok * pv->head_dim > 131072) ||
+      ec::attention_smem_bytes(max_tok, pv->head_dim, true) > 226 * 1024)
     return fail(EC_ERR_UNSUPPORTED, "dense attention over more than 131072 K bytes");
   return EC_OK;
 }
