@@ -14,6 +14,8 @@
 // the running max (a max-scan), both exponentials per token, and the
 // denominator chain in its own warp.
 #include <cfloat>
+#include <cooperative_groups.h>
+
 #include "attn.cuh"
 #include "ec_internal.cuh"
 
@@ -583,32 +585,33 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
 //   3. V rows land in the same buffer; threads 0..hd-1 run the output
 //      recurrence for one dimension each, the next warp the denominator.
 // ------------------------------------------------------------------------
-constexpr int kAttnThreads = 512;
-constexpr int kRingTok = 32;  // V tokens per ring chunk
-constexpr int kRing = 3;      // ring chunks
+constexpr int kAttnThreads = 256;
+constexpr int kSplit = 4;  // CTAs per (query head, sequence): one thread-block cluster
 
 struct AttnSmemLayout {
-  size_t kv, sc, sf, tks, tvs, lpos, boff, bphys, bfill, ksb, vsb, ring, total;
+  size_t sc, sf, tks, tvs, trow, boff, bphys, bfill, vraw, vf, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// One CTA of the cluster: all tokens' scores and factors, this CTA's quarter
+// of the head dimensions of V (raw and dequantised).
 __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int esize) {
   AttnSmemLayout L;
   const int nblk = max_tok / 16 + 4;  // selected blocks (partial last block included)
-  size_t o = 256 * 4;  // q head
-  L.kv = o;
-  o = align_up(o + (size_t)max_tok * hd * esize, 16);
+  const size_t arr = (size_t)(max_tok + 8) * 4;
+  const int dq = hd / kSplit;
+  size_t o = 128 * 4;  // q head
   L.sc = o;
-  o += (size_t)(max_tok + 8) * 4;
+  o += arr;
   L.sf = o;
-  o += (size_t)(max_tok + 8) * 4;
+  o += arr;
   L.tks = o;
-  o += (size_t)(max_tok + 8) * 4;
+  o += arr;
   L.tvs = o;
-  o += (size_t)(max_tok + 8) * 4;
-  L.lpos = o;
-  o += (size_t)(max_tok + 8) * 4;
+  o += arr;
+  L.trow = o;
+  o += arr;
   L.boff = o;
   o += nblk * 4;
   L.bphys = o;
@@ -616,9 +619,10 @@ __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int e
   L.bfill = o;
   o += nblk * 4;
   o = align_up(o, 16);
-  L.ksb = L.vsb = o;  // unused
-  L.ring = o;
-  o += (size_t)kRing * kRingTok * hd * 4;
+  L.vraw = o;
+  o = align_up(o + (size_t)max_tok * dq * esize, 16);
+  L.vf = o;  // transposed: [dq][max_tok + 4] floats
+  o += (size_t)(max_tok + 4) * dq * 4;
   L.total = o;
   return L;
 }
@@ -628,71 +632,73 @@ __device__ __forceinline__ float s8_to_f32(uint32_t byte) {
   return __fsub_rn(__uint_as_float(byte ^ 0x4B000080u), 8388736.0f);
 }
 
-// Attention for one (query head, sequence): op_paged_attention(_sparse)
-// (ops_attention.c:292-461) over the selected paged blocks in selection
-// order, or attention_head_sparse (ops_attention.c:131-170) over linear-mode
-// positions.  Phases:
-//   1. the selected K rows (and per-token scales) land in shared memory by
-//      bulk copies; block offsets come from a warp prefix sum;
-//   2. scores s_t = dot(q, k_t) * (1/sqrt(hd)) in the reference's 8-lane
-//      order (paired f32x2 arithmetic, same roundings);
-//   3. the running max m_t = max(m_{t-1}, s_t) by a block-wide max-scan, then
-//      both exponentials of every token in parallel (fast_expf);
-//   4. V rows land in the same buffer; spare warps dequantise them into a
-//      ring of float chunks; threads 0..hd-1 run the output recurrence
-//      o_t = fma(e_t, v_t, o_{t-1} * f_t) for one dimension each (the multiply
-//      skipped over runs where every f_t is 1), one more warp the
-//      denominator; out = o / sum.
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+
+// Attention for one (query head, sequence) by a cluster of kSplit CTAs:
+// op_paged_attention(_sparse) (ops_attention.c:292-461) over the selected
+// paged blocks in selection order, or attention_head_sparse
+// (ops_attention.c:131-170) over linear-mode positions.
+//   1. every CTA builds the token table (block offsets by a warp prefix sum)
+//      and starts 16-byte asynchronous copies of ITS quarter of every V row;
+//   2. CTA r scores tokens [r*T/4, (r+1)*T/4): K rows straight from global
+//      memory, dot in the reference's 8-lane order (paired f32x2, same
+//      roundings), times 1/sqrt(hd); each score is stored into all four
+//      CTAs' shared memory (distributed shared memory), then a cluster
+//      barrier;
+//   3. every CTA: running max m_t = max(m_{t-1}, s_t) by a block max-scan,
+//      both exponentials per token (fast_expf), its V quarter dequantised;
+//   4. one warp runs the output recurrence o_t = fma(e_t, v_t, o_{t-1} * f_t)
+//      for the CTA's hd/4 dimensions (the multiply skipped over runs where
+//      every f_t is 1), one thread the denominator; out = o * (1/sum).
+// Spreading a head over four SMs quarters the bytes each SM must pull.
 template <bool PAGED>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, StepBuffers sb,
                                                                  int layer, int max_tok) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
   extern __shared__ __align__(128) uint8_t smem[];
   constexpr int ES = PAGED ? 1 : 2;
-  const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r = (int)cl.block_rank();
+  const int h = blockIdx.x / kSplit, b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim;
   const int kvh = h / (H / KV);
+  const int dq = hd / kSplit;  // this CTA's dimensions: [r*dq, (r+1)*dq)
   const AttnSmemLayout Ly = attn_layout(max_tok, hd, ES);
   float* qs = reinterpret_cast<float*>(smem);
-  uint8_t* kvb = smem + Ly.kv;
   float* sc = reinterpret_cast<float*>(smem + Ly.sc);
   float* sf = reinterpret_cast<float*>(smem + Ly.sf);
   float* tks = reinterpret_cast<float*>(smem + Ly.tks);
   float* tvs = reinterpret_cast<float*>(smem + Ly.tvs);
-  int* lpos = reinterpret_cast<int*>(smem + Ly.lpos);
+  int* trow = reinterpret_cast<int*>(smem + Ly.trow);  // paged: K/V row; linear: position
   int* boff = reinterpret_cast<int*>(smem + Ly.boff);
   int* bphys = reinterpret_cast<int*>(smem + Ly.bphys);
   int* bfill = reinterpret_cast<int*>(smem + Ly.bfill);
-  float* ring = reinterpret_cast<float*>(smem + Ly.ring);
-  __shared__ __align__(8) uint64_t bar[2];
-  __shared__ __align__(8) uint64_t rfull[kRing], rempty[kRing];
+  uint8_t* vraw = smem + Ly.vraw;
+  float* vf = reinterpret_cast<float*>(smem + Ly.vf);
+  __shared__ __align__(8) uint64_t vbar;
   __shared__ int s_ntok, s_nsel;
   __shared__ float s_wmax[kAttnThreads / 32];
   __shared__ float s_sum;
-  const int cw = (hd + 31) >> 5;                   // chain warps
-  const int npw = kAttnThreads / 32 - cw - 1;      // ring producer warps
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], kAttnThreads);  // one cp.async arrival per thread
-    for (int k = 0; k < kRing; k++) {
-      mbar_init(&rfull[k], npw);
-      mbar_init(&rempty[k], cw);
-    }
+    mbar_init(&vbar, kAttnThreads);  // one cp.async arrival per thread
     fence_mbar_init();
   }
   pdl_launch_dependents();
   pdl_wait();
-  const bool mk = (h == 0 && b == 0 && layer == 1);
+  const bool mk = (h == 0 && r == 0 && b == 0 && layer == 1);
   (void)mk;
   PHASE_MARK(mk && tid == 0, 8);
   const int pos = step_pos(sb, b);
   const float* qg = sb.qrot + (long)b * H * hd;
   for (int d = tid; d < hd; d += blockDim.x) qs[d] = qg[h * hd + d];
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  bool ok = true;
+  const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;  // linear mode
 
   // ------------------------------------------ selected blocks / positions
-  int* trow = lpos;  // paged: K/V row of token i, (block * KV + kvh) * 16 + t
-  const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;  // linear mode
   if constexpr (PAGED) {
     const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
     const int nb = (n_tok + kBlk - 1) / kBlk;
@@ -726,7 +732,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
         s_ntok = carry;
         s_nsel = nsel;
       }
-      PHASE_MARK(mk && lane == 0, 15);
     }
     __syncthreads();
     const int nsl = s_nsel;
@@ -746,76 +751,89 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
     const int* sel = sb.sel + (long)b * sb.max_sel;
     const bool sparse = ns > 0 && ns < kv_len;
     const int T = sparse ? ns : kv_len;
-    for (int i = tid; i < T; i += blockDim.x) lpos[i] = sparse ? sel[i] : i;
+    for (int i = tid; i < T; i += blockDim.x) trow[i] = sparse ? sel[i] : i;
     if (tid == 0) s_ntok = T;
   }
   __syncthreads();
   const int T = s_ntok;
-  // V rows -> shared memory by 16-byte asynchronous copies from every thread,
-  // completing on bar[1] (counted per thread); they land while scores run
+  // this CTA's quarter of every V row -> shared memory, completing on vbar
   {
-    const int rowb = hd * ES;
-    const int lgp = 31 - __clz(rowb >> 4);  // 16-byte pieces per row (power of 2)
-    for (int e = tid; e < (T << lgp); e += blockDim.x) {
-      const int i = e >> lgp, pc = e & ((1 << lgp) - 1);
-      const uint8_t* src;
+    const int slice = dq * ES;  // bytes: 8, 16, 32 or 64
+    const int np = slice >= 16 ? slice >> 4 : 1;
+    for (int e = tid; e < T * np; e += blockDim.x) {
+      const int i = e / np, pc = e - i * np;
+      const uint8_t* row;
       if constexpr (PAGED)
-        src = reinterpret_cast<const uint8_t*>(kv.vq) + (size_t)trow[i] * hd + pc * 16;
+        row = reinterpret_cast<const uint8_t*>(kv.vq) + (size_t)trow[i] * hd;
       else
-        src = reinterpret_cast<const uint8_t*>(kv.lv + ((lrow + lpos[i]) * KV + kvh) * hd) + pc * 16;
-      cp_async16(kvb + (size_t)i * rowb + pc * 16, src);
+        row = reinterpret_cast<const uint8_t*>(kv.lv + ((lrow + trow[i]) * KV + kvh) * hd);
+      const uint8_t* src = row + r * slice + pc * 16;
+      uint8_t* dst = vraw + (size_t)i * slice + pc * 16;
+      if (slice >= 16)
+        cp_async16(dst, src);
+      else
+        cp_async8(dst, src);
     }
-    cp_async_arrive(&bar[1]);
+    cp_async_arrive(&vbar);
   }
   PHASE_MARK(mk && tid == 0, 9);
 
-  // ------------------------------------------------------------- scores
-  // K rows straight from global memory (16-byte read-only loads)
-  for (int i = tid; i < T; i += blockDim.x) {
-    float s;
-    if constexpr (PAGED) {
-      // piece c of this token's row sits at (c + t) mod np (stored rotated);
-      // acc[l & 7] += q[16c + l] * (k[16c + l] * scale_t), l = 0..15
-      const int row = trow[i];
-      const uint8_t* kr = reinterpret_cast<const uint8_t*>(kv.kq) + (size_t)row * hd;
-      const int t = row & (kBlk - 1);
-      const float ksc = tks[i];
-      const uint64_t ks2 = pack2(__float_as_uint(ksc), __float_as_uint(ksc));
-      const int np = hd >> 4;
-      uint4 u[8];
+  // ------------------------------------------- scores of this CTA's quarter
+  {
+    const int tq = (T + kSplit - 1) / kSplit;
+    const int i0 = r * tq, i1 = min(T, i0 + tq);
+    float* peer[kSplit];
 #pragma unroll
-      for (int c = 0; c < 8; c++)
-        if (c < np) u[c] = ldg_nc16(kr + (((c + t) & (np - 1)) << 4));
-      uint64_t acc[4] = {0, 0, 0, 0};
+    for (int k = 0; k < kSplit; k++) peer[k] = cl.map_shared_rank(sc, k);
+    for (int i = i0 + tid; i < i1; i += blockDim.x) {
+      float s;
+      if constexpr (PAGED) {
+        // piece c of this token's row sits at (c + t) mod np (stored rotated);
+        // acc[l & 7] += q[16c + l] * (k[16c + l] * scale_t), l = 0..15
+        const int row = trow[i];
+        const uint8_t* kr = reinterpret_cast<const uint8_t*>(kv.kq) + (size_t)row * hd;
+        const int t = row & (kBlk - 1);
+        const float ksc = tks[i];
+        const uint64_t ks2 = pack2(__float_as_uint(ksc), __float_as_uint(ksc));
+        const int npc = hd >> 4;
+        uint4 u[8];
 #pragma unroll
-      for (int c = 0; c < 8; c++) {
-        if (c >= np) break;
-        const ulonglong2* q2 = reinterpret_cast<const ulonglong2*>(qs + 16 * c);
-        const uint32_t wv[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
+        for (int c = 0; c < 8; c++)
+          if (c < npc) u[c] = ldg_nc16(kr + (((c + t) & (npc - 1)) << 4));
+        uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int g = 0; g < 4; g++) {
-          uint64_t w01, w23;
-          decode_pairs<EC_W_INT8>(wv[g], w01, w23);
-          const ulonglong2 qq = q2[g];
-          // elements 4g..4g+3 -> accumulator pairs (2g)&3 and (2g+1)&3
-          fma2(acc[(2 * g) & 3], mul2(w01, ks2), qq.x);
-          fma2(acc[(2 * g + 1) & 3], mul2(w23, ks2), qq.y);
+        for (int c = 0; c < 8; c++) {
+          if (c >= npc) break;
+          const ulonglong2* q2 = reinterpret_cast<const ulonglong2*>(qs + 16 * c);
+          const uint32_t wv[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
+#pragma unroll
+          for (int g = 0; g < 4; g++) {
+            uint64_t w01, w23;
+            decode_pairs<EC_W_INT8>(wv[g], w01, w23);
+            const ulonglong2 qq = q2[g];
+            // elements 4g..4g+3 -> accumulator pairs (2g)&3 and (2g+1)&3
+            fma2(acc[(2 * g) & 3], mul2(w01, ks2), qq.x);
+            fma2(acc[(2 * g + 1) & 3], mul2(w23, ks2), qq.y);
+          }
         }
-      }
-      float a8[8];
+        float a8[8];
 #pragma unroll
-      for (int l = 0; l < 4; l++) {
-        a8[2 * l] = lo_f(acc[l]);
-        a8[2 * l + 1] = hi_f(acc[l]);
+        for (int l = 0; l < 4; l++) {
+          a8[2 * l] = lo_f(acc[l]);
+          a8[2 * l + 1] = hi_f(acc[l]);
+        }
+        s = hsum8(a8);
+      } else {
+        s = dot_bf16_ref(kv.lk + ((lrow + trow[i]) * KV + kvh) * hd, qs, hd);
       }
-      s = hsum8(a8);
-    } else {
-      s = dot_bf16_ref(kv.lk + ((lrow + lpos[i]) * KV + kvh) * hd, qs, hd);
+      s = __fmul_rn(s, scale);
+#pragma unroll
+      for (int k = 0; k < kSplit; k++) peer[k][i] = s;
     }
-    sc[i] = __fmul_rn(s, scale);
   }
-  __syncthreads();
+  cl.sync();  // every CTA holds all T scores
   PHASE_MARK(mk && tid == 0, 10);
+
   // running max m_t = max(m_{t-1}, s_t) (exact), then the two exponentials
   {
     const int per = (T + blockDim.x - 1) / blockDim.x;
@@ -856,125 +874,128 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
       sc[i] = fast_expf(__fsub_rn(s, run));  // raw_exp
     }
   }
+  // V quarter: v * scale_t, exact, four elements at a time
+  bool ok = mbar_wait(&vbar, 0, sb.err);
+  // thread -> (token i, dimensions 4g..4g+3) with i fastest, so a warp's
+  // transposed stores fall in 32 consecutive words
+  const int ng = dq >> 2;
+  for (int w = tid; w < T * ng && ok; w += blockDim.x) {
+    const int g = w / T, i = w - g * T, d = 4 * g;
+    uint4 out;
+    if constexpr (PAGED) {
+      const uint32_t wv = *reinterpret_cast<const uint32_t*>(vraw + (size_t)i * dq + d);
+      const float ts = tvs[i];
+      const uint64_t s2 = pack2(__float_as_uint(ts), __float_as_uint(ts));
+      uint64_t p01, p23;
+      decode_pairs<EC_W_INT8>(wv, p01, p23);
+      p01 = mul2(p01, s2);
+      p23 = mul2(p23, s2);
+      out = make_uint4((uint32_t)p01, (uint32_t)(p01 >> 32), (uint32_t)p23, (uint32_t)(p23 >> 32));
+    } else {
+      const uint2 wv = *reinterpret_cast<const uint2*>(vraw + ((size_t)i * dq + d) * 2);
+      out = make_uint4(wv.x << 16, wv.x & 0xFFFF0000u, wv.y << 16, wv.y & 0xFFFF0000u);
+    }
+    const int ld = max_tok + 4;
+    vf[(size_t)d * ld + i] = __uint_as_float(out.x);
+    vf[(size_t)(d + 1) * ld + i] = __uint_as_float(out.y);
+    vf[(size_t)(d + 2) * ld + i] = __uint_as_float(out.z);
+    vf[(size_t)(d + 3) * ld + i] = __uint_as_float(out.w);
+  }
   __syncthreads();
-  // flag per 8 tokens: every scale factor is 1 (the running max did not move)
+  // flag per 32 tokens: every scale factor is 1 (the running max did not move)
   int* ones = reinterpret_cast<int*>(tks);  // K scales are no longer needed
-  for (int g = tid; g < (T + 7) >> 3; g += blockDim.x) {
+  for (int g = tid; g < (T + 31) >> 5; g += blockDim.x) {
     bool a1 = true;
-    for (int u = 0; u < 8 && 8 * g + u < T; u++) a1 = a1 && (sf[8 * g + u] == 1.0f);
+    for (int u = 0; u < 32 && 32 * g + u < T; u++) a1 = a1 && (sf[32 * g + u] == 1.0f);
     ones[g] = a1;
   }
   __syncthreads();
   PHASE_MARK(mk && tid == 0, 11);
 
   // -------------------------------------------------------- recurrences
-  const int nchunk = (T + kRingTok - 1) / kRingTok;
-  if (warp == cw) {
+  float o = 0.0f;
+  if (warp == 0) {
+    // out_t = fma(e_t, v_t, out_{t-1} * f_t) for dimension `lane` (lanes
+    // past dq shadow lane % dq and are discarded).  Chunks of 32 tokens live
+    // in registers: this lane's v of each token, and e, f of token base+lane
+    // (read back by shuffles); the next chunk loads while this one's chain
+    // runs.  With f_t == 1 the multiply is the identity: runs of eight such
+    // tokens skip it.
+    // out_t = fma(e_t, v_t, out_{t-1} * f_t) for dimension `lane` (lanes
+    // past dq shadow lane % dq and are discarded).  V is stored transposed,
+    // so a lane reads four tokens with one 16-byte load; e and f are
+    // broadcast loads.  A chunk of 32 tokens is loaded while the previous
+    // one's chain runs; with f_t == 1 the multiply is the identity and runs
+    // of four such tokens skip it.
+    ok = __all_sync(0xffffffffu, ok);
+    const float* row = vf + (size_t)(lane % dq) * (max_tok + 4);
+    float4 va[8], ea[8], vb[8], eb[8];
+    auto load = [&](float4* v, float4* e, int base) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        v[j] = *reinterpret_cast<const float4*>(row + base + 4 * j);
+        e[j] = *reinterpret_cast<const float4*>(sc + base + 4 * j);
+      }
+    };
+    auto run = [&](const float4* v, const float4* e, int base) {
+      if (ones[base >> 5]) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          o = __fmaf_rn(e[j].x, v[j].x, o);
+          o = __fmaf_rn(e[j].y, v[j].y, o);
+          o = __fmaf_rn(e[j].z, v[j].z, o);
+          o = __fmaf_rn(e[j].w, v[j].w, o);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float4 f = *reinterpret_cast<const float4*>(sf + base + 4 * j);
+          o = __fmaf_rn(e[j].x, v[j].x, __fmul_rn(o, f.x));
+          o = __fmaf_rn(e[j].y, v[j].y, __fmul_rn(o, f.y));
+          o = __fmaf_rn(e[j].z, v[j].z, __fmul_rn(o, f.z));
+          o = __fmaf_rn(e[j].w, v[j].w, __fmul_rn(o, f.w));
+        }
+      }
+    };
+    // two register buffers, one loading while the other runs
+    const int T32 = ok ? (T & ~31) : 0;
+    if (T32) load(va, ea, 0);
+    for (int base = 0; base < T32; base += 64) {
+      if (base + 32 < T32) load(vb, eb, base + 32);
+      run(va, ea, base);
+      if (base + 32 >= T32) break;
+      if (base + 64 < T32) load(va, ea, base + 64);
+      run(vb, eb, base + 32);
+    }
+    for (int i = T32; i < T && ok; i++) o = __fmaf_rn(sc[i], row[i], __fmul_rn(o, sf[i]));
+    PHASE_MARK(mk && lane == 0, 13);
+  } else if (warp == 1 && lane == 0) {
     // denominator: sum_t = fma(sum_{t-1}, f_t, e_t)
-    if (lane == 0) {
-      float sum = 0.0f;
-      int i = 0;
-      for (; i + 8 <= T; i += 8) {
-        const float4 f0 = *reinterpret_cast<const float4*>(sf + i);
-        const float4 f1 = *reinterpret_cast<const float4*>(sf + i + 4);
-        const float4 r0 = *reinterpret_cast<const float4*>(sc + i);
-        const float4 r1 = *reinterpret_cast<const float4*>(sc + i + 4);
-        sum = __fmaf_rn(sum, f0.x, r0.x);
-        sum = __fmaf_rn(sum, f0.y, r0.y);
-        sum = __fmaf_rn(sum, f0.z, r0.z);
-        sum = __fmaf_rn(sum, f0.w, r0.w);
-        sum = __fmaf_rn(sum, f1.x, r1.x);
-        sum = __fmaf_rn(sum, f1.y, r1.y);
-        sum = __fmaf_rn(sum, f1.z, r1.z);
-        sum = __fmaf_rn(sum, f1.w, r1.w);
-      }
-      for (; i < T; i++) sum = __fmaf_rn(sum, sf[i], sc[i]);
-      s_sum = sum;
+    float sum = 0.0f;
+    int i = 0;
+    for (; i + 8 <= T; i += 8) {
+      const float4 f0 = *reinterpret_cast<const float4*>(sf + i);
+      const float4 f1 = *reinterpret_cast<const float4*>(sf + i + 4);
+      const float4 r0 = *reinterpret_cast<const float4*>(sc + i);
+      const float4 r1 = *reinterpret_cast<const float4*>(sc + i + 4);
+      sum = __fmaf_rn(sum, f0.x, r0.x);
+      sum = __fmaf_rn(sum, f0.y, r0.y);
+      sum = __fmaf_rn(sum, f0.z, r0.z);
+      sum = __fmaf_rn(sum, f0.w, r0.w);
+      sum = __fmaf_rn(sum, f1.x, r1.x);
+      sum = __fmaf_rn(sum, f1.y, r1.y);
+      sum = __fmaf_rn(sum, f1.z, r1.z);
+      sum = __fmaf_rn(sum, f1.w, r1.w);
     }
-  } else if (warp > cw) {
-    // ring producers: chunk c of V rows -> floats ring[c % kRing][t][d]
-    const int pt = tid - (cw + 1) * 32, np = npw * 32;
-    if (ok) ok = mbar_wait(&bar[1], 0, sb.err);
-    for (int c = 0; c < nchunk; c++) {
-      const int slot = c % kRing;
-      if (c >= kRing && ok) ok = mbar_wait(&rempty[slot], ((c / kRing) - 1) & 1, sb.err);
-      float* dst = ring + (size_t)slot * kRingTok * hd;
-      const int t0 = c * kRingTok;
-      const int nt = min(kRingTok, T - t0);
-      // four consecutive elements of one token per step: v * scale_t, exact
-      const int lg = 31 - __clz(hd) - 2;  // hd / 4 groups per token
-      for (int e4 = pt; e4 < (nt * hd >> 2) && ok; e4 += np) {
-        const int t = e4 >> lg, d = (e4 & ((hd >> 2) - 1)) << 2;
-        uint4 out;
-        if constexpr (PAGED) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(kvb + (size_t)(t0 + t) * hd + d);
-          const float ts = tvs[t0 + t];
-          const uint64_t s2 = pack2(__float_as_uint(ts), __float_as_uint(ts));
-          uint64_t p01, p23;
-          decode_pairs<EC_W_INT8>(w, p01, p23);
-          p01 = mul2(p01, s2);
-          p23 = mul2(p23, s2);
-          out = make_uint4((uint32_t)p01, (uint32_t)(p01 >> 32), (uint32_t)p23,
-                           (uint32_t)(p23 >> 32));
-        } else {
-          const uint2 w = *reinterpret_cast<const uint2*>(
-              reinterpret_cast<const uint16_t*>(kvb) + (size_t)(t0 + t) * hd + d);
-          out = make_uint4(w.x << 16, w.x & 0xFFFF0000u, w.y << 16, w.y & 0xFFFF0000u);
-        }
-        *reinterpret_cast<uint4*>(dst + (size_t)t * hd + d) = out;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rfull[slot]);
-    }
-  } else if (tid < hd) {
-    // out_t = fma(e_t, v_t, out_{t-1} * f_t); with f_t == 1 the multiply is
-    // the identity and runs of eight such steps skip it
-    const int d = tid;
-    float o = 0.0f;
-    for (int c = 0; c < nchunk; c++) {
-      const int slot = c % kRing;
-      if (ok) ok = mbar_wait(&rfull[slot], (c / kRing) & 1, sb.err);
-      const float* src = ring + (size_t)slot * kRingTok * hd + d;
-      const int t0 = c * kRingTok;
-      const int nt = min(kRingTok, T - t0);
-      if (ok && nt == kRingTok) {
-#pragma unroll
-        for (int g = 0; g < kRingTok / 8; g++) {
-          const int i = t0 + 8 * g;
-          float vv[8];
-#pragma unroll
-          for (int u = 0; u < 8; u++) vv[u] = src[(8 * g + u) * hd];
-          const float4 r0 = *reinterpret_cast<const float4*>(sc + i);
-          const float4 r1 = *reinterpret_cast<const float4*>(sc + i + 4);
-          const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-          if (ones[i >> 3]) {
-#pragma unroll
-            for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], o);
-          } else {
-            const float4 f0 = *reinterpret_cast<const float4*>(sf + i);
-            const float4 f1 = *reinterpret_cast<const float4*>(sf + i + 4);
-            const float f[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-#pragma unroll
-            for (int u = 0; u < 8; u++) o = __fmaf_rn(r[u], vv[u], __fmul_rn(o, f[u]));
-          }
-        }
-      } else if (ok) {
-        for (int t = 0; t < nt; t++)
-          o = __fmaf_rn(sc[t0 + t], src[t * hd], __fmul_rn(o, sf[t0 + t]));
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rempty[slot]);
-    }
-    qs[d] = o;  // q no longer needed
-    PHASE_MARK(mk && d == 0, 13);
+    for (; i < T; i++) sum = __fmaf_rn(sum, sf[i], sc[i]);
+    s_sum = sum;
+    PHASE_MARK(mk, 14);
   }
-  PHASE_MARK(mk && warp == cw && lane == 0, 14);
   __syncthreads();
-  if (tid < hd) {
-    float o = qs[tid];
+  if (warp == 0 && lane < dq) {
     const float sum = s_sum;
     if (sum > 0.0f) o = __fmul_rn(o, __fdiv_rn(1.0f, sum));
-    sb.att[(long)b * H * hd + h * hd + tid] = o;
+    sb.att[(long)b * H * hd + h * hd + r * dq + lane] = o;
   }
 }
 
@@ -1002,6 +1023,27 @@ static cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaS
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// The attention kernel: grid (kSplit * heads, B) in clusters of kSplit CTAs.
+template <bool PAGED>
+static cudaError_t launch_attn(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
+                               int max_tok, size_t smem, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kSplit * kv.n_heads, B);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kSplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attention_kernel<PAGED>, kv, sb, layer, max_tok);
 }
 
 // paged_kv_append of one token into a one-layer view (k, v already rotated).
@@ -1089,8 +1131,7 @@ cudaError_t launch_attention_n(const KvLayout& kv, const StepBuffers& sb, int ma
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   cudaError_t e = opt_in_max_smem(attention_kernel<true>);
   if (e != cudaSuccess) return e;
-  return launch_ex(attention_kernel<true>, dim3(kv.n_heads, 1), dim3(kAttnThreads), smem, s, false,
-                   kv, sb, 0, max_tok);
+  return launch_attn<true>(kv, sb, 0, 1, max_tok, smem, s, false);
 }
 
 cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
@@ -1110,12 +1151,8 @@ cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int laye
                              cudaStream_t s, bool pdl) {
   const int max_tok = attn_max_tok(kv, sb);
   const size_t smem = attn_smem(kv, sb, max_tok);
-  if (kv.paged) {
-    return launch_ex(attention_kernel<true>, dim3(kv.n_heads, B), dim3(kAttnThreads), smem, s, pdl,
-                     kv, sb, layer, max_tok);
-  }
-  return launch_ex(attention_kernel<false>, dim3(kv.n_heads, B), dim3(kAttnThreads), smem, s, pdl,
-                   kv, sb, layer, max_tok);
+  if (kv.paged) return launch_attn<true>(kv, sb, layer, B, max_tok, smem, s, pdl);
+  return launch_attn<false>(kv, sb, layer, B, max_tok, smem, s, pdl);
 }
 
 }  // namespace ec
