@@ -511,6 +511,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
           __threadfence_block();
           return true;
         }
+        __nanosleep(32);
       }
       if (lane == 0) atomicCAS(sb.err, 0, EC_ERR_TIMEOUT);
       return false;

@@ -1,0 +1,43 @@
+// chain.cuh -- one layer's weight-streaming GEMVs as one persistent kernel.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "gemv.cuh"
+
+namespace ec {
+
+constexpr int kMaxChainPhases = 6;
+
+// One GEMV of the chain: y = W . prologue(x) with the given epilogue, W in
+// the packed layout of gemv_packed.cu with one fp32 scale per row.
+struct ChainPhase {
+  const uint8_t* w;
+  const float* scale;
+  const float* x;          // [K], complete when the previous phase is
+  const uint16_t* norm_w;  // PRO_RMSNORM: [K] bf16
+  float* y;
+  int N, K;
+  int pro, epi;
+  int silu_vec_limit;
+};
+
+struct ChainParams {
+  ChainPhase ph[kMaxChainPhases];
+  int nph;
+  int* ctr;  // [kMaxChainPhases + 1] zeroed counters, owned by this chain
+  int* err;
+  float eps;
+  int mark;    // record phase timestamps (builds with EC_PHASE_TIMING)
+  int kmax;    // set by chain_launch
+  int stages;  // set by chain_launch
+};
+
+// 512 or 32 when every phase has the same packed chunk width, else 0 (the
+// chain cannot run; launch the phases one by one).
+int chain_kce(const ChainParams& P);
+cudaError_t chain_prepare();
+// grid = the SM count (every CTA resident at once).
+cudaError_t chain_launch(int wkind, ChainParams P, int grid, cudaStream_t s, bool pdl);
+
+}  // namespace ec

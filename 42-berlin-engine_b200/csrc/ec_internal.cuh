@@ -126,17 +126,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000; "
+      "selp.u32 %0, 1, 0, p; }"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
 
-// Wait with an iteration limit (each try_wait already suspends for a
-// hardware-defined interval).  On timeout the error word is set and false is
-// returned; callers then skip their work and exit instead of hanging the GPU.
-constexpr uint32_t kWaitLimit = 1u << 22;
+// Wait with an iteration limit (each try_wait may suspend the thread for up
+// to 1 us until the phase completes, so the limit is about a second).  On
+// timeout the error word is set and false is returned; callers then skip
+// their work and exit instead of hanging the GPU.
+constexpr uint32_t kWaitLimit = 1u << 20;
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
   for (uint32_t i = 0; i < kWaitLimit; i++)
@@ -170,6 +172,12 @@ __device__ __forceinline__ uint4 ldg_nc16(const void* p) {
   return v;
 }
 
+// Prefetch [src, src + bytes) into L2 (no shared memory, no completion).
+// src and bytes multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(
@@ -185,6 +193,29 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Four INT8 weights (one 32-bit word, elements 0..3) times x (pairs 0,1 and
+// 2,3) accumulated into two f32x2 accumulators: each byte v becomes the exact
+// float 2^23 + 128 + v by one byte permute, the bias is subtracted in pairs,
+// then paired fma.rn -- four independent fma.rn chains.  bias2 holds
+// -(2^23 + 128) twice.
+__device__ __forceinline__ void fma4_i8(uint32_t w, uint64_t x01, uint64_t x23, uint64_t bias2,
+                                        uint64_t& acc01, uint64_t& acc23) {
+  asm("{\n\t.reg .b32 u, a, b, c, d;\n\t.reg .b64 p, q;\n\t"
+      "xor.b32 u, %4, 0x80808080;\n\t"
+      "prmt.b32 a, u, 0x4B000000, 0x7540;\n\t"
+      "prmt.b32 b, u, 0x4B000000, 0x7541;\n\t"
+      "prmt.b32 c, u, 0x4B000000, 0x7542;\n\t"
+      "prmt.b32 d, u, 0x4B000000, 0x7543;\n\t"
+      "mov.b64 p, {a, b};\n\t"
+      "mov.b64 q, {c, d};\n\t"
+      "add.rn.f32x2 p, p, %5;\n\t"
+      "add.rn.f32x2 q, q, %5;\n\t"
+      "fma.rn.f32x2 %0, p, %2, %0;\n\t"
+      "fma.rn.f32x2 %1, q, %3, %1;\n\t}"
+      : "+l"(acc01), "+l"(acc23)
+      : "l"(x01), "l"(x23), "r"(w), "l"(bias2));
+}
 
 // ------------------------------------------------ paired f32 arithmetic --
 // add/mul/fma.rn.f32x2 (sm_100): two independent IEEE operations, the same

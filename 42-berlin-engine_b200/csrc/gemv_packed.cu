@@ -31,6 +31,8 @@ namespace ec {
 
 namespace {
 
+// -(2^23 + 128), twice: the INT8 decode bias
+constexpr uint64_t kBias2 = 0xCB000080CB000080ull;
 constexpr int kMaxStages = 8;
 constexpr int kMaxWarps = 16;  // consumer warps
 
@@ -128,10 +130,14 @@ __global__ void __launch_bounds__(32 + 32 * kMaxWarps, 1) gemv_packed_kernel(Gem
             if (i > 0 && !live[1]) break;
             const uint32_t wv = *reinterpret_cast<const uint32_t*>(
                 base + (size_t)(wc * R + i) * 4 * KCE + pc * 128);
-            uint64_t w01, w23;
-            decode_pairs<WK>(wv, w01, w23);
-            fma2(acc01[i], w01, xv.x);
-            fma2(acc23[i], w23, xv.y);
+            if constexpr (WK == EC_W_INT8) {
+              fma4_i8(wv, xv.x, xv.y, kBias2, acc01[i], acc23[i]);
+            } else {
+              uint64_t w01, w23;
+              decode_pairs<WK>(wv, w01, w23);
+              fma2(acc01[i], w01, xv.x);
+              fma2(acc23[i], w23, xv.y);
+            }
           }
         }
       }

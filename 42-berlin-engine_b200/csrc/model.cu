@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "attn.cuh"
+#include "chain.cuh"
 #include "ec_internal.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
@@ -53,6 +54,8 @@ struct ec_ctx {
         *logits = nullptr;
   int *argmax = nullptr, *tokens = nullptr, *pos = nullptr, *sel = nullptr, *nsel = nullptr;
   int* err = nullptr;
+  int* chain_ctr = nullptr;  // [layers][kMaxChainPhases + 1]
+  bool chain = false;        // one persistent GEMV kernel per layer
   float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
   int max_sel = 0;
   ec::PackedPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_lm{};
@@ -276,6 +279,8 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   TRY(dalloc(ctx, &ctx->nsel, (size_t)S));
   TRY(dalloc(ctx, &ctx->err, 1));
   TRY(cudaMemset(ctx->err, 0, sizeof(int)));
+  TRY(dalloc(ctx, &ctx->chain_ctr, (size_t)L * (ec::kMaxChainPhases + 1)));
+  TRY(cudaMemset(ctx->chain_ctr, 0, (size_t)L * (ec::kMaxChainPhases + 1) * sizeof(int)));
   // KV
   ec::KvLayout& kv = ctx->kv;
   kv.n_layers = L;
@@ -356,6 +361,15 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   // GEMV plans
   const int wk = c.weight_kind;
   const int fr = gemv_force_r();
+  {
+    // the chain needs one packed chunk width for all of a layer's matrices
+    ec::ChainParams P{};
+    const int ks[5] = {H * hd, D, F, D, D};
+    for (int i = 0; i < 5; i++) P.ph[i].K = ks[i];
+    P.nph = 5;
+    const char* nc = getenv("EC_NO_CHAIN");
+    ctx->chain = ec::chain_kce(P) != 0 && !(nc && atoi(nc));
+  }
   // co-resident plans measured slower (the block scheduler may place two CTAs
   // of one GEMV on an SM whose previous CTA has finished): opt-in only
   const bool co = getenv("EC_GEMV_SMEM_KB") != nullptr;
@@ -374,6 +388,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     sb.sparse_blocks_k = c.sparse_blocks_k;
     TRY(ec::gemv_prepare());
     TRY(ec::packed_prepare());
+    TRY(ec::chain_prepare());
     TRY(ec::attn_prepare(ctx->kv, ctx->lsh, sb));
   }
 #undef TRY
@@ -509,14 +524,17 @@ extern "C" int ec_reset(ec_ctx* ctx, int seq) {
 
 namespace {
 
+double gemv_bytes(const Mat& m, int pro, int epi) {
+  return (double)m.rows * m.cols + 4.0 * m.rows + 4.0 * m.cols +
+         (pro == ec::PRO_RMSNORM ? 2.0 * m.cols : 0.0) +
+         (epi == ec::EPI_SWIGLU ? 2.0 * m.rows : 4.0 * m.rows) +
+         (epi == ec::EPI_RESID ? 4.0 * m.rows : 0.0);
+}
+
 cudaError_t gemv(ec_ctx* ctx, int kind, const Mat& m, const ec::PackedPlan& plan, int pro,
                  int epi, const float* x, const uint16_t* nw, float* y) {
   // algorithmic bytes: weights + row scales + x (+ norm weight) + y (+ y read)
-  const double by = (double)m.rows * m.cols + 4.0 * m.rows + 4.0 * m.cols +
-                    (pro == ec::PRO_RMSNORM ? 2.0 * m.cols : 0.0) +
-                    (epi == ec::EPI_SWIGLU ? 2.0 * m.rows : 4.0 * m.rows) +
-                    (epi == ec::EPI_RESID ? 4.0 * m.rows : 0.0);
-  ProfScope ps(ctx, kind, by);
+  ProfScope ps(ctx, kind, gemv_bytes(m, pro, epi));
   ec::GemvParams p{};
   p.w = m.w;
   p.scale = m.scale;
@@ -531,6 +549,22 @@ cudaError_t gemv(ec_ctx* ctx, int kind, const Mat& m, const ec::PackedPlan& plan
   p.err = ctx->err;
   ctx->launches++;
   return ec::packed_launch(ctx->c.weight_kind, pro, epi, plan, p, ctx->stream, true);
+}
+
+ec::ChainPhase chain_phase(const Mat& m, int pro, int epi, const float* x, const uint16_t* nw,
+                           float* y) {
+  ec::ChainPhase ph{};
+  ph.w = m.w;
+  ph.scale = m.scale;
+  ph.x = x;
+  ph.norm_w = nw;
+  ph.y = y;
+  ph.N = m.rows;
+  ph.K = m.cols;
+  ph.pro = pro;
+  ph.epi = epi;
+  ph.silu_vec_limit = (m.rows / 2) & ~7;
+  return ph;
 }
 
 // Enqueue one decode step for B sequences (tokens/pos in device memory).
@@ -586,10 +620,16 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
         return e;
     }
     ctx->launches++;
+    const bool chain = ctx->chain;
+    float* lg = ctx->logits + (size_t)b * c.vocab_size;
+    float* hb = ctx->hbuf + (size_t)b * F;
     for (int l = 0; l < c.n_layers; l++) {
-      if ((e = gemv(ctx, EC_K_GEMV_QKV, ctx->qkv[l], ctx->p_qkv, ec::PRO_RMSNORM, ec::EPI_STORE, x,
-                    ctx->attn_norm[l], sb.qkv)))
-        return e;
+      // with the chain, layer l's QKV ran at the end of layer l-1's chain
+      if (!chain || l == 0) {
+        if ((e = gemv(ctx, EC_K_GEMV_QKV, ctx->qkv[l], ctx->p_qkv, ec::PRO_RMSNORM, ec::EPI_STORE, x,
+                      ctx->attn_norm[l], sb.qkv)))
+          return e;
+      }
       {
         ProfScope ps(ctx, EC_K_KV_APPEND, 4.0 * (H + 2 * KV) * hd * 2 + 2.0 * KV * hd);
         if ((e = ec::launch_kv_append(kv, lsh, sb, l, 1, ctx->stream, true))) return e;
@@ -605,18 +645,47 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
         if ((e = ec::launch_attention(kv, sb, l, 1, ctx->stream, true))) return e;
       }
       ctx->launches++;
+      if (chain) {
+        // o (+x), gate/up (RMSNorm, SwiGLU), down (+x), then the next layer's
+        // QKV or the LM head: one persistent kernel
+        ec::ChainParams P{};
+        P.ph[0] = chain_phase(ctx->wo[l], ec::PRO_NONE, ec::EPI_RESID, sb.att, nullptr, x);
+        P.ph[1] = chain_phase(ctx->w13[l], ec::PRO_RMSNORM, ec::EPI_SWIGLU, x, ctx->ffn_norm[l], hb);
+        P.ph[2] = chain_phase(ctx->w2[l], ec::PRO_NONE, ec::EPI_RESID, hb, nullptr, x);
+        if (l + 1 < c.n_layers)
+          P.ph[3] = chain_phase(ctx->qkv[l + 1], ec::PRO_RMSNORM, ec::EPI_STORE, x,
+                                ctx->attn_norm[l + 1], sb.qkv);
+        else
+          P.ph[3] = chain_phase(ctx->lm, ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->final_norm, lg);
+        P.nph = 4;
+        P.ctr = ctx->chain_ctr + (size_t)l * (ec::kMaxChainPhases + 1);
+        P.err = ctx->err;
+        P.eps = c.norm_eps;
+        P.mark = l == 1;
+        const double by = gemv_bytes(ctx->wo[l], ec::PRO_NONE, ec::EPI_RESID) +
+                          gemv_bytes(ctx->w13[l], ec::PRO_RMSNORM, ec::EPI_SWIGLU) +
+                          gemv_bytes(ctx->w2[l], ec::PRO_NONE, ec::EPI_RESID) +
+                          gemv_bytes(l + 1 < c.n_layers ? ctx->qkv[l + 1] : ctx->lm, ec::PRO_RMSNORM,
+                                     ec::EPI_STORE);
+        ProfScope ps(ctx, EC_K_GEMV_CHAIN, by);
+        if ((e = ec::chain_launch(c.weight_kind, P, ctx->n_sm, ctx->stream, true))) return e;
+        ctx->launches++;
+        continue;
+      }
       if ((e = gemv(ctx, EC_K_GEMV_O, ctx->wo[l], ctx->p_o, ec::PRO_NONE, ec::EPI_RESID, sb.att, nullptr, x)))
         return e;
       if ((e = gemv(ctx, EC_K_GEMV_GATEUP, ctx->w13[l], ctx->p_w13, ec::PRO_RMSNORM, ec::EPI_SWIGLU, x,
-                    ctx->ffn_norm[l], ctx->hbuf + (size_t)b * F)))
+                    ctx->ffn_norm[l], hb)))
         return e;
-      if ((e = gemv(ctx, EC_K_GEMV_DOWN, ctx->w2[l], ctx->p_w2, ec::PRO_NONE, ec::EPI_RESID,
-                    ctx->hbuf + (size_t)b * F, nullptr, x)))
+      if ((e = gemv(ctx, EC_K_GEMV_DOWN, ctx->w2[l], ctx->p_w2, ec::PRO_NONE, ec::EPI_RESID, hb,
+                    nullptr, x)))
         return e;
     }
-    float* lg = ctx->logits + (size_t)b * c.vocab_size;
-    if ((e = gemv(ctx, EC_K_GEMV_LM, ctx->lm, ctx->p_lm, ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->final_norm, lg)))
-      return e;
+    if (!chain) {
+      if ((e = gemv(ctx, EC_K_GEMV_LM, ctx->lm, ctx->p_lm, ec::PRO_RMSNORM, ec::EPI_STORE, x,
+                    ctx->final_norm, lg)))
+        return e;
+    }
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * c.vocab_size);
     if ((e = ec::launch_argmax(lg, c.vocab_size, 1, ctx->argmax + b,
                                feedback ? const_cast<int*>(tokens) + b : nullptr,
@@ -751,8 +820,12 @@ extern "C" int ec_profile_read(ec_ctx* ctx, int kind, double* ms, int* launches,
 
 extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
   if (!ctx) return 0;
-  const int per_layer = ctx->kv.paged ? 6 : 7;
-  return B * (1 + ctx->c.n_layers * per_layer + 2);
+  // embed, [QKV(0)], per layer: QKV, append, [select], attention, o, gate/up,
+  // down -- or with the chain: append, [select], attention, chain -- then
+  // [LM head] and argmax
+  const int sel = ctx->kv.paged ? 0 : 1;
+  if (ctx->chain) return B * (2 + ctx->c.n_layers * (3 + sel) + 1);
+  return B * (1 + ctx->c.n_layers * (6 + sel) + 2);
 }
 
 extern "C" int ec_read_state(ec_ctx* ctx, int which, int seq, float* out, size_t n) {

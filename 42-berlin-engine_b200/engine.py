@@ -33,7 +33,7 @@ EXPORTS = [
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
-           "attention", "embed", "argmax"]
+           "attention", "embed", "argmax", "gemv_chain"]
 
 
 class ModelConfig(C.Structure):

@@ -141,7 +141,8 @@ int		ec_synchronize(ec_ctx *ctx);
 # define EC_K_ATTENTION 7
 # define EC_K_EMBED 8
 # define EC_K_ARGMAX 9
-# define EC_K_COUNT 10
+# define EC_K_GEMV_CHAIN 10	/* one layer's o, gate/up, down (+ next QKV / LM head) */
+# define EC_K_COUNT 11
 int		ec_profile_enable(ec_ctx *ctx, int on);
 int		ec_profile_read(ec_ctx *ctx, int kind, double *ms, int *launches,
 			double *bytes);

@@ -324,3 +324,28 @@ def test_paged_ops_argument_errors(eng, torch):
                                    None, None, None) == eng.EC_ERR_ARG
     assert L.ec_op_paged_attention(C.byref(pv), x.data_ptr(), x.data_ptr(), 8, 16, 65,
                                    None, None, None) == eng.EC_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("chain", [True, False])
+def test_layer_chain_matches_oracle(eng, torch, oracle, synth, monkeypatch, chain):
+    """Every matrix width a multiple of 512: each layer's o, gate/up, down and
+    the next QKV (the LM head after the last layer) run as one persistent
+    kernel.  1100 tokens (past the block-sparse threshold) bit-identical to
+    the restatement, with the chain and with one launch per matrix."""
+    monkeypatch.setenv("EC_NO_CHAIN", "0" if chain else "1")
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=3, n_heads=8, n_kv_heads=4,
+                            vocab_size=4096, seq_len=2048, head_dim=64, rope_theta=1e4)
+    model = synth.make_model(cfg, seed=21)
+    e = eng.Engine(cfg)
+    e.load(model)
+    # embed + QKV(0) + 3 per layer + argmax with the chain, 6 per layer without
+    assert e.launches_per_step(1) == (3 + 3 * 3 if chain else 3 + 6 * 3)
+    pm = oracle.PortModel(model)
+    toks = synth.prompt(cfg, 1100, seed=5)
+    for pos in range(1100):
+        check = pos % 50 == 0 or pos >= 1090
+        lg, _ = e.step([toks[pos]], [pos], want_logits=check)
+        want = pm.forward(int(toks[pos]), pos)
+        if check:
+            assert np.array_equal(bits(lg[0]), bits(want)), f"step {pos}"
+    e.close()
