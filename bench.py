@@ -276,13 +276,20 @@ def run_cuda(args):
         cur_tok, cur_pos = int(am[0]), cur_pos + 1
     prof = e.profile_read()
     e.profile(False)
-    gemv = [k for k in prof if k.startswith("gemv")]
-    g_ms = sum(prof[k]["ms"] for k in gemv)
-    g_n = sum(prof[k]["launches"] for k in gemv)
-    g_by = sum(prof[k]["bytes"] for k in gemv)
+    # roofline of the dominant kernel: its algorithmic bytes per launch over its
+    # event-timed average launch duration
     tot_ms = sum(v["ms"] for v in prof.values())
+    dom = max(prof, key=lambda k: prof[k]["ms"])
+    d = prof[dom]
     peak, peak_kind = peaks()
-    achieved = (g_by / g_n) / (g_ms / g_n * 1e-3) / 1e9 if g_n else 0.0
+    achieved = (d["bytes"] / d["launches"]) / (d["ms"] / d["launches"] * 1e-3) / 1e9 \
+        if d["launches"] and d["bytes"] else 0.0
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(tpath):
+        tj = json.load(open(tpath))
+        if tj.get("kernel") == dom:
+            traffic = tj["traffic_bytes_per_launch"]
     weight_bytes = (sum(int(np.prod(s)) for s in S.mat_shapes(cfg).values()) * cfg.n_layers
                     + cfg.vocab_size * cfg.dim)
     kv_tok = cfg.n_layers * cfg.n_kv_heads * (cfg.head_dim * 2 + 8)
@@ -302,9 +309,12 @@ def run_cuda(args):
             "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B * (cfg.vocab_size + 1)},
             "gpu_launches": e.launches_per_step(B) * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "gemv (all weight-streaming launches)",
+            "roofline": {"bound": "hbm", "kernel": dom,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "traffic_source": "ncu dram bytes per launch, profiles/",
+                         "algorithmic_bytes_per_launch": round(d["bytes"] / d["launches"])
+                         if d["launches"] else None,
                          "peak_source": peak_kind,
                          "step_frac": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4),
                          "step_bytes": step_bytes},
