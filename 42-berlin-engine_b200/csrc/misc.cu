@@ -197,6 +197,132 @@ cudaError_t launch_embed(const uint16_t* emb, const int* tokens, float* x, int d
   return cudaLaunchKernelEx(&cfg, embed_kernel, emb, tokens, x, dim, vocab);
 }
 
+// argmax_simd_f32 split over kArgParts CTAs per row: CTA p reduces an
+// 8-aligned range to its 8 lane partials (first index of the lane maximum);
+// the last CTA to finish combines the ranges in order (strict >: on a tie the
+// earlier range, i.e. the smaller index of that lane, stays), then the lanes
+// in order (strict >), then the scalar tail -- the reference's result.
+constexpr int kArgParts = 32;
+
+__global__ void __launch_bounds__(256) argmax_split_kernel(const float* __restrict__ logits,
+                                                           int n, int* __restrict__ out,
+                                                           int* tokens, int* pos, float* pv,
+                                                           int* pi, int* ctr) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.y, p = blockIdx.x, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const float* x = logits + (long)b * n;
+  const int n8 = n & ~7;
+  const int per = ((n8 / kArgParts) + 7) & ~7;
+  const int lo = min(n8, p * per), hi = min(n8, lo + per);
+  __shared__ float s_v[8][8];
+  __shared__ int s_i[8][8];
+  __shared__ bool s_last;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = lo + tid; i < hi; i += blockDim.x) {  // blockDim % 8 == 0: lane tid % 8
+    const float v = x[i];
+    if (bi == 0x7fffffff || v > bv) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 8; o < 32; o <<= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane < 8) {
+    s_v[warp][lane] = bv;
+    s_i[warp][lane] = bi;
+  }
+  __syncthreads();
+  float* gv = pv + ((long)b * kArgParts + p) * 8;
+  int* gi = pi + ((long)b * kArgParts + p) * 8;
+  if (tid < 8) {
+    float v = s_v[0][tid];
+    int i = s_i[0][tid];
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) {
+      const float ov = s_v[w][tid];
+      const int oi = s_i[w][tid];
+      if (oi != 0x7fffffff && (i == 0x7fffffff || ov > v || (ov == v && oi < i))) {
+        v = ov;
+        i = oi;
+      }
+    }
+    gv[tid] = v;
+    gi[tid] = i;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(ctr + b, 1) == kArgParts - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if (tid < 8) {
+    const float* av = pv + (long)b * kArgParts * 8;
+    const int* ai = pi + (long)b * kArgParts * 8;
+    float v = -INFINITY;
+    int i = 0x7fffffff;
+    for (int q = 0; q < kArgParts; q++) {
+      const float ov = av[q * 8 + tid];
+      const int oi = ai[q * 8 + tid];
+      if (oi != 0x7fffffff && (i == 0x7fffffff || ov > v)) {
+        v = ov;
+        i = oi;
+      }
+    }
+    s_v[0][tid] = v;
+    s_i[0][tid] = i;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    ctr[b] = 0;
+    float best = s_v[0][0];
+    int idx = s_i[0][0];
+    for (int l = 1; l < 8; l++)
+      if (s_v[0][l] > best) {
+        best = s_v[0][l];
+        idx = s_i[0][l];
+      }
+    for (int i = n8; i < n; i++)
+      if (x[i] > best) {
+        best = x[i];
+        idx = i;
+      }
+    out[b] = idx;
+    if (tokens) tokens[b] = idx;
+    if (pos) pos[b] += 1;
+  }
+}
+
+size_t argmax_scratch_bytes(int B) { return (size_t)B * kArgParts * 8 * 8 + (size_t)B * 4; }
+
+cudaError_t launch_argmax_split(const float* logits, int n, int B, int* out, int* tokens,
+                                int* pos, void* scratch, cudaStream_t s, bool pdl) {
+  if (n < 8 * kArgParts) return launch_argmax(logits, n, B, out, tokens, pos, s, pdl);
+  float* pv = static_cast<float*>(scratch);
+  int* pi = reinterpret_cast<int*>(pv + (size_t)B * kArgParts * 8);
+  int* ctr = pi + (size_t)B * kArgParts * 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kArgParts, B);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, argmax_split_kernel, logits, n, out, tokens, pos, pv, pi, ctr);
+}
+
 cudaError_t launch_argmax(const float* logits, int n, int B, int* out, int* tokens, int* pos,
                           cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};

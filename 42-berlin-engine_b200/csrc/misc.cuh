@@ -6,6 +6,11 @@
 namespace ec {
 cudaError_t launch_embed(const uint16_t* emb, const int* tokens, float* x, int dim, int vocab, int B,
                          cudaStream_t s, bool pdl);
+// The decode step's argmax over kArgParts CTAs per row; scratch holds
+// argmax_scratch_bytes(B), its counters zero (they return to zero).
+size_t argmax_scratch_bytes(int B);
+cudaError_t launch_argmax_split(const float* logits, int n, int B, int* out, int* tokens,
+                                int* pos, void* scratch, cudaStream_t s, bool pdl);
 cudaError_t launch_argmax(const float* logits, int n, int B, int* out, int* tokens, int* pos,
                           cudaStream_t s, bool pdl);
 cudaError_t launch_rmsnorm(float* out, const float* x, const uint16_t* w, int n, float eps,

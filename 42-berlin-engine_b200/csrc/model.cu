@@ -55,6 +55,7 @@ struct ec_ctx {
   int *argmax = nullptr, *tokens = nullptr, *pos = nullptr, *sel = nullptr, *nsel = nullptr;
   int* err = nullptr;
   int* chain_ctr = nullptr;  // [layers][kMaxChainPhases + 1]
+  void* amax = nullptr;      // split-argmax partials and counters
   bool chain = false;        // one persistent GEMV kernel per layer
   float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
   int max_sel = 0;
@@ -279,6 +280,12 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   TRY(dalloc(ctx, &ctx->nsel, (size_t)S));
   TRY(dalloc(ctx, &ctx->err, 1));
   TRY(cudaMemset(ctx->err, 0, sizeof(int)));
+  {
+    uint8_t* am = nullptr;
+    TRY(dalloc(ctx, &am, ec::argmax_scratch_bytes(S)));
+    TRY(cudaMemset(am, 0, ec::argmax_scratch_bytes(S)));
+    ctx->amax = am;
+  }
   TRY(dalloc(ctx, &ctx->chain_ctr, (size_t)L * (ec::kMaxChainPhases + 1)));
   TRY(cudaMemset(ctx->chain_ctr, 0, (size_t)L * (ec::kMaxChainPhases + 1) * sizeof(int)));
   // KV
@@ -687,9 +694,13 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
         return e;
     }
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * c.vocab_size);
-    if ((e = ec::launch_argmax(lg, c.vocab_size, 1, ctx->argmax + b,
-                               feedback ? const_cast<int*>(tokens) + b : nullptr,
-                               feedback ? const_cast<int*>(pos) + b : nullptr, ctx->stream, true)))
+    // sequence b's partials and counter live at offset b of the scratch
+    if ((e = ec::launch_argmax_split(lg, c.vocab_size, 1, ctx->argmax + b,
+                                     feedback ? const_cast<int*>(tokens) + b : nullptr,
+                                     feedback ? const_cast<int*>(pos) + b : nullptr,
+                                     static_cast<uint8_t*>(ctx->amax) +
+                                         (size_t)b * (ec::argmax_scratch_bytes(1)),
+                                     ctx->stream, true)))
       return e;
     ctx->launches++;
   }
