@@ -253,6 +253,289 @@ __global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_kernel(ChainPa
   }
 }
 
+// ---------------------------------------------------------------------------
+// Batched chain: NB sequences (2..8) share one pass over the weights.  Each
+// ring slot carries one 512-column chunk of a group of row quads AND the same
+// chunk of every sequence's input vector; a weight word is decoded once and
+// accumulated into NB sets of lane accumulators, each in the reference's
+// order, so every sequence's result is bit-identical to its batch-1 result.
+// The producer issues weight copies as far ahead as the ring allows, across
+// phase boundaries; a slot's vector copies go out only once that phase's
+// input is complete (grid counter), so the weight stream never waits for
+// activations.  RMSNorm runs as its own phase (PRO_NORM_ROWS): CTA b stages
+// row b, runs the reference's 8-lane sum of squares and writes the
+// normalised row, which the next phase streams.
+template <int WK, int NB>
+__global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_nb_kernel(ChainParams P) {
+  constexpr int KCE = 512;
+  constexpr int kWB = kWarps * 4 * KCE;  // weight bytes per slot
+  constexpr int kXB = NB * KCE * 4;      // vector bytes per slot
+  constexpr int kSlot = kWB + kXB;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int S = P.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kStagesMax;
+  uint64_t* rbar = empty + kStagesMax;
+  float* red = reinterpret_cast<float*>(rbar + 2);  // 16 floats
+  float* rowbuf = reinterpret_cast<float*>(smem + 512);     // [kmax] (norm rows)
+  uint8_t* ring = smem + 512 + ((P.kmax * 4 + 127) & ~127);
+  __shared__ int s_go;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = gridDim.x;
+  if (tid == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    mbar_init(rbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    struct Cur {
+      int p = 0, g = 0, c = 0;
+      int sp_p = -1;  // phase whose split is cached
+      Split sp;
+    };
+    // first task at or after u (skipping phases without weights); false at end
+    auto settle = [&](Cur& u) -> bool {
+      while (u.p < P.nph) {
+        const ChainPhase& ph = P.ph[u.p];
+        if (ph.pro != PRO_NORM_ROWS) {
+          if (u.sp_p != u.p) {
+            u.sp = split_t<KCE>(ph, blockIdx.x, G);
+            u.sp_p = u.p;
+          }
+          if (u.g < u.sp.ngroups) return true;
+        }
+        u.p++;
+        u.g = u.c = 0;
+      }
+      return false;
+    };
+    auto advance = [&](Cur& u) {
+      if (++u.c == u.sp.nchunks) {
+        u.c = 0;
+        u.g++;
+      }
+    };
+    Cur cw, cx;  // next weight copy, next vector copy
+    int t = 0, tx = 0, ready = -1;
+    bool have_w = settle(cw), have_x = settle(cx);
+    uint32_t idle = 0;
+    while (have_x) {
+      // weights for task t when its slot is free
+      if (have_w) {
+        const int s = t % S;
+        if (t < S || mbar_test(&empty[s], ((t / S) - 1) & 1)) {
+          const ChainPhase& ph = P.ph[cw.p];
+          const Split& sp = cw.sp;
+          const int gq0 = sp.q0 + cw.g * sp.qs, gn = min(sp.qs, sp.q1 - gq0);
+          const uint32_t wb = (uint32_t)gn * 4 * KCE;
+          mbar_expect_tx(&full[s], wb + kXB);
+          bulk_g2s(ring + (size_t)s * kSlot, ph.w + ((long)cw.c * sp.nq + gq0) * 4 * KCE, wb,
+                   &full[s]);
+          t++;
+          advance(cw);
+          have_w = settle(cw);
+          idle = 0;
+          continue;
+        }
+      }
+      // vectors for task tx once its phase's input is complete
+      if (tx < t) {
+        if (cx.p > ready) {
+          if (cx.p == 0) {
+            pdl_wait();  // the previous kernel wrote phase 0's input
+          } else if (ld_acquire(P.ctr + cx.p - 1) < G) {
+            if (++idle > (kWaitLimit << 4)) {
+              atomicCAS(P.err, 0, EC_ERR_TIMEOUT);
+              return;
+            }
+            __nanosleep(64);
+            continue;
+          }
+          fence_proxy_async();
+          ready = cx.p;
+        }
+        const ChainPhase& ph = P.ph[cx.p];
+        const int s = tx % S;
+        uint8_t* xd = ring + (size_t)s * kSlot + kWB;
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+          bulk_g2s(xd + b * KCE * 4, ph.x + (long)b * ph.x_stride + (long)cx.c * KCE, KCE * 4,
+                   &full[s]);
+        tx++;
+        advance(cx);
+        have_x = settle(cx);
+        idle = 0;
+        continue;
+      }
+      if (++idle > (kWaitLimit << 4)) {
+        atomicCAS(P.err, 0, EC_ERR_TIMEOUT);
+        return;
+      }
+      __nanosleep(64);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int ct = tid - 32, wc = warp - 1, nc = kWarps * 32;
+  const int rq = lane >> 3, sl = lane & 7;
+  bool ok = true;
+  int t = 0, nrm = 0;  // nrm: norm phases so far (rbar's phase parity)
+  for (int p = 0; p < P.nph; p++) {
+    const ChainPhase& ph = P.ph[p];
+    if (ph.pro == PRO_NORM_ROWS) {
+      // wait for the input, then CTA b normalises row b
+      if (p == 0) pdl_wait();
+      if (ct == 0) {
+        bool got = p == 0;
+        for (uint32_t it = 0; it < kWaitLimit && ok && !got; it++) {
+          if (ld_acquire(P.ctr + p - 1) >= G) got = true;
+          else __nanosleep(64);
+        }
+        if (!got && ok) atomicCAS(P.err, 0, EC_ERR_TIMEOUT);
+        s_go = got && ok;
+        fence_proxy_async();
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(nc));
+      ok = ok && s_go;
+      const int b = blockIdx.x;
+      if (b < NB && ok) {
+        if (ct == 0) {
+          mbar_expect_tx(rbar, (uint32_t)(ph.K * 4));
+          bulk_g2s(rowbuf, ph.x + (long)b * ph.x_stride, (uint32_t)(ph.K * 4), rbar);
+        }
+        ok = mbar_wait(rbar, nrm & 1, P.err);
+        if (ok) rmsnorm_smem(rowbuf, ph.norm_w, ph.K, P.eps, red, ct, nc);
+        float* y = ph.y + (long)b * ph.y_stride;
+        for (int j = ct; j < ph.K && ok; j += nc) y[j] = rowbuf[j];
+      }
+      nrm++;
+    } else {
+      if (p == 0) pdl_wait();  // the epilogue may read what earlier kernels wrote
+      const Split sp = split_t<KCE>(ph, blockIdx.x, G);
+      for (int g = 0; g < sp.ngroups; g++) {
+        const int gq0 = sp.q0 + g * sp.qs, gn = min(sp.qs, sp.q1 - gq0);
+        uint64_t acc01[NB], acc23[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) acc01[b] = acc23[b] = 0;
+        for (int c = 0; c < sp.nchunks; c++, t++) {
+          const int s = t % S;
+          if (ok) ok = mbar_wait(&full[s], (t / S) & 1, P.err);
+          if (ok && wc < gn) {
+            const uint8_t* wbase = ring + (size_t)s * kSlot + (size_t)wc * 4 * KCE + rq * 32 + sl * 4;
+            const float* xsl = reinterpret_cast<const float*>(ring + (size_t)s * kSlot + kWB) + sl * 4;
+#pragma unroll 4
+            for (int pc = 0; pc < KCE / 32; pc++) {
+              const uint32_t wv = *reinterpret_cast<const uint32_t*>(wbase + pc * 128);
+              uint64_t w01, w23;
+              decode_pairs<WK>(wv, w01, w23);
+#pragma unroll
+              for (int b = 0; b < NB; b++) {
+                const ulonglong2 xv =
+                    *reinterpret_cast<const ulonglong2*>(xsl + b * KCE + pc * 32);
+                fma2(acc01[b], w01, xv.x);
+                fma2(acc23[b], w23, xv.y);
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+          // combine lanes: (g0+g1)+(g2+g3) per 8-lane position, then hsum8
+          float v[4] = {lo_f(acc01[b]), hi_f(acc01[b]), lo_f(acc23[b]), hi_f(acc23[b])};
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const float t1 = __fadd_rn(v[k], __shfl_xor_sync(0xffffffffu, v[k], 2));
+            v[k] = __fadd_rn(t1, __shfl_xor_sync(0xffffffffu, t1, 4));
+          }
+#pragma unroll
+          for (int k = 0; k < 4; k++) v[k] = __fadd_rn(v[k], __shfl_xor_sync(0xffffffffu, v[k], 1));
+          float sum = __fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3]));
+          const int gr = (gq0 + wc) * 4 + rq;
+          const bool valid = ok && wc < gn && gr < ph.N;
+          if (valid) sum = __fmul_rn(sum, ph.scale[gr]);
+          float* y = ph.y + (long)b * ph.y_stride;
+          if (ph.epi == EPI_SWIGLU) {
+            const float up = __shfl_down_sync(0xffffffffu, sum, 8);
+            if (valid && sl == 0 && (rq & 1) == 0) {
+              const int o = gr >> 1;
+              float sig;
+              if (o < ph.silu_vec_limit)
+                sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_expf_vec(__fsub_rn(0.0f, sum))));
+              else
+                sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, fast_expf(-sum)));
+              y[o] = __fmul_rn(__fmul_rn(sum, sig), up);
+            }
+          } else if (ph.epi == EPI_RESID) {
+            if (valid && sl == 0) y[gr] = __fadd_rn(y[gr], sum);
+          } else {
+            if (valid && sl == 0) y[gr] = sum;
+          }
+        }
+      }
+    }
+    // ---- phase done on this CTA: publish (release) for every other CTA
+    asm volatile("bar.sync 1, %0;" ::"r"(nc));
+    if (ct == 0) {
+      fence_proxy_async();
+      __threadfence();
+      atomicAdd(P.ctr + p, 1);
+    }
+  }
+  if (ct == 0) {
+    __threadfence();
+    if (atomicAdd(P.ctr + kMaxChainPhases, 1) == G - 1) {
+      for (int p = 0; p <= kMaxChainPhases; p++) atomicExch(P.ctr + p, 0);
+    }
+  }
+}
+
+template <int WK, int NB>
+cudaError_t launch_nb(const ChainParams& P, int grid, int smem, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(32 + 32 * kWarps);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_chain_nb_kernel<WK, NB>, P);
+}
+
+template <int WK>
+cudaError_t dispatch_nb(int nb, const ChainParams& P, int grid, int smem, cudaStream_t s, bool pdl,
+                        bool attr_only) {
+  auto go = [&](auto kern, auto launch) -> cudaError_t {
+    if (attr_only)
+      return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 256);
+    return launch(P, grid, smem, s, pdl);
+  };
+  switch (nb) {
+    case 2: return go(gemv_chain_nb_kernel<WK, 2>, launch_nb<WK, 2>);
+    case 3: return go(gemv_chain_nb_kernel<WK, 3>, launch_nb<WK, 3>);
+    case 4: return go(gemv_chain_nb_kernel<WK, 4>, launch_nb<WK, 4>);
+    case 5: return go(gemv_chain_nb_kernel<WK, 5>, launch_nb<WK, 5>);
+    case 6: return go(gemv_chain_nb_kernel<WK, 6>, launch_nb<WK, 6>);
+    case 7: return go(gemv_chain_nb_kernel<WK, 7>, launch_nb<WK, 7>);
+    case 8: return go(gemv_chain_nb_kernel<WK, 8>, launch_nb<WK, 8>);
+  }
+  return cudaErrorInvalidValue;
+}
+
 template <int WK, int KCE>
 cudaError_t launch_t(const ChainParams& P, int grid, int smem, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
@@ -290,7 +573,38 @@ cudaError_t chain_prepare() {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (!e) e = cudaFuncSetAttribute(gemv_chain_kernel<EC_W_FP8, 32>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  ChainParams P{};
+  for (int nb = 2; nb <= 8 && !e; nb++) {
+    e = dispatch_nb<EC_W_INT8>(nb, P, 0, 0, nullptr, false, true);
+    if (!e) e = dispatch_nb<EC_W_FP8>(nb, P, 0, 0, nullptr, false, true);
+  }
   return e;
+}
+
+int chain_nb_smem(int kmax, int nb, int* stages) {
+  const int fixed = 512 + ((kmax * 4 + 127) & ~127);
+  const int slot = kWarps * 4 * 512 + nb * 512 * 4;
+  int s = (227 * 1024 - 256 - fixed) / slot;
+  if (s > kStagesMax) s = kStagesMax;
+  if (s < 2) return -1;
+  *stages = s;
+  return fixed + s * slot;
+}
+
+cudaError_t chain_launch_nb(int wkind, ChainParams P, int nb, int grid, cudaStream_t s, bool pdl) {
+  if (nb < 2 || nb > 8 || P.nph < 1 || P.nph > kMaxChainPhases) return cudaErrorInvalidValue;
+  P.kmax = 0;
+  for (int p = 0; p < P.nph; p++) {
+    if (P.ph[p].pro != PRO_NORM_ROWS && (P.ph[p].K % 512)) return cudaErrorInvalidValue;
+    if (P.ph[p].pro == PRO_NORM_ROWS && P.ph[p].K > P.kmax) P.kmax = P.ph[p].K;
+  }
+  int stages = 0;
+  const int smem = chain_nb_smem(P.kmax, nb, &stages);
+  if (smem < 0) return cudaErrorInvalidValue;
+  P.stages = stages;
+  if (wkind == EC_W_INT8) return dispatch_nb<EC_W_INT8>(nb, P, grid, smem, s, pdl, false);
+  if (wkind == EC_W_FP8) return dispatch_nb<EC_W_FP8>(nb, P, grid, smem, s, pdl, false);
+  return cudaErrorInvalidValue;
 }
 
 int chain_smem(const ChainParams& P, int kce, int* stages) {

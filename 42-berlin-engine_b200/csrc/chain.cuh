@@ -20,7 +20,13 @@ struct ChainPhase {
   int N, K;
   int pro, epi;
   int silu_vec_limit;
+  int x_stride, y_stride;  // batched chain: floats between sequences
 };
+
+// Batched chain: one more phase kind, the RMSNorm of NB rows into y (no
+// weights; CTA b normalises row b), so that the GEMV phases read normalised
+// vectors chunk by chunk.
+constexpr int PRO_NORM_ROWS = 2;
 
 struct ChainParams {
   ChainPhase ph[kMaxChainPhases];
@@ -39,5 +45,9 @@ int chain_kce(const ChainParams& P);
 cudaError_t chain_prepare();
 // grid = the SM count (every CTA resident at once).
 cudaError_t chain_launch(int wkind, ChainParams P, int grid, cudaStream_t s, bool pdl);
+// The same chain over nb sequences (2..8) at once: each weight byte is
+// decoded once and accumulated for every sequence in the reference's order.
+// Phases with pro == PRO_NORM_ROWS normalise (x -> y, norm_w, K columns).
+cudaError_t chain_launch_nb(int wkind, ChainParams P, int nb, int grid, cudaStream_t s, bool pdl);
 
 }  // namespace ec

@@ -25,6 +25,9 @@ extern "C" const char* ec_last_error(void) { return g_err; }
 
 namespace {
 
+// sequences per batched-chain pass
+constexpr int kPack = 8;
+
 struct Mat {
   uint8_t* w = nullptr;  // packed layout (gemv_packed.cu), rows padded to a multiple of 4
   float* scale = nullptr;  // per row (INT8 and FP8 alike, FP8 expanded)
@@ -54,7 +57,9 @@ struct ec_ctx {
         *logits = nullptr;
   int *argmax = nullptr, *tokens = nullptr, *pos = nullptr, *sel = nullptr, *nsel = nullptr;
   int* err = nullptr;
-  int* chain_ctr = nullptr;  // [layers][kMaxChainPhases + 1]
+  int* chain_ctr = nullptr;  // [layers][packs][kMaxChainPhases + 1]
+  float* xn = nullptr;       // batched chain: RMSNorm'd rows [max_batch][dim]
+  int npacks = 1;            // batched-chain passes per step (max_batch / 8, rounded up)
   void* amax = nullptr;      // split-argmax partials and counters
   bool chain = false;        // one persistent GEMV kernel per layer
   float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
@@ -286,8 +291,14 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     TRY(cudaMemset(am, 0, ec::argmax_scratch_bytes(S)));
     ctx->amax = am;
   }
-  TRY(dalloc(ctx, &ctx->chain_ctr, (size_t)L * (ec::kMaxChainPhases + 1)));
-  TRY(cudaMemset(ctx->chain_ctr, 0, (size_t)L * (ec::kMaxChainPhases + 1) * sizeof(int)));
+  {
+    // one counter block per (layer, pack of up to 8 sequences), plus layer 0's QKV
+    ctx->npacks = (S + kPack - 1) / kPack;
+    const size_t nctr = (size_t)(L + 1) * ctx->npacks * (ec::kMaxChainPhases + 1);
+    TRY(dalloc(ctx, &ctx->chain_ctr, nctr));
+    TRY(cudaMemset(ctx->chain_ctr, 0, nctr * sizeof(int)));
+  }
+  TRY(dalloc(ctx, &ctx->xn, (size_t)S * D));
   // KV
   ec::KvLayout& kv = ctx->kv;
   kv.n_layers = L;
@@ -574,8 +585,150 @@ ec::ChainPhase chain_phase(const Mat& m, int pro, int epi, const float* x, const
   return ph;
 }
 
+// The batched step (B > 1 with the chain): every sequence-parallel kernel runs
+// once for all B sequences; the weight-streaming GEMVs run as one batched
+// chain per layer per pack of up to kPack sequences.
+cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos, int B,
+                                 bool feedback) {
+  const ec_model_config& c = ctx->c;
+  const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
+  const int V = c.vocab_size, L = c.n_layers, QW = (H + 2 * KV) * hd;
+  cudaError_t e;
+  ctx->launches = 0;
+  ec::StepBuffers sb{};
+  sb.rope_cos = ctx->rope_cos;
+  sb.rope_sin = ctx->rope_sin;
+  sb.sparse_k = c.sparse_k;
+  sb.window = c.window;
+  sb.sparse_blocks_k = c.sparse_blocks_k;
+  sb.err = ctx->err;
+  sb.max_sel = ctx->max_sel;
+  sb.pos = pos;
+  sb.qkv = ctx->qkvb;
+  sb.qrot = ctx->qrot;
+  sb.att = ctx->att;
+  sb.sel = ctx->sel;
+  sb.nsel = ctx->nsel;
+  auto phase = [&](const Mat& m, int pro, int epi, const float* x, int xs, const uint16_t* nw,
+                   float* y, int ys) {
+    ec::ChainPhase ph = chain_phase(m, pro, epi, x, nw, y);
+    ph.x_stride = xs;
+    ph.y_stride = ys;
+    return ph;
+  };
+  auto norm = [&](const float* x, const uint16_t* nw, float* y) {
+    ec::ChainPhase ph{};
+    ph.x = x;
+    ph.norm_w = nw;
+    ph.y = y;
+    ph.K = D;
+    ph.pro = ec::PRO_NORM_ROWS;
+    ph.x_stride = D;
+    ph.y_stride = D;
+    return ph;
+  };
+  auto run = [&](ec::ChainParams& P, int layer_slot, int pack, int nb) -> cudaError_t {
+    P.ctr = ctx->chain_ctr +
+            ((size_t)layer_slot * ctx->npacks + pack) * (ec::kMaxChainPhases + 1);
+    P.err = ctx->err;
+    P.eps = c.norm_eps;
+    double by = 0;
+    for (int i = 0; i < P.nph; i++)
+      if (P.ph[i].pro != ec::PRO_NORM_ROWS) by += (double)P.ph[i].N * P.ph[i].K;
+    ProfScope ps(ctx, EC_K_GEMV_CHAIN, by);
+    ctx->launches++;
+    if (nb == 1) return ec::chain_launch(c.weight_kind, P, ctx->n_sm, ctx->stream, true);
+    return ec::chain_launch_nb(c.weight_kind, P, nb, ctx->n_sm, ctx->stream, true);
+  };
+  {
+    ProfScope ps(ctx, EC_K_EMBED, (2.0 + 4.0) * D * B);
+    if ((e = ec::launch_embed(ctx->emb, tokens, ctx->x, D, c.vocab_size, B, ctx->stream, true)))
+      return e;
+    ctx->launches++;
+  }
+  // layer 0's QKV (its own counter block: slot L)
+  for (int b0 = 0, pk = 0; b0 < B; b0 += kPack, pk++) {
+    const int nb = B - b0 < kPack ? B - b0 : kPack;
+    ec::ChainParams P{};
+    if (nb == 1) {
+      P.ph[0] = chain_phase(ctx->qkv[0], ec::PRO_RMSNORM, ec::EPI_STORE, ctx->x + (size_t)b0 * D,
+                            ctx->attn_norm[0], ctx->qkvb + (size_t)b0 * QW);
+      P.nph = 1;
+    } else {
+      P.ph[0] = norm(ctx->x + (size_t)b0 * D, ctx->attn_norm[0], ctx->xn + (size_t)b0 * D);
+      P.ph[1] = phase(ctx->qkv[0], ec::PRO_NONE, ec::EPI_STORE, ctx->xn + (size_t)b0 * D, D, nullptr,
+                      ctx->qkvb + (size_t)b0 * QW, QW);
+      P.nph = 2;
+    }
+    if ((e = run(P, L, pk, nb))) return e;
+  }
+  for (int l = 0; l < L; l++) {
+    {
+      ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
+      if ((e = ec::launch_kv_append(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
+      ctx->launches++;
+    }
+    if (!ctx->kv.paged) {
+      ProfScope ps(ctx, EC_K_SELECT, 0.0);
+      if ((e = ec::launch_linear_select(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
+      ctx->launches++;
+    }
+    {
+      ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
+      if ((e = ec::launch_attention(ctx->kv, sb, l, B, ctx->stream, true))) return e;
+      ctx->launches++;
+    }
+    const bool last = l + 1 == L;
+    for (int b0 = 0, pk = 0; b0 < B; b0 += kPack, pk++) {
+      const int nb = B - b0 < kPack ? B - b0 : kPack;
+      float* x = ctx->x + (size_t)b0 * D;
+      float* xn = ctx->xn + (size_t)b0 * D;
+      float* hb = ctx->hbuf + (size_t)b0 * F;
+      float* att = ctx->att + (size_t)b0 * H * hd;
+      ec::ChainParams P{};
+      if (nb == 1) {
+        P.ph[0] = chain_phase(ctx->wo[l], ec::PRO_NONE, ec::EPI_RESID, att, nullptr, x);
+        P.ph[1] = chain_phase(ctx->w13[l], ec::PRO_RMSNORM, ec::EPI_SWIGLU, x, ctx->ffn_norm[l], hb);
+        P.ph[2] = chain_phase(ctx->w2[l], ec::PRO_NONE, ec::EPI_RESID, hb, nullptr, x);
+        P.ph[3] = last ? chain_phase(ctx->lm, ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->final_norm,
+                                     ctx->logits + (size_t)b0 * V)
+                       : chain_phase(ctx->qkv[l + 1], ec::PRO_RMSNORM, ec::EPI_STORE, x,
+                                     ctx->attn_norm[l + 1], ctx->qkvb + (size_t)b0 * QW);
+        P.nph = 4;
+      } else {
+        P.ph[0] = phase(ctx->wo[l], ec::PRO_NONE, ec::EPI_RESID, att, H * hd, nullptr, x, D);
+        P.ph[1] = norm(x, ctx->ffn_norm[l], xn);
+        P.ph[2] = phase(ctx->w13[l], ec::PRO_NONE, ec::EPI_SWIGLU, xn, D, nullptr, hb, F);
+        P.ph[3] = phase(ctx->w2[l], ec::PRO_NONE, ec::EPI_RESID, hb, F, nullptr, x, D);
+        P.ph[4] = norm(x, last ? ctx->final_norm : ctx->attn_norm[l + 1], xn);
+        P.ph[5] = last ? phase(ctx->lm, ec::PRO_NONE, ec::EPI_STORE, xn, D, nullptr,
+                               ctx->logits + (size_t)b0 * V, V)
+                       : phase(ctx->qkv[l + 1], ec::PRO_NONE, ec::EPI_STORE, xn, D, nullptr,
+                               ctx->qkvb + (size_t)b0 * QW, QW);
+        P.nph = 6;
+      }
+      if ((e = run(P, l, pk, nb))) return e;
+    }
+  }
+  {
+    ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
+    for (int b = 0; b < B; b++) {
+      if ((e = ec::launch_argmax_split(ctx->logits + (size_t)b * V, V, 1, ctx->argmax + b,
+                                       feedback ? const_cast<int*>(tokens) + b : nullptr,
+                                       feedback ? const_cast<int*>(pos) + b : nullptr,
+                                       static_cast<uint8_t*>(ctx->amax) +
+                                           (size_t)b * ec::argmax_scratch_bytes(1),
+                                       ctx->stream, true)))
+        return e;
+      ctx->launches++;
+    }
+  }
+  return cudaSuccess;
+}
+
 // Enqueue one decode step for B sequences (tokens/pos in device memory).
 cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback) {
+  if (ctx->chain && B > 1) return enqueue_step_batched(ctx, tokens, pos, B, feedback);
   const ec_model_config& c = ctx->c;
   const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
   cudaError_t e;
@@ -665,7 +818,7 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
         else
           P.ph[3] = chain_phase(ctx->lm, ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->final_norm, lg);
         P.nph = 4;
-        P.ctr = ctx->chain_ctr + (size_t)l * (ec::kMaxChainPhases + 1);
+        P.ctr = ctx->chain_ctr + (size_t)l * ctx->npacks * (ec::kMaxChainPhases + 1);
         P.err = ctx->err;
         P.eps = c.norm_eps;
         P.mark = l == 1;
@@ -835,6 +988,10 @@ extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
   // down -- or with the chain: append, [select], attention, chain -- then
   // [LM head] and argmax
   const int sel = ctx->kv.paged ? 0 : 1;
+  if (ctx->chain && B > 1) {
+    const int packs = (B + kPack - 1) / kPack;
+    return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + B;
+  }
   if (ctx->chain) return B * (2 + ctx->c.n_layers * (3 + sel) + 1);
   return B * (1 + ctx->c.n_layers * (6 + sel) + 2);
 }

@@ -43,6 +43,7 @@ def _load(name):
 
 
 METRIC = "decode tok/s (Llama-3-8B-shaped INT8, b=1 per GPU, 2k context)"
+METRIC_B = "decode tok/s (Llama-3-8B-shaped INT8, b={} per GPU, 2k context)"
 PROMPT = 2048
 SEED = 1234
 
@@ -199,7 +200,7 @@ def run_cuda(args):
     eng = _load("engine")
     S = _load("synth")
     cfg = S.LLAMA3_8B
-    B = 1
+    B = args.batch
     e = eng.Engine(cfg, device=local, max_batch=B)
     src = S.DeviceModel(cfg, seed=SEED, device=local)
 
@@ -218,11 +219,12 @@ def run_cuda(args):
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     # prompt: 2048 random tokens through the decode path (KV cache filled)
-    prompt = S.prompt(cfg, PROMPT, seed=7 + rank)
-    for p in range(PROMPT):
-        _, am = e.step([prompt[p]], [p], want_logits=False)
-    tok = torch.tensor([int(am[0])], dtype=torch.int32, device=f"cuda:{local}")
-    pos = torch.tensor([PROMPT], dtype=torch.int32, device=f"cuda:{local}")
+    # B independent sequences, each its own random prompt, decoded together
+    prompts = [S.prompt(cfg, args.prompt, seed=7 + rank * 1000 + b) for b in range(B)]
+    for p in range(args.prompt):
+        _, am = e.step([int(pr[p]) for pr in prompts], [p] * B, want_logits=False)
+    tok = torch.tensor([int(a) for a in am], dtype=torch.int32, device=f"cuda:{local}")
+    pos = torch.tensor([args.prompt] * B, dtype=torch.int32, device=f"cuda:{local}")
     stream = torch.cuda.ExternalStream(e.stream())
 
     def steps(n):
@@ -253,15 +255,15 @@ def run_cuda(args):
     value = ws * B * 1000.0 / ms
 
     # end to end through the C ABI with host buffers (token/pos in, logits out)
-    cur_tok, cur_pos = int(tok.item()), int(pos.item())
+    cur_tok, cur_pos = [int(v) for v in tok.cpu()], [int(v) for v in pos.cpu()]
     host_logits = np.empty((B, cfg.vocab_size), np.float32)
     for _ in range(2):
-        lg, am = e.step([cur_tok], [cur_pos])
-        cur_tok, cur_pos = int(am[0]), cur_pos + 1
+        lg, am = e.step(cur_tok, cur_pos)
+        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        lg, am = e.step([cur_tok], [cur_pos])
-        cur_tok, cur_pos = int(am[0]), cur_pos + 1
+        lg, am = e.step(cur_tok, cur_pos)
+        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
     e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
     if ws > 1:
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
@@ -272,8 +274,8 @@ def run_cuda(args):
     # live per-kernel timing (profiling mode: events around each launch)
     e.profile(True)
     for _ in range(3):
-        lg, am = e.step([cur_tok], [cur_pos], want_logits=False)
-        cur_tok, cur_pos = int(am[0]), cur_pos + 1
+        lg, am = e.step(cur_tok, cur_pos, want_logits=False)
+        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
     prof = e.profile_read()
     e.profile(False)
     # roofline of the dominant kernel: its algorithmic bytes per launch over its
@@ -293,17 +295,18 @@ def run_cuda(args):
     weight_bytes = (sum(int(np.prod(s)) for s in S.mat_shapes(cfg).values()) * cfg.n_layers
                     + cfg.vocab_size * cfg.dim)
     kv_tok = cfg.n_layers * cfg.n_kv_heads * (cfg.head_dim * 2 + 8)
-    att_tokens = min(PROMPT + args.warmup + args.steps, 64 * 16)
-    step_bytes = weight_bytes + kv_tok * att_tokens
+    att_tokens = min(args.prompt + args.warmup + args.steps, 64 * 16)
+    step_bytes = weight_bytes + B * kv_tok * att_tokens
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": ws,
+            "metric": METRIC if B == 1 else METRIC_B.format(B), "value": round(value, 3),
+            "unit": "tok/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": "llama3-8b-shape decode b=1 per GPU", "global_batch": ws * B,
-                       "context": PROMPT, "weights": "int8 per-row pow2 scale",
+            "config": {"workload": f"llama3-8b-shape decode b={B} per GPU", "global_batch": ws * B,
+                       "context": args.prompt, "weights": "int8 per-row pow2 scale",
                        "kv": "paged int8", "parallelism": f"dp{ws} (replicas)",
                        "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"},
             "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
@@ -351,6 +354,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="tokens already in the cache")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="sequences decoded together per GPU (b=64: the batched metric)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

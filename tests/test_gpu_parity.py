@@ -349,3 +349,29 @@ def test_layer_chain_matches_oracle(eng, torch, oracle, synth, monkeypatch, chai
         if check:
             assert np.array_equal(bits(lg[0]), bits(want)), f"step {pos}"
     e.close()
+
+
+@pytest.mark.parametrize("B", [3, 9])
+def test_batched_chain_matches_oracle(eng, torch, oracle, synth, B):
+    """B sequences per decode step: the sequence-parallel kernels run once for
+    all B, the weight-streaming GEMVs as one batched chain per pack of up to 8
+    sequences (B = 9: a pack of 8 and a pack of 1).  Every sequence's logits
+    bit-identical to its own restatement model, and the greedy tokens."""
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4,
+                            vocab_size=4096, seq_len=2048, head_dim=64, rope_theta=1e4)
+    model = synth.make_model(cfg, seed=23)
+    e = eng.Engine(cfg, max_batch=B)
+    e.load(model)
+    packs = (B + 7) // 8
+    assert e.launches_per_step(B) == 1 + packs + 2 * (2 + packs) + B
+    pms = [oracle.PortModel(model) for _ in range(B)]
+    prompts = [synth.prompt(cfg, 70, seed=40 + b) for b in range(B)]
+    for t in range(70):
+        check = t % 10 == 0 or t >= 66
+        lg, am = e.step([int(p[t]) for p in prompts], [t] * B, want_logits=check)
+        for b in range(B):
+            want = pms[b].forward(int(prompts[b][t]), t)
+            if check:
+                assert np.array_equal(bits(lg[b]), bits(want)), f"step {t} sequence {b}"
+                assert am[b] == oracle.port().port_argmax(want, want.size)
+    e.close()
