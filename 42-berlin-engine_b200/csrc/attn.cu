@@ -597,7 +597,8 @@ __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a -
 
 // One CTA of the cluster: all tokens' scores and factors, this CTA's quarter
 // of the head dimensions of V (raw and dequantised).
-__host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int esize) {
+__host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int esize,
+                                                      bool vf = true) {
   AttnSmemLayout L;
   const int nblk = max_tok / 16 + 4;  // selected blocks (partial last block included)
   const size_t arr = (size_t)(max_tok + 8) * 4;
@@ -622,8 +623,8 @@ __host__ __device__ inline AttnSmemLayout attn_layout(int max_tok, int hd, int e
   o = align_up(o, 16);
   L.vraw = o;
   o = align_up(o + (size_t)max_tok * dq * esize, 16);
-  L.vf = o;  // transposed: [dq][max_tok + 4] floats
-  o += (size_t)(max_tok + 4) * dq * 4;
+  L.vf = o;  // transposed: [dq][max_tok + 4] floats (absent without vf)
+  if (vf) o += (size_t)(max_tok + 4) * dq * 4;
   L.total = o;
   return L;
 }
@@ -655,9 +656,13 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
 //      for the CTA's hd/4 dimensions (the multiply skipped over runs where
 //      every f_t is 1), one thread the denominator; out = o * (1/sum).
 // Spreading a head over four SMs quarters the bytes each SM must pull.
-template <bool PAGED>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, StepBuffers sb,
-                                                                 int layer, int max_tok) {
+// VF: dequantise this CTA's V quarter once into a float buffer read by a
+// register-pipelined chain (lowest latency, one CTA per SM); without it the
+// chain dequantises as it goes, the CTA needs a quarter of the shared memory
+// and several CTAs share an SM (batched steps: throughput over latency).
+template <bool PAGED, bool VF>
+__global__ void __launch_bounds__(kAttnThreads, VF ? 1 : 3)
+    attention_kernel(KvLayout kv, StepBuffers sb, int layer, int max_tok) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   extern __shared__ __align__(128) uint8_t smem[];
@@ -668,7 +673,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim;
   const int kvh = h / (H / KV);
   const int dq = hd / kSplit;  // this CTA's dimensions: [r*dq, (r+1)*dq)
-  const AttnSmemLayout Ly = attn_layout(max_tok, hd, ES);
+  const AttnSmemLayout Ly = attn_layout(max_tok, hd, ES, VF);
   float* qs = reinterpret_cast<float*>(smem);
   float* sc = reinterpret_cast<float*>(smem + Ly.sc);
   float* sf = reinterpret_cast<float*>(smem + Ly.sf);
@@ -879,7 +884,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
   bool ok = mbar_wait(&vbar, 0, sb.err);
   // thread -> (token i, dimensions 4g..4g+3) with i fastest, so a warp's
   // transposed stores fall in 32 consecutive words
-  const int ng = dq >> 2;
+  const int ng = VF ? dq >> 2 : 0;
   for (int w = tid; w < T * ng && ok; w += blockDim.x) {
     const int g = w / T, i = w - g * T, d = 4 * g;
     uint4 out;
@@ -929,6 +934,19 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
     // one's chain runs; with f_t == 1 the multiply is the identity and runs
     // of four such tokens skip it.
     ok = __all_sync(0xffffffffu, ok);
+    if constexpr (!VF) {
+      // v_t dequantised in the loop (v * scale_t, exact); o * 1 == o, so the
+      // multiply needs no skipping for exactness
+      const int dd = lane % dq;
+      for (int i = 0; i < T && ok; i++) {
+        float v;
+        if constexpr (PAGED)
+          v = __fmul_rn(s8_to_f32(vraw[(size_t)i * dq + dd]), tvs[i]);
+        else
+          v = bf16_to_f32(reinterpret_cast<const uint16_t*>(vraw)[(size_t)i * dq + dd]);
+        o = __fmaf_rn(sc[i], v, __fmul_rn(o, sf[i]));
+      }
+    }
     const float* row = vf + (size_t)(lane % dq) * (max_tok + 4);
     float4 va[8], ea[8], vb[8], eb[8];
     auto load = [&](float4* v, float4* e, int base) {
@@ -959,7 +977,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
       }
     };
     // two register buffers, one loading while the other runs
-    const int T32 = ok ? (T & ~31) : 0;
+    const int T32 = (ok && VF) ? (T & ~31) : 0;
     if (T32) load(va, ea, 0);
     for (int base = 0; base < T32; base += 64) {
       if (base + 32 < T32) load(vb, eb, base + 32);
@@ -968,7 +986,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(KvLayout kv, St
       if (base + 64 < T32) load(va, ea, base + 64);
       run(vb, eb, base + 32);
     }
-    for (int i = T32; i < T && ok; i++) o = __fmaf_rn(sc[i], row[i], __fmul_rn(o, sf[i]));
+    for (int i = T32; i < T && ok && VF; i++) o = __fmaf_rn(sc[i], row[i], __fmul_rn(o, sf[i]));
     PHASE_MARK(mk && lane == 0, 13);
   } else if (warp == 1 && lane == 0) {
     // denominator: sum_t = fma(sum_{t-1}, f_t, e_t)
@@ -1027,7 +1045,7 @@ static cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaS
 }
 
 // The attention kernel: grid (kSplit * heads, B) in clusters of kSplit CTAs.
-template <bool PAGED>
+template <bool PAGED, bool VF>
 static cudaError_t launch_attn(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
                                int max_tok, size_t smem, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
@@ -1044,7 +1062,7 @@ static cudaError_t launch_attn(const KvLayout& kv, const StepBuffers& sb, int la
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attention_kernel<PAGED>, kv, sb, layer, max_tok);
+  return cudaLaunchKernelEx(&cfg, attention_kernel<PAGED, VF>, kv, sb, layer, max_tok);
 }
 
 // paged_kv_append of one token into a one-layer view (k, v already rotated).
@@ -1100,8 +1118,10 @@ cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuf
   const int smem = (int)attn_smem(kv, sb, max_tok);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   // the largest opt-in: per-op calls share these kernels with other sizes
-  cudaError_t e = opt_in_max_smem(attention_kernel<true>);
-  if (!e) e = opt_in_max_smem(attention_kernel<false>);
+  cudaError_t e = opt_in_max_smem(attention_kernel<true, true>);
+  if (!e) e = opt_in_max_smem(attention_kernel<false, true>);
+  if (!e) e = opt_in_max_smem(attention_kernel<true, false>);
+  if (!e) e = opt_in_max_smem(attention_kernel<false, false>);
   const int cap_c = sb.window + lsh.max_cand * lsh.unit;
   const int ssel = cap_c * 8 + 1024 * 8 + 256 * 4;
   if (!e && ssel <= 227 * 1024)
@@ -1130,9 +1150,9 @@ cudaError_t launch_attention_n(const KvLayout& kv, const StepBuffers& sb, int ma
                                cudaStream_t s) {
   const size_t smem = attention_smem_bytes(max_tok, kv.head_dim, kv.paged != 0);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  cudaError_t e = opt_in_max_smem(attention_kernel<true>);
+  cudaError_t e = opt_in_max_smem(attention_kernel<true, true>);
   if (e != cudaSuccess) return e;
-  return launch_attn<true>(kv, sb, 0, 1, max_tok, smem, s, false);
+  return launch_attn<true, true>(kv, sb, 0, 1, max_tok, smem, s, false);
 }
 
 cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
@@ -1151,9 +1171,14 @@ cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const
 cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
                              cudaStream_t s, bool pdl) {
   const int max_tok = attn_max_tok(kv, sb);
-  const size_t smem = attn_smem(kv, sb, max_tok);
-  if (kv.paged) return launch_attn<true>(kv, sb, layer, B, max_tok, smem, s, pdl);
-  return launch_attn<false>(kv, sb, layer, B, max_tok, smem, s, pdl);
+  // from 4 sequences on, throughput over latency: the smaller variant
+  const bool vf = B < 4;
+  const size_t smem = attn_layout(max_tok, kv.head_dim, kv.paged ? 1 : 2, vf).total;
+  if (kv.paged)
+    return vf ? launch_attn<true, true>(kv, sb, layer, B, max_tok, smem, s, pdl)
+              : launch_attn<true, false>(kv, sb, layer, B, max_tok, smem, s, pdl);
+  return vf ? launch_attn<false, true>(kv, sb, layer, B, max_tok, smem, s, pdl)
+            : launch_attn<false, false>(kv, sb, layer, B, max_tok, smem, s, pdl);
 }
 
 }  // namespace ec
