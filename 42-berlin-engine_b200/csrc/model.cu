@@ -1139,6 +1139,56 @@ extern "C" int ec_op_gemv_packed(int wkind, const void* w, const float* scale, c
   return EC_OK;
 }
 
+extern "C" int ec_op_gemv_packed_batch(int wkind, const void* w, const float* scale,
+                                       const float* x, float* y, int m, int k, int nb,
+                                       void* stream) {
+  if (!w || !x || !y || !scale || m <= 0 || k <= 0 || nb <= 0) return fail(EC_ERR_ARG, "bad argument");
+  if (wkind != EC_W_INT8 && wkind != EC_W_FP8) return fail(EC_ERR_ARG, "INT8 or FP8 weights");
+  if (nb > 1 && k % 512) return fail(EC_ERR_UNSUPPORTED, "batched GEMV needs k % 512 == 0");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  EC_CUDA_TRY(ec::chain_prepare());
+  int* ctr = nullptr;
+  const size_t cb = (ec::kMaxChainPhases + 2) * sizeof(int);  // counters + error word
+  EC_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&ctr), cb, s));
+  int rc = EC_OK;
+  cudaError_t e = cudaMemsetAsync(ctr, 0, cb, s);
+  for (int b0 = 0; b0 < nb && e == cudaSuccess; b0 += kPack) {
+    const int n = nb - b0 < kPack ? nb - b0 : kPack;
+    ec::ChainParams P{};
+    ec::ChainPhase& ph = P.ph[0];
+    ph.w = static_cast<const uint8_t*>(w);
+    ph.scale = scale;
+    ph.x = x + (size_t)b0 * k;
+    ph.y = y + (size_t)b0 * m;
+    ph.N = m;
+    ph.K = k;
+    ph.pro = ec::PRO_NONE;
+    ph.epi = ec::EPI_STORE;
+    ph.x_stride = k;
+    ph.y_stride = m;
+    P.nph = 1;
+    P.ctr = ctr;
+    P.err = ctr + ec::kMaxChainPhases + 1;
+    if (wkind == EC_W_FP8) {
+      // the chain reads one scale per row: per-tensor FP8 scale -> per-op packed kernel
+      rc = ec_op_gemv_packed(wkind, w, scale, ph.x, ph.y, m, k, stream);
+      for (int i = 1; i < n && rc == EC_OK; i++)
+        rc = ec_op_gemv_packed(wkind, w, scale, ph.x + (size_t)i * k, ph.y + (size_t)i * m, m, k, stream);
+      if (rc != EC_OK) break;
+      continue;
+    }
+    e = n == 1 ? ec::chain_launch(wkind, P, nsm, s, false)
+               : ec::chain_launch_nb(wkind, P, n, nsm, s, false);
+  }
+  cudaFreeAsync(ctr, s);
+  if (rc != EC_OK) return rc;
+  EC_CUDA_TRY(e);
+  return EC_OK;
+}
+
 extern "C" int ec_op_rmsnorm(float* out, const float* x, const uint16_t* w, int n, float eps,
                              void* stream) {
   if (!out || !x || !w || n <= 0) return fail(EC_ERR_ARG, "bad argument");

@@ -26,7 +26,7 @@ EXPORTS = [
     "ec_reset", "ec_decode_step", "ec_decode_step_device", "ec_logits_device",
     "ec_argmax_device", "ec_stream", "ec_synchronize", "ec_read_state", "ec_read_lsh",
     "ec_read_counters", "ec_launches_per_step", "ec_op_gemv", "ec_gemv_packed_bytes", "ec_gemv_pack",
-    "ec_op_gemv_packed", "ec_op_rmsnorm", "ec_op_rope",
+    "ec_op_gemv_packed", "ec_op_gemv_packed_batch", "ec_op_rmsnorm", "ec_op_rope",
     "ec_op_silu_mul", "ec_op_quant_int8", "ec_op_argmax", "ec_op_paged_append",
     "ec_op_paged_attention", "ec_op_paged_attention_static", "ec_transformer_init", "ec_transformer_set_tensor",
     "ec_transformer_forward", "ec_transformer_argmax", "ec_transformer_reset",
@@ -88,6 +88,7 @@ def lib():
             "ec_gemv_packed_bytes": (C.c_size_t, [i, i]),
             "ec_gemv_pack": (i, [vp, vp, i, i, vp]),
             "ec_op_gemv_packed": (i, [i, vp, vp, vp, vp, i, i, vp]),
+            "ec_op_gemv_packed_batch": (i, [i, vp, vp, vp, vp, i, i, i, vp]),
             "ec_op_rmsnorm": (i, [vp, vp, vp, i, f, vp]),
             "ec_op_rope": (i, [vp, i, i, i, vp, vp, i, vp]),
             "ec_op_silu_mul": (i, [vp, vp, vp, i, vp]),

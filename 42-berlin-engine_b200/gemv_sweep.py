@@ -1,4 +1,5 @@
-"""Quantised GEMV sweep at batch 1, through ec_op_gemv.
+"""Quantised GEMV sweep at batch 1, 8, 64, 512 through the
+packed-layout entry points (ec_op_gemv_packed, ec_op_gemv_packed_batch).
 
 For each (N, K) in {(4096,4096), (14336,4096), (4096,14336), (128256,4096)} and
 weight kind INT8 (per-row fp32 scale) / FP8-E4M3 (per-tensor scale): time the
@@ -56,8 +57,9 @@ def run_case(torch, eng, kind, n, k, args, peak):
         ws = [torch.randn((n, k), generator=g, device=dev).to(torch.bfloat16)
               for _ in range(copies)]
         sc = None
-    x = torch.randn(k, generator=g, device=dev)
-    y = torch.empty(n, device=dev)
+    nb = args.batch_now
+    x = torch.randn((nb, k), generator=g, device=dev)
+    y = torch.empty((nb, n), device=dev)
     sptr = sc.data_ptr() if sc is not None else None
 
     op = L.ec_op_gemv
@@ -72,8 +74,12 @@ def run_case(torch, eng, kind, n, k, args, peak):
         ws = pk
 
     def run(i):
-        eng.check(op(wk, ws[i % copies].data_ptr(), sptr, x.data_ptr(), y.data_ptr(),
-                     n, k, stream.cuda_stream))
+        if nb == 1:
+            eng.check(op(wk, ws[i % copies].data_ptr(), sptr, x.data_ptr(), y.data_ptr(),
+                         n, k, stream.cuda_stream))
+        else:
+            eng.check(L.ec_op_gemv_packed_batch(wk, ws[i % copies].data_ptr(), sptr, x.data_ptr(),
+                                                y.data_ptr(), n, k, nb, stream.cuda_stream))
 
     for i in range(args.warmup):
         run(i)
@@ -85,9 +91,10 @@ def run_case(torch, eng, kind, n, k, args, peak):
     ev[1].record(stream)
     torch.cuda.synchronize()
     us = ev[0].elapsed_time(ev[1]) * 1e3 / args.iters
-    algo = wbytes + (4 * n if kind == "int8" else 4) + 4 * k + 4 * n
+    algo = wbytes + (4 * n if kind == "int8" else 4) + 4 * k * nb + 4 * n * nb
     gbs = algo / (us * 1e-6) / 1e9
-    return {"kernel": "gemv", "layout": args.layout, "kind": kind, "N": n, "K": k, "batch": 1, "us": round(us, 2),
+    return {"kernel": "gemv", "layout": args.layout, "kind": kind, "N": n, "K": k, "batch": nb,
+            "us": round(us, 2), "TFLOPs": round(2.0 * nb * n * k / (us * 1e-6) / 1e12, 2),
             "algo_bytes": algo, "GBps": round(gbs, 1), "frac_of_measured_peak": round(gbs / peak, 4),
             "l2": f"{copies} rotating weight copies"}
 
@@ -99,6 +106,7 @@ def main():
     ap.add_argument("--shapes", default=",".join(f"{n}x{k}" for n, k in SHAPES))
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", default="1", help="activation vectors per call, e.g. 1,8,64,512")
     ap.add_argument("--layout", default="packed", choices=["packed", "rowmajor"],
                     help="packed: the decode step's kernel; rowmajor: ec_op_gemv")
     ap.add_argument("--l2-bytes", type=float, default=512e6, help="bytes of weight copies rotated")
@@ -111,8 +119,12 @@ def main():
     for kind in args.kinds.split(","):
         for shp in args.shapes.split(","):
             n, k = (int(v) for v in shp.split("x"))
-            print(json.dumps(run_case(torch, eng, kind, n, k, args, peak)), flush=True)
-            torch.cuda.empty_cache()
+            for nb in (int(v) for v in args.batch.split(",")):
+                if nb > 1 and (args.layout != "packed" or kind == "bf16"):
+                    continue
+                args.batch_now = nb
+                print(json.dumps(run_case(torch, eng, kind, n, k, args, peak)), flush=True)
+                torch.cuda.empty_cache()
 
 
 if __name__ == "__main__":

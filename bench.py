@@ -112,10 +112,7 @@ class Clocks:
 
 
 def dist_setup():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return ws, rank, local
+    return _load("dp").rank_env()
 
 
 def cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads):
@@ -192,11 +189,9 @@ class _HostWeights:
 def run_cuda(args):
     import torch
     ws, rank, local = dist_setup()
-    if ws > 1:
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dp = _load("dp")
     torch.cuda.set_device(local)
+    dp.init("nccl", torch.device("cuda", local))
     eng = _load("engine")
     S = _load("synth")
     cfg = S.LLAMA3_8B
@@ -233,8 +228,7 @@ def run_cuda(args):
 
     steps(args.warmup)
     e.sync()
-    if ws > 1:
-        torch.distributed.barrier()
+    dp.barrier()
     with Clocks(local) as clk:
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
@@ -247,12 +241,9 @@ def run_cuda(args):
         e.sync()
         torch.cuda.synchronize()
         ms = ev0.elapsed_time(ev1) / args.steps
-    if ws > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-        torch.distributed.barrier()
-    value = ws * B * 1000.0 / ms
+    ms = dp.max_over_ranks(ms, f"cuda:{local}")
+    dp.barrier()
+    value = dp.job_throughput(B, ws, ms)
 
     # end to end through the C ABI with host buffers (token/pos in, logits out)
     cur_tok, cur_pos = [int(v) for v in tok.cpu()], [int(v) for v in pos.cpu()]
@@ -265,10 +256,7 @@ def run_cuda(args):
         lg, am = e.step(cur_tok, cur_pos)
         cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
     e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
-    if ws > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = dp.max_over_ranks(e2e_ms, f"cuda:{local}")
     del host_logits
 
     # live per-kernel timing (profiling mode: events around each launch)
@@ -343,8 +331,7 @@ def run_cuda(args):
                                         "kind": "reference", "sample": f"failed: {exc}"}
         print(json.dumps(line), flush=True)
     e.close()
-    if ws > 1:
-        torch.distributed.destroy_process_group()
+    dp.finish()
 
 
 def main():

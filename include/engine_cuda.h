@@ -172,6 +172,13 @@ int		ec_op_gemv(int wkind, const void *w, const float *scale, const float *x,
 ** (INT8 or FP8 bytes), and ec_op_gemv_packed computes y = W . x, bit-identical
 ** to ec_op_gemv on the row-major matrix.  k must be a multiple of 32. */
 size_t	ec_gemv_packed_bytes(int m, int k);
+/* op_matmul for nb activation vectors at once, each bit-identical to
+** ec_op_gemv_packed on that vector alone: x [nb][k], y [nb][m] (device).
+** INT8: the weights are read once per 8 vectors (FP8: once per vector).  k
+** must be a multiple of 512 when nb > 1.  Uses a small counter buffer from the
+** stream-ordered allocator. */
+int		ec_op_gemv_packed_batch(int wkind, const void *w_packed, const float *scale,
+			const float *x, float *y, int m, int k, int nb, void *stream);
 int		ec_gemv_pack(const void *w_rowmajor, void *w_packed, int m, int k,
 			void *stream);
 int		ec_op_gemv_packed(int wkind, const void *w_packed, const float *scale,

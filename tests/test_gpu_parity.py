@@ -108,6 +108,31 @@ def test_gemv_packed(eng, torch, synth, oracle, monkeypatch, rows_per_thread, ki
     assert np.array_equal(bits(dy.cpu().numpy()), bits(y))
 
 
+@pytest.mark.parametrize("nb", [1, 3, 8, 11])
+def test_gemv_packed_batch(eng, torch, synth, oracle, nb):
+    """nb activation vectors through one weight pass: each result bit-identical
+    to the restatement of op_matmul on that vector."""
+    m, k = 1000, 2048
+    rng = np.random.default_rng(nb)
+    w = rng.standard_normal((m, k), dtype=np.float32) * np.float32(0.02)
+    xs = rng.standard_normal((nb, k), dtype=np.float32)
+    q, s = synth.quant_int8_rows(w, pow2=False)
+    P = oracle.port()
+    L = eng.lib()
+    dq, ds, dx = dev(torch, q), dev(torch, s), dev(torch, xs)
+    packed = torch.empty(L.ec_gemv_packed_bytes(m, k), dtype=torch.uint8, device="cuda")
+    eng.check(L.ec_gemv_pack(dq.data_ptr(), packed.data_ptr(), m, k, None))
+    dy = torch.full((nb, m), float("nan"), dtype=torch.float32, device="cuda")
+    eng.check(L.ec_op_gemv_packed_batch(eng.EC_W_INT8, packed.data_ptr(), ds.data_ptr(),
+                                        dx.data_ptr(), dy.data_ptr(), m, k, nb, None))
+    torch.cuda.synchronize()
+    got = dy.cpu().numpy()
+    for b in range(nb):
+        y = np.zeros(m, np.float32)
+        P.port_gemv_q8(y, q, s, np.ascontiguousarray(xs[b]), m, k)
+        assert np.array_equal(bits(got[b]), bits(y)), f"vector {b}"
+
+
 def test_small_ops(eng, torch):
     L = eng.lib()
     # RMSNorm
