@@ -17,6 +17,7 @@
 #include <cooperative_groups.h>
 
 #include "attn.cuh"
+#include "select.cuh"
 #include "ec_internal.cuh"
 
 namespace ec {
@@ -204,110 +205,6 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
 // Linear-mode selection (inference.c:228-423): one CTA per sequence.
 // sel[b] receives the top-K positions in the reference's heap order.
 // ------------------------------------------------------------------------
-__device__ __forceinline__ float dot_bf16_ref(const uint16_t* a, const float* b, int n) {
-  float acc[8];
-#pragma unroll
-  for (int l = 0; l < 8; l++) acc[l] = 0.0f;
-  int i = 0;
-  for (; i + 7 < n; i += 8) {
-    const uint4 u = *reinterpret_cast<const uint4*>(a + i);
-    float w[8];
-    dec_bf16x2(u.x, w);
-    dec_bf16x2(u.y, w + 2);
-    dec_bf16x2(u.z, w + 4);
-    dec_bf16x2(u.w, w + 6);
-#pragma unroll
-    for (int l = 0; l < 8; l++) acc[l] = __fmaf_rn(w[l], b[i + l], acc[l]);
-  }
-  float s = __fadd_rn(0.0f, hsum8(acc));
-  for (; i < n; i++) s = __fmaf_rn(bf16_to_f32(a[i]), b[i], s);
-  return s;
-}
-
-// Exact replay of heap_push (ops_heap.h:40-100): a min-heap of at most `cap`
-// entries; while not full a value is appended at position size+1 and sifted
-// up past every ancestor strictly greater than it; once full, a value
-// strictly greater than the root replaces it and is sifted down (the left
-// child unless the right one is strictly smaller, while that child is
-// strictly smaller than the value).  The result, in the reference's heap
-// array order, is the index half of hp[1 .. size].
-//
-// Nodes are packed (score bits, index) pairs, 1-based, so a sibling pair is
-// one 16-byte load; positions beyond `size` hold +inf, so a sift-down of
-// fixed depth D (2^D > cap) needs no bound checks: an +inf child is never
-// taken.  One warp: a ballot skips every candidate that cannot beat the
-// current root (the root only grows), lane 0 runs the operations.
-__device__ __forceinline__ void hnode_up(uint2* hp, int n, float v, int vi) {
-  while (n > 1) {
-    const int p = n >> 1;
-    const uint2 pn = hp[p];
-    if (__uint_as_float(pn.x) <= v) break;
-    hp[n] = pn;
-    n = p;
-  }
-  hp[n] = make_uint2(__float_as_uint(v), (unsigned)vi);
-}
-
-template <int D>
-__device__ __forceinline__ void hnode_down(uint2* hp, float v, int vi) {
-  int n = 1;
-  bool go = true;
-#pragma unroll
-  for (int lv = 0; lv < D; lv++) {
-    const int l = 2 * n;
-    const uint4 pr = *reinterpret_cast<const uint4*>(hp + l);
-    const bool right = __uint_as_float(pr.z) < __uint_as_float(pr.x);
-    const uint2 cn = right ? make_uint2(pr.z, pr.w) : make_uint2(pr.x, pr.y);
-    go = go && (__uint_as_float(cn.x) < v);
-    if (go) {
-      hp[n] = cn;
-      n = l + right;
-    }
-  }
-  hp[n] = make_uint2(__float_as_uint(v), (unsigned)vi);
-}
-
-// hp holds 2^(D+1) nodes.  `ready(j)` (whole warp, j non-decreasing) returns
-// once score[0..j] may be read, or false to give up.  idx == nullptr:
-// candidate i carries index i + idx_base.  Candidates go by windows of 32: a
-// ballot against the root at the window's start drops those that cannot be
-// taken (the root only grows); lane 0 runs the rest in order.
-template <int D, typename Ready>
-__device__ int warp_heap_select(const float* score, const int* idx, int idx_base, int n, int cap,
-                                uint2* hp, int lane, Ready ready) {
-  for (int i = lane; i < (2 << D); i += 32) hp[i] = make_uint2(0x7F800000u, 0u);
-  __syncwarp();
-  if (cap <= 0) return 0;
-  int size = 0;      // lane 0's copy is authoritative; broadcast per window
-  float root = 0.0f;
-  for (int base = 0; base < n; base += 32) {
-    if (!ready(min(base + 31, n - 1))) return 0;
-    const int i = base + lane;
-    const bool full = size >= cap;
-    const float sv = i < n ? score[i] : 0.0f;
-    unsigned pend = __ballot_sync(0xffffffffu, i < n && (!full || sv > root));
-    if (lane == 0) {
-      while (pend) {
-        const int k = base + __ffs(pend) - 1;
-        pend &= pend - 1;
-        const float v = score[k];
-        const int vi = idx ? idx[k] : k + idx_base;
-        if (size < cap) {
-          hnode_up(hp, ++size, v, vi);
-          if (size == cap) root = __uint_as_float(hp[1].x);
-        } else if (v > root) {
-          hnode_down<D>(hp, v, vi);
-          root = __uint_as_float(hp[1].x);
-        }
-      }
-    }
-    size = __shfl_sync(0xffffffffu, size, 0);
-    root = __shfl_sync(0xffffffffu, root, 0);
-    __syncwarp();
-  }
-  return size;
-}
-
 __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayout lsh,
                                                             StepBuffers sb, int layer) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -702,7 +599,7 @@ __global__ void __launch_bounds__(kAttnThreads, VF ? 1 : 3)
   const float* qg = sb.qrot + (long)b * H * hd;
   for (int d = tid; d < hd; d += blockDim.x) qs[d] = qg[h * hd + d];
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;  // linear mode
+  const long lrow = ((long)(kv.shared_cache ? 0 : b) * kv.n_layers + layer) * kv.seq_len;  // linear
 
   // ------------------------------------------ selected blocks / positions
   if constexpr (PAGED) {

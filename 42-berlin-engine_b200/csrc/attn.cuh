@@ -20,6 +20,7 @@ struct KvLayout {
   // linear BF16: [S*L][seq_len][KV][hd]
   uint16_t* lk;
   uint16_t* lv;
+  int shared_cache;     // linear: every sequence index reads sequence 0's cache
 };
 
 struct LshLayout {

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "attn.cuh"
+#include "lsh_host.h"
 #include "chain.cuh"
 #include "ec_internal.cuh"
 #include "gemv.cuh"
@@ -91,16 +92,6 @@ cudaError_t dalloc(ec_ctx* c, T** p, size_t n) {
   c->allocs.push_back(v);
   *p = static_cast<T*>(v);
   return cudaSuccess;
-}
-
-// rand_gaussian, src/compute/ops_lsh.c:22-34 (host libm, same formula)
-float rand_gaussian(unsigned* seed) {
-  *seed = *seed * 1103515245u + 12345u;
-  float u1 = (float)((*seed >> 16) & 0x7FFF) / 32767.0f;
-  *seed = *seed * 1103515245u + 12345u;
-  float u2 = (float)((*seed >> 16) & 0x7FFF) / 32767.0f;
-  if (u1 < 1e-6f) u1 = 1e-6f;
-  return sqrtf(-2.0f * logf(u1)) * cosf(2.0f * 3.14159265f * u2);
 }
 
 // EC_GEMV_ROWS_PER_THREAD=1|2 overrides the GEMV plans' choice (tuning).
@@ -349,21 +340,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   lsh.radius = c.lsh_radius;
   lsh.max_cand = c.lsh_max_cand;
   if (lsh.tables > 0) {
-    std::vector<float> hp((size_t)lsh.tables * lsh.bits * hd);
-    for (int t = 0; t < lsh.tables; t++) {
-      unsigned seed = 42u + (unsigned)t;
-      for (int b = 0; b < lsh.bits; b++) {
-        float* row = &hp[((size_t)t * lsh.bits + b) * hd];
-        float norm = 0.0f;
-        for (int d = 0; d < hd; d++) {
-          row[d] = rand_gaussian(&seed);
-          norm = norm + row[d] * row[d];
-        }
-        norm = sqrtf(norm);
-        if (norm > 1e-6f)
-          for (int d = 0; d < hd; d++) row[d] = row[d] / norm;
-      }
-    }
+    const std::vector<float> hp = ec::lsh_hyperplanes(lsh.tables, lsh.bits, hd);
     TRY(dalloc(ctx, &ctx->hp, hp.size()));
     TRY(cudaMemcpy(ctx->hp, hp.data(), hp.size() * 4, cudaMemcpyHostToDevice));
     lsh.hp = ctx->hp;

@@ -30,7 +30,8 @@ EXPORTS = [
     "ec_op_silu_mul", "ec_op_quant_int8", "ec_op_argmax", "ec_op_paged_append",
     "ec_op_paged_attention", "ec_op_paged_attention_static", "ec_transformer_init", "ec_transformer_set_tensor",
     "ec_transformer_forward", "ec_transformer_argmax", "ec_transformer_reset",
-    "ec_transformer_free", "ec_profile_enable", "ec_profile_read",
+    "ec_transformer_free", "ec_profile_enable", "ec_profile_read", "ec_lsh_attn_create",
+    "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain"]
@@ -55,6 +56,12 @@ class PagedView(C.Structure):
     _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("k_scale", C.c_void_p),
                 ("v_scale", C.c_void_p), ("centroid", C.c_void_p), ("page_table", C.c_void_p),
                 ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("max_blocks", C.c_int)]
+
+
+class LshAttnConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_heads", "n_kv_heads", "head_dim", "max_tokens", "tables",
+                                       "bits", "unit", "radius", "max_cand", "window", "top_k",
+                                       "max_queries")]
 
 
 _lib = None
@@ -104,6 +111,11 @@ def lib():
             "ec_transformer_argmax": (i, [C.POINTER(Transformer)]),
             "ec_transformer_reset": (i, [C.POINTER(Transformer)]),
             "ec_transformer_free": (None, [C.POINTER(Transformer)]),
+            "ec_lsh_attn_create": (i, [C.POINTER(LshAttnConfig), i, C.POINTER(vp)]),
+            "ec_lsh_attn_destroy": (None, [vp]),
+            "ec_lsh_attn_build": (i, [vp, vp, vp, i, vp]),
+            "ec_lsh_attn_query": (i, [vp, vp, i, vp, vp, vp, vp]),
+            "ec_lsh_attn_read": (i, [vp, i, vp, C.c_size_t]),
             "ec_profile_enable": (i, [vp, i]),
             "ec_profile_read": (i, [vp, i, C.POINTER(C.c_double), C.POINTER(i),
                                     C.POINTER(C.c_double)]),

@@ -261,6 +261,51 @@ int		ec_op_paged_attention_static(const ec_paged_view *pv, const float *q,
 			float *out, int n_heads, int n_tokens, int sparse_blocks_k,
 			int *selected_out, int *n_selected_out, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Isolated LSH sparse attention over a linear BF16 cache (BASELINE          */
+/* configuration 3): the reference's linear-mode selection, inference.c:     */
+/* 228-423, with lsh_init / lsh_update / lsh_hash / lsh_find_candidates      */
+/* (ops_lsh.c:40-418) generalised to `tables` x `bits` codes over `unit`-    */
+/* token units of KV head 0, then attention_head_sparse (ops_attention.c:    */
+/* 131-170) over the selection in heap order.  The reference's own setting   */
+/* is tables 1, bits 16, unit 64, radius 4, max_cand 64, window 128.         */
+/* ------------------------------------------------------------------------ */
+typedef struct ec_lsh_attn_config
+{
+	int		n_heads;
+	int		n_kv_heads;
+	int		head_dim;		/* 32, 64 or 128 */
+	int		max_tokens;		/* cache capacity */
+	int		tables;			/* 1..16 hash tables */
+	int		bits;			/* 1..16 bits per code */
+	int		unit;			/* tokens per hashed unit (mean key of KV head 0) */
+	int		radius;			/* Hamming radius of a probe */
+	int		max_cand;		/* candidate units per query */
+	int		window;			/* always-attended recent positions */
+	int		top_k;			/* 1..511 positions attended */
+	int		max_queries;	/* queries per ec_lsh_attn_query call */
+}	ec_lsh_attn_config;
+
+typedef struct ec_lsh_attn	ec_lsh_attn;
+
+int		ec_lsh_attn_create(const ec_lsh_attn_config *c, int device,
+			ec_lsh_attn **out);
+void	ec_lsh_attn_destroy(ec_lsh_attn *h);
+/* Index the first n_tokens positions of k, v ([max_tokens][n_kv_heads]
+** [head_dim] BF16, device; the handle keeps the pointers): one code per
+** table per full unit, buckets newest first (lsh_update's chain order). */
+int		ec_lsh_attn_build(ec_lsh_attn *h, const uint16_t *k, const uint16_t *v,
+			int n_tokens, void *stream);
+/* n_queries queries q [n][n_heads][head_dim] (device, rotated) at position
+** n_tokens - 1: selection then attention into out [n][n_heads][head_dim].
+** selected_out [n][top_k] and n_selected_out [n] (device, optional)
+** receive the attended positions in heap order (-1: all positions). */
+int		ec_lsh_attn_query(ec_lsh_attn *h, const float *q, int n_queries,
+			float *out, int *selected_out, int *n_selected_out, void *stream);
+/* Test hook: 0 codes [tables][units] (uint32), 1 bucket offsets
+** [tables][2^bits + 1], 2 per query (units found, candidates). */
+int		ec_lsh_attn_read(ec_lsh_attn *h, int which, void *out, size_t n);
+
 # ifdef __cplusplus
 }
 # endif

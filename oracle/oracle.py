@@ -113,6 +113,8 @@ def port():
         _sig(lib, "port_lsh_update", None, C.POINTER(PortLsh), f32p, C.c_int)
         _sig(lib, "port_lsh_find", C.c_int, C.POINTER(PortLsh),
              np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS"), i32p, C.c_int)
+        _sig(lib, "port_lsh_attend", C.c_int, C.POINTER(PortLsh), u16p, u16p, C.c_int, f32p,
+             C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, i32p, f32p)
         _sig(lib, "port_paged_create", C.POINTER(PortPaged), C.c_int, C.c_int, C.c_int)
         _sig(lib, "port_paged_free", None, C.POINTER(PortPaged))
         _sig(lib, "port_paged_append", None, C.POINTER(PortPaged), f32p, f32p, C.c_int)

@@ -77,6 +77,10 @@ uint32_t	port_lsh_hash(const t_port_lsh *l, int table, const float *v);
 void	port_lsh_update(t_port_lsh *l, const float *key, int pos);
 int		port_lsh_find(const t_port_lsh *l, const uint32_t *qhash,
 			int *unit_ids, int max_units);
+int		port_lsh_attend(const t_port_lsh *l, const uint16_t *k,
+			const uint16_t *v, int kv_len, const float *q, int n_heads,
+			int n_kv_heads, int head_dim, int window, int max_cand, int sparse_k,
+			int *topk, float *out);
 
 /* ---- paged INT8 KV cache, one layer ------------------------------------ */
 # define PORT_KV_BLOCK 16
