@@ -915,6 +915,310 @@ __global__ void __launch_bounds__(kAttnThreads, VF ? 1 : 3)
   }
 }
 
+// ------------------------------------------------------------------------
+// Batched steps, paged KV: one CTA per (KV head, sequence) computes the
+// attention of every query head of the group (op_paged_attention(_sparse),
+// ops_attention.c:292-461, per head, bit for bit as attention_kernel):
+//   1. token table, K / V scales, and the group's V rows (all head
+//      dimensions) copied to shared memory with cp.async;
+//   2. each K row is read once and decoded once for all query heads of the
+//      group; the dots keep the reference's 8-lane order per head;
+//   3. running max per head by a 128-thread max-scan, both exponentials;
+//   4. thread (head j, dimensions 4c..4c+3) runs four output recurrences
+//      o_t = fma(e_t, v_t, o_{t-1} * f_t) as paired f32x2 operations, the
+//      first thread of each head also the denominator.
+// 128 threads per query head of the group; hd / 4 of them run recurrences.
+struct GroupSmemLayout {
+  size_t qs, sc, sf, tks, tvs, trow, boff, bphys, bfill, ones, vraw, total;
+  int ld;
+};
+
+__host__ __device__ inline GroupSmemLayout group_layout(int max_tok, int hd, int hpg) {
+  GroupSmemLayout L;
+  L.ld = (max_tok + 31) / 32 * 32 + 32;
+  const int nblk = max_tok / 16 + 4;
+  size_t o = 0;
+  L.qs = o;
+  o += (size_t)hpg * hd * 4;
+  L.sc = o;
+  o += (size_t)hpg * L.ld * 4;
+  L.sf = o;
+  o += (size_t)hpg * L.ld * 4;
+  L.tks = o;
+  o += (size_t)L.ld * 4;
+  L.tvs = o;
+  o += (size_t)L.ld * 4;
+  L.trow = o;
+  o += (size_t)L.ld * 4;
+  L.boff = o;
+  o += nblk * 4;
+  L.bphys = o;
+  o += nblk * 4;
+  L.bfill = o;
+  o += nblk * 4;
+  L.ones = o;
+  o += (size_t)hpg * (L.ld / 32) * 4;
+  o = align_up(o, 16);
+  L.vraw = o;
+  o += (size_t)L.ld * hd;
+  L.total = o;
+  return L;
+}
+
+constexpr int kGrpMaxHeads = 8;
+
+template <int HPG>
+__global__ void __launch_bounds__(128 * HPG, 1)
+    attention_group_kernel(KvLayout kv, StepBuffers sb, int layer, int max_tok) {
+  constexpr int JB = HPG < 4 ? HPG : 4;  // heads per pass over a K row
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim;
+  constexpr int hpg = HPG;
+  const int h0 = g * hpg;
+  const GroupSmemLayout Ly = group_layout(max_tok, hd, hpg);
+  const int ld = Ly.ld;
+  float* qs = reinterpret_cast<float*>(smem + Ly.qs);
+  float* sc = reinterpret_cast<float*>(smem + Ly.sc);
+  float* sf = reinterpret_cast<float*>(smem + Ly.sf);
+  float* tks = reinterpret_cast<float*>(smem + Ly.tks);
+  float* tvs = reinterpret_cast<float*>(smem + Ly.tvs);
+  int* trow = reinterpret_cast<int*>(smem + Ly.trow);
+  int* boff = reinterpret_cast<int*>(smem + Ly.boff);
+  int* bphys = reinterpret_cast<int*>(smem + Ly.bphys);
+  int* bfill = reinterpret_cast<int*>(smem + Ly.bfill);
+  int* ones = reinterpret_cast<int*>(smem + Ly.ones);
+  uint8_t* vraw = smem + Ly.vraw;
+  __shared__ __align__(8) uint64_t vbar;
+  __shared__ int s_ntok, s_nsel;
+  __shared__ float s_wmax[4 * kGrpMaxHeads];
+  __shared__ float s_sum[kGrpMaxHeads];
+  if (tid == 0) {
+    mbar_init(&vbar, blockDim.x);  // one cp.async arrival per thread
+    fence_mbar_init();
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  const int pos = step_pos(sb, b);
+  const float* qg = sb.qrot + (long)b * H * hd + (long)h0 * hd;
+  for (int d = tid; d < hpg * hd; d += blockDim.x) qs[d] = qg[d];
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+
+  // ------------------------------------------------------ token table
+  const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
+  const int nb = (n_tok + kBlk - 1) / kBlk;
+  const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
+  const int* pt = kv.page_table + base;
+  const int ns = sb.nsel[b];
+  const int* sel = sb.sel + (long)b * sb.max_sel;
+  const int nsel = ns > 0 ? ns : nb;
+  if (warp == 0) {
+    int carry = 0;
+    for (int k0 = 0; k0 < nsel; k0 += 32) {
+      const int k = k0 + lane;
+      int fill = 0;
+      if (k < nsel) {
+        const int lb = ns > 0 ? sel[k] : k;
+        bphys[k] = (int)(base + pt[lb]);
+        fill = (lb == nb - 1) ? n_tok - lb * kBlk : kBlk;
+        bfill[k] = fill;
+      }
+      int incl = fill;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      if (k < nsel) boff[k] = carry + incl - fill;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      s_ntok = carry;
+      s_nsel = nsel;
+    }
+  }
+  __syncthreads();
+  const int T = s_ntok, nsl = s_nsel;
+  const int Tp = (T + 31) & ~31;
+  for (int j = tid; j < nsl * kBlk; j += blockDim.x) {
+    const int k = j >> 4, t = j & 15;
+    if (t < bfill[k]) {
+      const int i = boff[k] + t;
+      const int row = (bphys[k] * KV + g) * kBlk + t;
+      trow[i] = row;
+      tks[i] = kv.ks[row];
+      tvs[i] = kv.vs[row];
+    }
+  }
+  // padding tokens [T, Tp): e = 0, f = 1 leave every recurrence unchanged
+  for (int i = T + tid; i < Tp; i += blockDim.x) tvs[i] = 0.0f;
+  __syncthreads();
+  // the group's V rows -> shared memory (hd bytes each), completing on vbar
+  {
+    const int np = hd >> 4;
+    for (int e = tid; e < T * np; e += blockDim.x) {
+      const int i = e / np, pc = e - i * np;
+      cp_async16(vraw + (size_t)i * hd + pc * 16,
+                 reinterpret_cast<const uint8_t*>(kv.vq) + (size_t)trow[i] * hd + pc * 16);
+    }
+    cp_async_arrive(&vbar);
+  }
+
+  // ------------------------------------- scores: one K row, every head
+  {
+    const int npc = hd >> 4;
+    for (int i = tid; i < T; i += blockDim.x) {
+      const int row = trow[i];
+      const uint8_t* kr = reinterpret_cast<const uint8_t*>(kv.kq) + (size_t)row * hd;
+      const int t = row & (kBlk - 1);
+      const float ksc = tks[i];
+      const uint64_t ks2 = pack2(__float_as_uint(ksc), __float_as_uint(ksc));
+#pragma unroll 1
+      for (int j0 = 0; j0 < HPG; j0 += JB) {
+        uint64_t acc[JB][4];
+#pragma unroll
+        for (int j = 0; j < JB; j++)
+#pragma unroll
+          for (int l = 0; l < 4; l++) acc[j][l] = 0;
+        for (int c = 0; c < npc; c++) {
+          // piece c of this token's row sits at (c + t) mod npc (stored rotated)
+          const uint4 u = ldg_nc16(kr + (((c + t) & (npc - 1)) << 4));
+          const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int gq = 0; gq < 4; gq++) {
+            uint64_t w01, w23;
+            decode_pairs<EC_W_INT8>(wv[gq], w01, w23);
+            w01 = mul2(w01, ks2);
+            w23 = mul2(w23, ks2);
+#pragma unroll
+            for (int j = 0; j < JB; j++) {
+              const ulonglong2 qq =
+                  reinterpret_cast<const ulonglong2*>(qs + (j0 + j) * hd + 16 * c)[gq];
+              fma2(acc[j][(2 * gq) & 3], w01, qq.x);
+              fma2(acc[j][(2 * gq + 1) & 3], w23, qq.y);
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < JB; j++) {
+          float a8[8];
+#pragma unroll
+          for (int l = 0; l < 4; l++) {
+            a8[2 * l] = lo_f(acc[j][l]);
+            a8[2 * l + 1] = hi_f(acc[j][l]);
+          }
+          sc[(j0 + j) * ld + i] = __fmul_rn(hsum8(a8), scale);
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // ------------- running max per head (threads 128j .. 128j + 127), exps
+  {
+    const int j = tid >> 7, ht = tid & 127;
+    float* scj = sc + j * ld;
+    float* sfj = sf + j * ld;
+    const int per = (T + 127) / 128;
+    const int lo = ht * per, hi = min(lo + per, T);
+    float m = -INFINITY;
+    for (int i = lo; i < hi; i++) m = (scj[i] > m) ? scj[i] : m;
+    float incl = m;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl = (t > incl) ? t : incl;
+    }
+    if (lane == 31) s_wmax[warp] = incl;
+    __syncthreads();
+    float pre = -INFINITY;
+    for (int w = j * 4; w < warp; w++) pre = (s_wmax[w] > pre) ? s_wmax[w] : pre;
+    float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (lane == 0) excl = -INFINITY;
+    float run = (excl > pre) ? excl : pre;
+    for (int i = lo; i < hi; i++) {
+      const float s = scj[i];
+      const float prev = run;
+      run = (s > prev) ? s : prev;
+      sfj[i] = fast_expf(__fsub_rn(prev, run));
+      scj[i] = fast_expf(__fsub_rn(s, run));
+    }
+    for (int i = T + ht; i < Tp; i += 128) {
+      scj[i] = 0.0f;
+      sfj[i] = 1.0f;
+    }
+  }
+  __syncthreads();
+  // flag per head per 32 tokens: every scale factor is 1
+  for (int w = tid; w < hpg * (Tp >> 5); w += blockDim.x) {
+    const int j = w / (Tp >> 5), gq = w - j * (Tp >> 5);
+    bool a1 = true;
+    for (int u = 0; u < 32; u++) a1 = a1 && (sf[j * ld + 32 * gq + u] == 1.0f);
+    ones[j * (ld / 32) + gq] = a1;
+  }
+  const bool ok = __syncthreads_and(mbar_wait(&vbar, 0, sb.err));
+
+  // --------------------------------------------------------- recurrences
+  const int q4 = hd >> 2;  // threads per head
+  const bool chainer = tid < hpg * q4 && ok;
+  const int j = tid / q4, d0 = (tid - j * q4) * 4;
+  const bool lead = d0 == 0;
+  uint64_t o01 = 0, o23 = 0;
+  if (chainer) {
+    const float* scj = sc + j * ld;
+    const float* sfj = sf + j * ld;
+    const int* onej = ones + j * (ld / 32);
+    float sum = 0.0f;
+    for (int i0 = 0; i0 < Tp; i0 += 32) {
+      const bool one = onej[i0 >> 5] != 0;
+#pragma unroll 2
+      for (int i = i0; i < i0 + 32; i += 4) {
+        const float4 e4 = *reinterpret_cast<const float4*>(scj + i);
+        const float4 t4 = *reinterpret_cast<const float4*>(tvs + i);
+        const float4 f4 = *reinterpret_cast<const float4*>(sfj + i);
+        uint32_t w[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+          w[k] = *reinterpret_cast<const uint32_t*>(vraw + (size_t)(i + k) * hd + d0);
+        const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
+        const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
+        const float fv[4] = {f4.x, f4.y, f4.z, f4.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          uint64_t v01, v23;
+          decode_pairs<EC_W_INT8>(w[k], v01, v23);
+          const uint64_t t2 = pack2(__float_as_uint(tv[k]), __float_as_uint(tv[k]));
+          v01 = mul2(v01, t2);
+          v23 = mul2(v23, t2);
+          const uint64_t e2 = pack2(__float_as_uint(ev[k]), __float_as_uint(ev[k]));
+          if (!one) {
+            const uint64_t f2 = pack2(__float_as_uint(fv[k]), __float_as_uint(fv[k]));
+            o01 = mul2(o01, f2);
+            o23 = mul2(o23, f2);
+          }
+          fma2(o01, e2, v01);
+          fma2(o23, e2, v23);
+          if (lead) sum = __fmaf_rn(sum, fv[k], ev[k]);
+        }
+      }
+    }
+    if (lead) s_sum[j] = sum;
+  }
+  __syncthreads();
+  if (chainer) {
+    const float sm = s_sum[j];
+    float r4[4] = {lo_f(o01), hi_f(o01), lo_f(o23), hi_f(o23)};
+    if (sm > 0.0f) {
+      const float inv = __fdiv_rn(1.0f, sm);
+#pragma unroll
+      for (int k = 0; k < 4; k++) r4[k] = __fmul_rn(r4[k], inv);
+    }
+    *reinterpret_cast<float4*>(sb.att + (long)b * H * hd + (long)(h0 + j) * hd + d0) =
+        make_float4(r4[0], r4[1], r4[2], r4[3]);
+  }
+}
+
 static int attn_max_tok(const KvLayout& kv, const StepBuffers& sb) {
   if (kv.paged) return kBlk * sb.sparse_blocks_k;
   return sb.sparse_k > 0 ? sb.sparse_k : kv.seq_len;
@@ -1016,6 +1320,10 @@ cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuf
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   // the largest opt-in: per-op calls share these kernels with other sizes
   cudaError_t e = opt_in_max_smem(attention_kernel<true, true>);
+  if (!e) e = opt_in_max_smem(attention_group_kernel<1>);
+  if (!e) e = opt_in_max_smem(attention_group_kernel<2>);
+  if (!e) e = opt_in_max_smem(attention_group_kernel<4>);
+  if (!e) e = opt_in_max_smem(attention_group_kernel<8>);
   if (!e) e = opt_in_max_smem(attention_kernel<false, true>);
   if (!e) e = opt_in_max_smem(attention_kernel<true, false>);
   if (!e) e = opt_in_max_smem(attention_kernel<false, false>);
@@ -1065,9 +1373,26 @@ cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const
   return launch_ex(linear_select_kernel, dim3(B), dim3(256), smem, s, pdl, kv, lsh, sb, layer);
 }
 
+bool use_group_attention(const KvLayout& kv, const StepBuffers& sb, int B) {
+  const int hpg = kv.n_heads / kv.n_kv_heads;
+  return kv.paged && B >= 4 && (hpg == 1 || hpg == 2 || hpg == 4 || hpg == 8) &&
+         group_layout(attn_max_tok(kv, sb), kv.head_dim, hpg).total <= 227 * 1024 - 256;
+}
+
 cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
                              cudaStream_t s, bool pdl) {
   const int max_tok = attn_max_tok(kv, sb);
+  if (use_group_attention(kv, sb, B)) {
+    const int hpg = kv.n_heads / kv.n_kv_heads;
+    const size_t smem = group_layout(max_tok, kv.head_dim, hpg).total;
+    const dim3 grid(kv.n_kv_heads, B), block(128 * hpg);
+    switch (hpg) {
+      case 1: return launch_ex(attention_group_kernel<1>, grid, block, smem, s, pdl, kv, sb, layer, max_tok);
+      case 2: return launch_ex(attention_group_kernel<2>, grid, block, smem, s, pdl, kv, sb, layer, max_tok);
+      case 4: return launch_ex(attention_group_kernel<4>, grid, block, smem, s, pdl, kv, sb, layer, max_tok);
+      default: return launch_ex(attention_group_kernel<8>, grid, block, smem, s, pdl, kv, sb, layer, max_tok);
+    }
+  }
   // from 4 sequences on, throughput over latency: the smaller variant
   const bool vf = B < 4;
   const size_t smem = attn_layout(max_tok, kv.head_dim, kv.paged ? 1 : 2, vf).total;

@@ -15,6 +15,7 @@
 #include "ec_internal.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
+#include "tc_gemm.cuh"
 
 static thread_local char g_err[512];
 
@@ -32,6 +33,7 @@ constexpr int kPack = 8;
 struct Mat {
   uint8_t* w = nullptr;  // packed layout (gemv_packed.cu), rows padded to a multiple of 4
   float* scale = nullptr;  // per row (INT8 and FP8 alike, FP8 expanded)
+  uint8_t* tc = nullptr;   // tensor-core layout (tc_gemm.cu) when batched steps use it
   int rows = 0, cols = 0;
 };
 
@@ -63,6 +65,10 @@ struct ec_ctx {
   int npacks = 1;            // batched-chain passes per step (max_batch / 8, rounded up)
   void* amax = nullptr;      // split-argmax partials and counters
   bool chain = false;        // one persistent GEMV kernel per layer
+  bool tc = false;           // steps of >= tensor_min_batch sequences: tensor-core GEMMs
+  int8_t* tc_digits = nullptr;
+  double* tc_sx = nullptr;
+  int* tc_ws = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
   int max_sel = 0;
   ec::PackedPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_lm{};
@@ -376,6 +382,32 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     ec_destroy(ctx);
     return fail(EC_ERR_UNSUPPORTED, "no GEMV plan for this shape");
   }
+  // tensor-core GEMMs for large batched steps (INT8, K a multiple of 128)
+  if (c.tensor_min_batch > 0 && wk == EC_W_INT8 && D % ec::kTcKb == 0 && F % ec::kTcKb == 0 &&
+      (H * hd) % ec::kTcKb == 0) {
+    ctx->tc = true;
+    const int pb = S < ec::kTcMaxRows ? S : ec::kTcMaxRows;
+    size_t wsb = 0;
+    auto tc_alloc = [&](Mat& m) -> cudaError_t {
+      cudaError_t e2 = dalloc(ctx, &m.tc, ec::tc_weight_bytes(m.rows, m.cols));
+      if (e2 == cudaSuccess) e2 = cudaMemset(m.tc, 0, ec::tc_weight_bytes(m.rows, m.cols));
+      const size_t w = ec::tc_ws_bytes(m.rows, m.cols, pb, ctx->n_sm);
+      if (w > wsb) wsb = w;
+      return e2;
+    };
+    for (int l = 0; l < L; l++) {
+      TRY(tc_alloc(ctx->qkv[l]));
+      TRY(tc_alloc(ctx->wo[l]));
+      TRY(tc_alloc(ctx->w13[l]));
+      TRY(tc_alloc(ctx->w2[l]));
+    }
+    TRY(tc_alloc(ctx->lm));
+    const int kmax = F > D ? (F > H * hd ? F : H * hd) : (D > H * hd ? D : H * hd);
+    TRY(dalloc(ctx, &ctx->tc_digits, ec::tc_digit_bytes(pb, kmax)));
+    TRY(dalloc(ctx, &ctx->tc_sx, (size_t)ec::kTcMaxRows));
+    TRY(dalloc(ctx, &ctx->tc_ws, wsb / 4));
+    TRY(ec::tc_prepare());
+  }
   {
     ec::StepBuffers sb{};
     sb.sparse_k = c.sparse_k;
@@ -429,6 +461,8 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
       d = static_cast<const uint8_t*>(tmp);
     }
     e2 = ec::packed_pack(d, m.w, m.rows, m.cols, nr, row_base, row_stride, ctx->stream);
+    if (e2 == cudaSuccess && m.tc)
+      e2 = ec::tc_pack(d, m.tc, m.rows, m.cols, nr, row_base, row_stride, ctx->stream);
     if (e2 == cudaSuccess) e2 = cudaStreamSynchronize(ctx->stream);
     if (tmp) cudaFree(tmp);
     return e2;
@@ -703,8 +737,136 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   return cudaSuccess;
 }
 
+// The batched step on the tensor cores (B >= tensor_min_batch, INT8): the
+// sequence-parallel kernels as in enqueue_step_batched; every projection is
+// tc_quant (RMSNorm when the reference has one, digit planes) -> tc_gemm
+// (tcgen05, whole tiles finished in its epilogue) -> tc_combine (tiles split
+// between CTAs), per pass of up to kTcMaxRows sequences.
+cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback) {
+  const ec_model_config& c = ctx->c;
+  const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
+  const int V = c.vocab_size, L = c.n_layers, QW = (H + 2 * KV) * hd;
+  cudaError_t e;
+  ctx->launches = 0;
+  ec::StepBuffers sb{};
+  sb.rope_cos = ctx->rope_cos;
+  sb.rope_sin = ctx->rope_sin;
+  sb.sparse_k = c.sparse_k;
+  sb.window = c.window;
+  sb.sparse_blocks_k = c.sparse_blocks_k;
+  sb.err = ctx->err;
+  sb.max_sel = ctx->max_sel;
+  sb.pos = pos;
+  sb.qkv = ctx->qkvb;
+  sb.qrot = ctx->qrot;
+  sb.att = ctx->att;
+  sb.sel = ctx->sel;
+  sb.nsel = ctx->nsel;
+  // one projection of nb rows: x [nb][K] (x_stride apart) -> y per epi
+  auto proj = [&](const Mat& m, const float* x, int xs, const uint16_t* nw, float* y, int ys,
+                  int epi, int nb) -> cudaError_t {
+    ec::TcQuant q{};
+    q.x = x;
+    q.x_stride = xs;
+    q.norm_w = nw;
+    q.eps = c.norm_eps;
+    q.digits = ctx->tc_digits;
+    q.sx = ctx->tc_sx;
+    q.B = nb;
+    q.K = m.cols;
+    ec::TcGemm g{};
+    g.w = m.tc;
+    g.digits = ctx->tc_digits;
+    g.ws = ctx->tc_ws;
+    g.N = m.rows;
+    g.K = m.cols;
+    g.B = nb;
+    g.grid = ctx->n_sm;
+    g.err = ctx->err;
+    g.out.sx = ctx->tc_sx;
+    g.out.scale = m.scale;
+    g.out.y = y;
+    g.out.y_stride = ys;
+    g.out.epi = epi;
+    g.out.silu_vec_limit = (m.rows / 2) & ~7;
+    cudaError_t e2;
+    {
+      ProfScope ps(ctx, EC_K_TC_AUX, 4.0 * nb * m.cols + (double)ec::tc_digit_bytes(nb, m.cols));
+      if ((e2 = ec::tc_quant(q, ctx->stream, true))) return e2;
+    }
+    {
+      ProfScope ps(ctx, EC_K_TC_GEMM, (double)m.rows * m.cols + 4.0 * m.rows);
+      if ((e2 = ec::tc_gemm(g, ctx->stream, true))) return e2;
+    }
+    ProfScope ps(ctx, EC_K_TC_AUX, 0.0);
+    ctx->launches += 3;
+    return ec::tc_combine(g, ctx->stream, true);
+  };
+  {
+    ProfScope ps(ctx, EC_K_EMBED, (2.0 + 4.0) * D * B);
+    if ((e = ec::launch_embed(ctx->emb, tokens, ctx->x, D, c.vocab_size, B, ctx->stream, true)))
+      return e;
+    ctx->launches++;
+  }
+  for (int b0 = 0; b0 < B; b0 += ec::kTcMaxRows) {
+    const int nb = B - b0 < ec::kTcMaxRows ? B - b0 : ec::kTcMaxRows;
+    if ((e = proj(ctx->qkv[0], ctx->x + (size_t)b0 * D, D, ctx->attn_norm[0],
+                  ctx->qkvb + (size_t)b0 * QW, QW, ec::EPI_STORE, nb)))
+      return e;
+  }
+  for (int l = 0; l < L; l++) {
+    {
+      ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
+      if ((e = ec::launch_kv_append(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
+      ctx->launches++;
+    }
+    if (!ctx->kv.paged) {
+      ProfScope ps(ctx, EC_K_SELECT, 0.0);
+      if ((e = ec::launch_linear_select(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
+      ctx->launches++;
+    }
+    {
+      ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
+      if ((e = ec::launch_attention(ctx->kv, sb, l, B, ctx->stream, true))) return e;
+      ctx->launches++;
+    }
+    const bool last = l + 1 == L;
+    for (int b0 = 0; b0 < B; b0 += ec::kTcMaxRows) {
+      const int nb = B - b0 < ec::kTcMaxRows ? B - b0 : ec::kTcMaxRows;
+      float* x = ctx->x + (size_t)b0 * D;
+      float* hb = ctx->hbuf + (size_t)b0 * F;
+      const float* att = ctx->att + (size_t)b0 * H * hd;
+      if ((e = proj(ctx->wo[l], att, H * hd, nullptr, x, D, ec::EPI_RESID, nb))) return e;
+      if ((e = proj(ctx->w13[l], x, D, ctx->ffn_norm[l], hb, F, ec::EPI_SWIGLU, nb))) return e;
+      if ((e = proj(ctx->w2[l], hb, F, nullptr, x, D, ec::EPI_RESID, nb))) return e;
+      if (last)
+        e = proj(ctx->lm, x, D, ctx->final_norm, ctx->logits + (size_t)b0 * V, V, ec::EPI_STORE, nb);
+      else
+        e = proj(ctx->qkv[l + 1], x, D, ctx->attn_norm[l + 1], ctx->qkvb + (size_t)b0 * QW, QW,
+                 ec::EPI_STORE, nb);
+      if (e) return e;
+    }
+  }
+  {
+    ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
+    for (int b = 0; b < B; b++) {
+      if ((e = ec::launch_argmax_split(ctx->logits + (size_t)b * V, V, 1, ctx->argmax + b,
+                                       feedback ? const_cast<int*>(tokens) + b : nullptr,
+                                       feedback ? const_cast<int*>(pos) + b : nullptr,
+                                       static_cast<uint8_t*>(ctx->amax) +
+                                           (size_t)b * ec::argmax_scratch_bytes(1),
+                                       ctx->stream, true)))
+        return e;
+      ctx->launches++;
+    }
+  }
+  return cudaSuccess;
+}
+
 // Enqueue one decode step for B sequences (tokens/pos in device memory).
 cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback) {
+  if (ctx->tc && B >= ctx->c.tensor_min_batch)
+    return enqueue_step_tc(ctx, tokens, pos, B, feedback);
   if (ctx->chain && B > 1) return enqueue_step_batched(ctx, tokens, pos, B, feedback);
   const ec_model_config& c = ctx->c;
   const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
@@ -965,6 +1127,12 @@ extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
   // down -- or with the chain: append, [select], attention, chain -- then
   // [LM head] and argmax
   const int sel = ctx->kv.paged ? 0 : 1;
+  if (ctx->tc && B >= ctx->c.tensor_min_batch) {
+    // embed, per pass QKV(0) (quant, GEMM, combine), per layer append,
+    // [select], attention and 4 projections per pass, argmax per sequence
+    const int passes = (B + ec::kTcMaxRows - 1) / ec::kTcMaxRows;
+    return 1 + 3 * passes + ctx->c.n_layers * (2 + sel + 12 * passes) + B;
+  }
   if (ctx->chain && B > 1) {
     const int packs = (B + kPack - 1) / kPack;
     return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + B;

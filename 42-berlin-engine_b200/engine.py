@@ -32,9 +32,10 @@ EXPORTS = [
     "ec_transformer_forward", "ec_transformer_argmax", "ec_transformer_reset",
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read", "ec_lsh_attn_create",
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
+    "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
-           "attention", "embed", "argmax", "gemv_chain"]
+           "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_aux"]
 
 
 class ModelConfig(C.Structure):
@@ -44,7 +45,7 @@ class ModelConfig(C.Structure):
         (n, C.c_int) for n in (
             "weight_kind", "use_paged_kv", "sparse_k", "window", "sparse_blocks_k",
             "lsh_tables", "lsh_bits", "lsh_unit", "lsh_max_units", "lsh_radius",
-            "lsh_max_cand", "max_batch")]
+            "lsh_max_cand", "max_batch", "tensor_min_batch")]
 
 
 class Transformer(C.Structure):
@@ -94,6 +95,9 @@ def lib():
             "ec_op_gemv": (i, [i, vp, vp, vp, vp, i, i, vp]),
             "ec_gemv_packed_bytes": (C.c_size_t, [i, i]),
             "ec_gemv_pack": (i, [vp, vp, i, i, vp]),
+            "ec_gemm_tc_bytes": (C.c_size_t, [i, i]),
+            "ec_gemm_tc_pack": (i, [vp, vp, i, i, vp]),
+            "ec_op_gemm_tc": (i, [vp, vp, vp, vp, i, i, i, vp]),
             "ec_op_gemv_packed": (i, [i, vp, vp, vp, vp, i, i, vp]),
             "ec_op_gemv_packed_batch": (i, [i, vp, vp, vp, vp, i, i, i, vp]),
             "ec_op_rmsnorm": (i, [vp, vp, vp, i, f, vp]),

@@ -63,7 +63,16 @@ def run_case(torch, eng, kind, n, k, args, peak):
     sptr = sc.data_ptr() if sc is not None else None
 
     op = L.ec_op_gemv
-    if args.layout == "packed" and kind != "bf16":
+    if args.layout == "tc":
+        # tensor-core layout (INT8 only): ec_op_gemm_tc = digit planes +
+        # tcgen05 GEMM + combine, synchronised at the end of every call
+        pk = []
+        for w_ in ws:
+            dst = torch.zeros(L.ec_gemm_tc_bytes(n, k), dtype=torch.uint8, device=dev)
+            eng.check(L.ec_gemm_tc_pack(w_.data_ptr(), dst.data_ptr(), n, k, stream.cuda_stream))
+            pk.append(dst)
+        ws = pk
+    elif args.layout == "packed" and kind != "bf16":
         # the decode step's layout: repack each copy once, outside the timing
         op = L.ec_op_gemv_packed
         pk = []
@@ -74,7 +83,10 @@ def run_case(torch, eng, kind, n, k, args, peak):
         ws = pk
 
     def run(i):
-        if nb == 1:
+        if args.layout == "tc":
+            eng.check(L.ec_op_gemm_tc(ws[i % copies].data_ptr(), sptr, x.data_ptr(), y.data_ptr(),
+                                      n, k, nb, stream.cuda_stream))
+        elif nb == 1:
             eng.check(op(wk, ws[i % copies].data_ptr(), sptr, x.data_ptr(), y.data_ptr(),
                          n, k, stream.cuda_stream))
         else:
@@ -107,8 +119,9 @@ def main():
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", default="1", help="activation vectors per call, e.g. 1,8,64,512")
-    ap.add_argument("--layout", default="packed", choices=["packed", "rowmajor"],
-                    help="packed: the decode step's kernel; rowmajor: ec_op_gemv")
+    ap.add_argument("--layout", default="packed", choices=["packed", "rowmajor", "tc"],
+                    help="packed: the decode step's kernel; rowmajor: ec_op_gemv; "
+                         "tc: the tensor-core GEMM (INT8)")
     ap.add_argument("--l2-bytes", type=float, default=512e6, help="bytes of weight copies rotated")
     args = ap.parse_args()
     eng = _load("engine")
@@ -120,7 +133,9 @@ def main():
         for shp in args.shapes.split(","):
             n, k = (int(v) for v in shp.split("x"))
             for nb in (int(v) for v in args.batch.split(",")):
-                if nb > 1 and (args.layout != "packed" or kind == "bf16"):
+                if args.layout == "tc" and kind != "int8":
+                    continue
+                if nb > 1 and (args.layout == "rowmajor" or kind == "bf16"):
                     continue
                 args.batch_now = nb
                 print(json.dumps(run_case(torch, eng, kind, n, k, args, peak)), flush=True)

@@ -196,7 +196,8 @@ def run_cuda(args):
     S = _load("synth")
     cfg = S.LLAMA3_8B
     B = args.batch
-    e = eng.Engine(cfg, device=local, max_batch=B)
+    tmb = args.tensor_min_batch if B >= args.tensor_min_batch > 0 else 0
+    e = eng.Engine(cfg, device=local, max_batch=B, tensor_min_batch=tmb)
     src = S.DeviceModel(cfg, seed=SEED, device=local)
 
     def sink(kind, layer, name, t, s):
@@ -296,6 +297,7 @@ def run_cuda(args):
             "config": {"workload": f"llama3-8b-shape decode b={B} per GPU", "global_batch": ws * B,
                        "context": args.prompt, "weights": "int8 per-row pow2 scale",
                        "kv": "paged int8", "parallelism": f"dp{ws} (replicas)",
+                       "gemm": "tcgen05 int8 (digit planes)" if tmb else "cuda-core gemv chain",
                        "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"},
             "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B * (cfg.vocab_size + 1)},
@@ -344,6 +346,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="tokens already in the cache")
     ap.add_argument("--batch", type=int, default=1,
                     help="sequences decoded together per GPU (b=64: the batched metric)")
+    ap.add_argument("--tensor-min-batch", type=int, default=16,
+                    help="batches this large run their GEMMs on the tensor cores (0: never)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

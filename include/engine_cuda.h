@@ -80,6 +80,10 @@ typedef struct ec_model_config
 	int		lsh_radius;		/* LSH_HAMMING_RADIUS (ops_lsh.h:37) */
 	int		lsh_max_cand;	/* candidate units per query (inference.c:300) */
 	int		max_batch;		/* sequences per decode step */
+	int		tensor_min_batch;	/* INT8 steps of at least this many sequences run
+							** their GEMMs on the tensor cores (ec_op_gemm_tc
+							** arithmetic: deterministic, not bit-identical
+							** to the reference); 0 = never (default) */
 }	ec_model_config;
 
 typedef struct ec_ctx	ec_ctx;
@@ -142,7 +146,9 @@ int		ec_synchronize(ec_ctx *ctx);
 # define EC_K_EMBED 8
 # define EC_K_ARGMAX 9
 # define EC_K_GEMV_CHAIN 10	/* one layer's o, gate/up, down (+ next QKV / LM head) */
-# define EC_K_COUNT 11
+# define EC_K_TC_GEMM 11	/* tensor-core GEMM (batched steps) */
+# define EC_K_TC_AUX 12		/* its digit planes and split-tile combine */
+# define EC_K_COUNT 13
 int		ec_profile_enable(ec_ctx *ctx, int on);
 int		ec_profile_read(ec_ctx *ctx, int kind, double *ms, int *launches,
 			double *bytes);
@@ -183,6 +189,22 @@ int		ec_gemv_pack(const void *w_rowmajor, void *w_packed, int m, int k,
 			void *stream);
 int		ec_op_gemv_packed(int wkind, const void *w_packed, const float *scale,
 			const float *x, float *y, int m, int k, void *stream);
+
+/* op_matmul (src/compute/ops.h:33) for nb activation rows at once on the
+** tensor cores, INT8 weights only (the large-batch decode and prefill path;
+** the reference runs op_matmul once per row).  ec_gemm_tc_bytes gives the
+** size of an m x k matrix in the tensor-core layout (128-row tiles; k a
+** multiple of 128), ec_gemm_tc_pack fills it from row-major INT8 device
+** weights, and ec_op_gemm_tc computes y [nb][m] = scale . (W x) for x [nb][k]
+** (device).  Each x row is rounded to 21-bit fixed point against its own
+** max |x| (relative error <= 2^-22 of that max), multiplied exactly in int32
+** and scaled once: not bit-identical to ec_op_gemv, but deterministic and
+** independent of the launch.  Scratch comes from the stream-ordered
+** allocator; k <= 51200. */
+size_t	ec_gemm_tc_bytes(int m, int k);
+int		ec_gemm_tc_pack(const void *w_rowmajor, void *w_tc, int m, int k, void *stream);
+int		ec_op_gemm_tc(const void *w_tc, const float *scale, const float *x, float *y,
+			int m, int k, int nb, void *stream);
 
 /* op_rmsnorm (src/compute/ops.h:34, ops_norm.c:126); out may alias x. */
 int		ec_op_rmsnorm(float *out, const float *x, const uint16_t *w, int n,

@@ -400,3 +400,26 @@ def test_batched_chain_matches_oracle(eng, torch, oracle, synth, B):
                 assert np.array_equal(bits(lg[b]), bits(want)), f"step {t} sequence {b}"
                 assert am[b] == oracle.port().port_argmax(want, want.size)
     e.close()
+
+
+def test_group_attention_hd128_sparse(eng, torch, oracle, synth):
+    """Batched steps (B >= 4) run one attention CTA per (KV head, sequence)
+    for all query heads of the group.  Llama-like geometry (4 query heads per
+    KV head, head_dim 128), past SPARSE_BLOCKS_K blocks so the block-sparse
+    order matters: every checked step's logits bit-identical per sequence."""
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=4, n_kv_heads=1,
+                            vocab_size=2048, seq_len=2048, head_dim=128, rope_theta=5e5)
+    model = synth.make_model(cfg, seed=31)
+    B = 4
+    e = eng.Engine(cfg, max_batch=B)
+    e.load(model)
+    pms = [oracle.PortModel(model) for _ in range(B)]
+    prompts = [synth.prompt(cfg, 1060, seed=80 + b) for b in range(B)]
+    for t in range(1060):
+        check = t % 100 == 0 or t >= 1050
+        lg, _ = e.step([int(p[t]) for p in prompts], [t] * B, want_logits=check)
+        for b in range(B):
+            want = pms[b].forward(int(prompts[b][t]), t)
+            if check:
+                assert np.array_equal(bits(lg[b]), bits(want)), f"step {t} sequence {b}"
+    e.close()
