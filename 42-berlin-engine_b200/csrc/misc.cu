@@ -206,13 +206,17 @@ constexpr int kArgParts = 32;
 
 __global__ void __launch_bounds__(256) argmax_split_kernel(const float* __restrict__ logits,
                                                            int n, int* __restrict__ out,
-                                                           int* tokens, int* pos, float* pv,
-                                                           int* pi, int* ctr) {
+                                                           int* tokens, int* pos,
+                                                           uint8_t* scratch) {
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.y, p = blockIdx.x, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const float* x = logits + (long)b * n;
+  // sequence b's slice of the scratch: partial values, indices, counter
+  float* pv = reinterpret_cast<float*>(scratch + (size_t)b * (kArgParts * 8 * 8 + 4));
+  int* pi = reinterpret_cast<int*>(pv + kArgParts * 8);
+  int* ctr = pi + kArgParts * 8;
   const int n8 = n & ~7;
   const int per = ((n8 / kArgParts) + 7) & ~7;
   const int lo = min(n8, p * per), hi = min(n8, lo + per);
@@ -242,8 +246,8 @@ __global__ void __launch_bounds__(256) argmax_split_kernel(const float* __restri
     s_i[warp][lane] = bi;
   }
   __syncthreads();
-  float* gv = pv + ((long)b * kArgParts + p) * 8;
-  int* gi = pi + ((long)b * kArgParts + p) * 8;
+  float* gv = pv + p * 8;
+  int* gi = pi + p * 8;
   if (tid < 8) {
     float v = s_v[0][tid];
     int i = s_i[0][tid];
@@ -261,14 +265,14 @@ __global__ void __launch_bounds__(256) argmax_split_kernel(const float* __restri
   __syncthreads();
   if (tid == 0) {
     __threadfence();
-    s_last = atomicAdd(ctr + b, 1) == kArgParts - 1;
+    s_last = atomicAdd(ctr, 1) == kArgParts - 1;
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   if (tid < 8) {
-    const float* av = pv + (long)b * kArgParts * 8;
-    const int* ai = pi + (long)b * kArgParts * 8;
+    const float* av = pv;
+    const int* ai = pi;
     float v = -INFINITY;
     int i = 0x7fffffff;
     for (int q = 0; q < kArgParts; q++) {
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(256) argmax_split_kernel(const float* __restri
   }
   __syncthreads();
   if (tid == 0) {
-    ctr[b] = 0;
+    ctr[0] = 0;
     float best = s_v[0][0];
     int idx = s_i[0][0];
     for (int l = 1; l < 8; l++)
@@ -303,14 +307,12 @@ __global__ void __launch_bounds__(256) argmax_split_kernel(const float* __restri
   }
 }
 
-size_t argmax_scratch_bytes(int B) { return (size_t)B * kArgParts * 8 * 8 + (size_t)B * 4; }
+// per sequence: kArgParts x 8 partial values and indices, one counter
+size_t argmax_scratch_bytes(int B) { return (size_t)B * (kArgParts * 8 * 8 + 4); }
 
 cudaError_t launch_argmax_split(const float* logits, int n, int B, int* out, int* tokens,
                                 int* pos, void* scratch, cudaStream_t s, bool pdl) {
   if (n < 8 * kArgParts) return launch_argmax(logits, n, B, out, tokens, pos, s, pdl);
-  float* pv = static_cast<float*>(scratch);
-  int* pi = reinterpret_cast<int*>(pv + (size_t)B * kArgParts * 8);
-  int* ctr = pi + (size_t)B * kArgParts * 8;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kArgParts, B);
   cfg.blockDim = dim3(256);
@@ -320,7 +322,8 @@ cudaError_t launch_argmax_split(const float* logits, int n, int B, int* out, int
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, argmax_split_kernel, logits, n, out, tokens, pos, pv, pi, ctr);
+  return cudaLaunchKernelEx(&cfg, argmax_split_kernel, logits, n, out, tokens, pos,
+                            static_cast<uint8_t*>(scratch));
 }
 
 cudaError_t launch_argmax(const float* logits, int n, int B, int* out, int* tokens, int* pos,

@@ -723,16 +723,13 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   }
   {
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
-    for (int b = 0; b < B; b++) {
-      if ((e = ec::launch_argmax_split(ctx->logits + (size_t)b * V, V, 1, ctx->argmax + b,
-                                       feedback ? const_cast<int*>(tokens) + b : nullptr,
-                                       feedback ? const_cast<int*>(pos) + b : nullptr,
-                                       static_cast<uint8_t*>(ctx->amax) +
-                                           (size_t)b * ec::argmax_scratch_bytes(1),
-                                       ctx->stream, true)))
-        return e;
-      ctx->launches++;
-    }
+    // one launch for all B sequences (scratch slice b per sequence)
+    if ((e = ec::launch_argmax_split(ctx->logits, V, B, ctx->argmax,
+                                     feedback ? const_cast<int*>(tokens) : nullptr,
+                                     feedback ? const_cast<int*>(pos) : nullptr, ctx->amax,
+                                     ctx->stream, true)))
+      return e;
+    ctx->launches++;
   }
   return cudaSuccess;
 }
@@ -791,14 +788,14 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
     g.out.silu_vec_limit = (m.rows / 2) & ~7;
     cudaError_t e2;
     {
-      ProfScope ps(ctx, EC_K_TC_AUX, 4.0 * nb * m.cols + (double)ec::tc_digit_bytes(nb, m.cols));
+      ProfScope ps(ctx, EC_K_TC_QUANT, 4.0 * nb * m.cols + (double)ec::tc_digit_bytes(nb, m.cols));
       if ((e2 = ec::tc_quant(q, ctx->stream, true))) return e2;
     }
     {
       ProfScope ps(ctx, EC_K_TC_GEMM, (double)m.rows * m.cols + 4.0 * m.rows);
       if ((e2 = ec::tc_gemm(g, ctx->stream, true))) return e2;
     }
-    ProfScope ps(ctx, EC_K_TC_AUX, 0.0);
+    ProfScope ps(ctx, EC_K_TC_COMBINE, 0.0);
     ctx->launches += 3;
     return ec::tc_combine(g, ctx->stream, true);
   };
@@ -849,16 +846,13 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
   }
   {
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
-    for (int b = 0; b < B; b++) {
-      if ((e = ec::launch_argmax_split(ctx->logits + (size_t)b * V, V, 1, ctx->argmax + b,
-                                       feedback ? const_cast<int*>(tokens) + b : nullptr,
-                                       feedback ? const_cast<int*>(pos) + b : nullptr,
-                                       static_cast<uint8_t*>(ctx->amax) +
-                                           (size_t)b * ec::argmax_scratch_bytes(1),
-                                       ctx->stream, true)))
-        return e;
-      ctx->launches++;
-    }
+    // one launch for all B sequences (scratch slice b per sequence)
+    if ((e = ec::launch_argmax_split(ctx->logits, V, B, ctx->argmax,
+                                     feedback ? const_cast<int*>(tokens) : nullptr,
+                                     feedback ? const_cast<int*>(pos) : nullptr, ctx->amax,
+                                     ctx->stream, true)))
+      return e;
+    ctx->launches++;
   }
   return cudaSuccess;
 }
@@ -1131,11 +1125,11 @@ extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
     // embed, per pass QKV(0) (quant, GEMM, combine), per layer append,
     // [select], attention and 4 projections per pass, argmax per sequence
     const int passes = (B + ec::kTcMaxRows - 1) / ec::kTcMaxRows;
-    return 1 + 3 * passes + ctx->c.n_layers * (2 + sel + 12 * passes) + B;
+    return 1 + 3 * passes + ctx->c.n_layers * (2 + sel + 12 * passes) + 1;
   }
   if (ctx->chain && B > 1) {
     const int packs = (B + kPack - 1) / kPack;
-    return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + B;
+    return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + 1;
   }
   if (ctx->chain) return B * (2 + ctx->c.n_layers * (3 + sel) + 1);
   return B * (1 + ctx->c.n_layers * (6 + sel) + 2);

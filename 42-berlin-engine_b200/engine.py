@@ -35,7 +35,7 @@ EXPORTS = [
     "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
-           "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_aux"]
+           "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
 
 
 class ModelConfig(C.Structure):

@@ -147,8 +147,9 @@ int		ec_synchronize(ec_ctx *ctx);
 # define EC_K_ARGMAX 9
 # define EC_K_GEMV_CHAIN 10	/* one layer's o, gate/up, down (+ next QKV / LM head) */
 # define EC_K_TC_GEMM 11	/* tensor-core GEMM (batched steps) */
-# define EC_K_TC_AUX 12		/* its digit planes and split-tile combine */
-# define EC_K_COUNT 13
+# define EC_K_TC_QUANT 12	/* its input rows -> digit planes (RMSNorm fused) */
+# define EC_K_TC_COMBINE 13	/* its tiles split between CTAs -> outputs */
+# define EC_K_COUNT 14
 int		ec_profile_enable(ec_ctx *ctx, int on);
 int		ec_profile_read(ec_ctx *ctx, int kind, double *ms, int *launches,
 			double *bytes);

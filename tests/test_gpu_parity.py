@@ -388,7 +388,7 @@ def test_batched_chain_matches_oracle(eng, torch, oracle, synth, B):
     e = eng.Engine(cfg, max_batch=B)
     e.load(model)
     packs = (B + 7) // 8
-    assert e.launches_per_step(B) == 1 + packs + 2 * (2 + packs) + B
+    assert e.launches_per_step(B) == 1 + packs + 2 * (2 + packs) + 1
     pms = [oracle.PortModel(model) for _ in range(B)]
     prompts = [synth.prompt(cfg, 70, seed=40 + b) for b in range(B)]
     for t in range(70):

@@ -109,7 +109,7 @@ def test_tensor_core_decode_matches_oracle(eng, torch, oracle, synth, B, steps):
     e = eng.Engine(cfg, max_batch=B, tensor_min_batch=16)
     e.load(model)
     passes = (B + 79) // 80
-    assert e.launches_per_step(B) == 1 + 3 * passes + 2 * (2 + 12 * passes) + B
+    assert e.launches_per_step(B) == 1 + 3 * passes + 2 * (2 + 12 * passes) + 1
     pms = [oracle.PortModel(model) for _ in range(B)]
     prompts = [synth.prompt(cfg, 8, seed=60 + b) for b in range(B)]
     toks = [int(p[0]) for p in prompts]
