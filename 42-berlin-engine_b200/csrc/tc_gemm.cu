@@ -275,19 +275,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Tiles split between CTAs: CTA i finishes the tile in which GEMM CTA i
-// starts, when that start is inside the tile and no earlier CTA starts inside
-// it too.  Thread (r, grp) owns row tile * 128 + r for sequences grp, grp + 4 ..
-constexpr int kCombGroups = 4;
+// Tiles split between CTAs: CTA (i, y) finishes sequences 4y .. 4y + 3 of
+// the tile in which GEMM CTA i starts, when that start is inside the tile and
+// no earlier CTA starts inside it too.  Thread r owns row tile * 128 + r; its
+// loads of one segment are independent, so a CTA waits about one memory
+// round trip per segment.
+constexpr int kCombSeq = 4;
 
-__global__ void __launch_bounds__(kTcRows * kCombGroups) tc_combine_kernel(TcGemm g, int NP,
-                                                                           int maxseg) {
+__global__ void __launch_bounds__(kTcRows) tc_combine_kernel(TcGemm g, int NP, int maxseg) {
   pdl_wait();
   pdl_launch_dependents();
   const int Kb = g.K / kTcKb;
   const long W = (long)((g.N + kTcRows - 1) / kTcRows) * Kb;
   const int G = g.grid < W ? g.grid : (int)W;
-  const int i = blockIdx.x, r = threadIdx.x & (kTcRows - 1), grp = threadIdx.x / kTcRows;
+  const int i = blockIdx.x, r = threadIdx.x, b0 = blockIdx.y * kCombSeq;
   if (i == 0) return;
   const long si = unit_start(i, W, G);
   const long t = si / Kb, ub = t * Kb, ue = ub + Kb;
@@ -295,31 +296,26 @@ __global__ void __launch_bounds__(kTcRows * kCombGroups) tc_combine_kernel(TcGem
   const int n = (int)t * kTcRows + r;
   const int Bp = tc_bpad(g.B);
   const float sc = n < g.N ? g.out.scale[n] : 0.0f;
-  // this tile's partial sums: CTAs i - 1, i, ... while they start inside it;
-  // all of this thread's sequences accumulate in registers segment by
-  // segment, so the loads of a segment are independent of each other
-  constexpr int kPer = (kTcMaxRows + kCombGroups - 1) / kCombGroups;
-  long long tot[kPer];
+  long long tot[kCombSeq];
 #pragma unroll
-  for (int k = 0; k < kPer; k++) tot[k] = 0;
+  for (int k = 0; k < kCombSeq; k++) tot[k] = 0;
+  // this tile's partial sums: CTAs i - 1, i, ... while they start inside it
   for (int j = i - 1; j < G; j++) {
     const long sj = unit_start(j, W, G);
     if (sj >= ue) break;
     const int* p = g.ws + ((size_t)(j * maxseg + (int)(t - sj / Kb)) * NP) * kTcRows + r;
 #pragma unroll
-    for (int k = 0; k < kPer; k++) {
-      const int b = grp + k * kCombGroups;
+    for (int k = 0; k < kCombSeq; k++) {
+      const int b = b0 + k;
       if (b < g.B)
-        tot[k] += (long long)__ldg(p + (size_t)b * kTcRows) * 16384 +
-                  (long long)__ldg(p + (size_t)(Bp + b) * kTcRows) * 128 +
-                  (long long)__ldg(p + (size_t)(2 * Bp + b) * kTcRows);
+        tot[k] += (long long)__ldcg(p + (size_t)b * kTcRows) * 16384 +
+                  (long long)__ldcg(p + (size_t)(Bp + b) * kTcRows) * 128 +
+                  (long long)__ldcg(p + (size_t)(2 * Bp + b) * kTcRows);
     }
   }
 #pragma unroll
-  for (int k = 0; k < kPer; k++) {
-    const int b = grp + k * kCombGroups;
-    if (b < g.B) emit(g.out, g.N, n, b, finish(tot[k], g.out.sx[b], sc));
-  }
+  for (int k = 0; k < kCombSeq; k++)
+    if (b0 + k < g.B) emit(g.out, g.N, n, b0 + k, finish(tot[k], g.out.sx[b0 + k], sc));
 }
 
 // One CTA per sequence: (RMSNorm,) max |x|, digit planes.
@@ -478,7 +474,8 @@ cudaError_t tc_combine(const TcGemm& g, cudaStream_t s, bool pdl) {
   const int Kb = g.K / kTcKb;
   const long W = (long)((g.N + kTcRows - 1) / kTcRows) * Kb;
   const int G = g.grid < W ? g.grid : (int)W;
-  return launch_ex(tc_combine_kernel, dim3(G), dim3(kTcRows * kCombGroups), 0, s, pdl, g, tc_np(g.B),
+  return launch_ex(tc_combine_kernel, dim3(G, (g.B + kCombSeq - 1) / kCombSeq), dim3(kTcRows), 0,
+                   s, pdl, g, tc_np(g.B),
                    max_segments(W, G, Kb));
 }
 

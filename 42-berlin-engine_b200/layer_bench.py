@@ -3,7 +3,7 @@ but few layers and a small vocabulary (a small case for profilers: a few
 hundred MB on the device).
 
   python 42-berlin-engine_b200/layer_bench.py [--layers 2] [--prompt 2048]
-        [--steps 20] [--paged 1] [--vocab 4096]
+        [--steps 20] [--paged 1] [--vocab 4096] [--batch 1] [--tensor-min-batch 16]
 
 Prints one JSON line: ms per step (graph replay, CUDA events) and the
 per-kernel device time from the library's profiling mode.
@@ -51,40 +51,45 @@ def main():
     ap.add_argument("--paged", type=int, default=1)
     ap.add_argument("--vocab", type=int, default=4096)
     ap.add_argument("--sparse-k", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=1, help="sequences per step")
+    ap.add_argument("--tensor-min-batch", type=int, default=16)
     args = ap.parse_args()
+    B = args.batch
     eng, S = _load("engine"), _load("synth")
     base = S.LLAMA3_8B
     cfg = S.ModelConfig(dim=base.dim, hidden_dim=base.hidden_dim, n_layers=args.layers,
                         n_heads=base.n_heads, n_kv_heads=base.n_kv_heads,
                         vocab_size=args.vocab, seq_len=base.seq_len, head_dim=base.head_dim,
                         rope_theta=base.rope_theta)
-    e = eng.Engine(cfg, use_paged_kv=bool(args.paged), sparse_k=args.sparse_k)
+    tmb = args.tensor_min_batch if B >= args.tensor_min_batch > 0 else 0
+    e = eng.Engine(cfg, use_paged_kv=bool(args.paged), sparse_k=args.sparse_k, max_batch=B,
+                   tensor_min_batch=tmb)
     load_device_model(eng, e, S.DeviceModel(cfg, seed=3, device=0))
     torch.cuda.synchronize()
-    toks = S.prompt(cfg, args.prompt, seed=5)
+    toks = [S.prompt(cfg, args.prompt, seed=5 + b) for b in range(B)]
     for p in range(args.prompt):
-        _, am = e.step([toks[p]], [p], want_logits=False)
-    tok = torch.tensor([int(am[0])], dtype=torch.int32, device="cuda")
-    pos = torch.tensor([args.prompt], dtype=torch.int32, device="cuda")
+        _, am = e.step([t[p] for t in toks], [p] * B, want_logits=False)
+    tok = torch.tensor([int(a) for a in am], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([args.prompt] * B, dtype=torch.int32, device="cuda")
     stream = torch.cuda.ExternalStream(e.stream())
     for _ in range(3):
-        e.step_device(tok.data_ptr(), pos.data_ptr(), 1, True)
+        e.step_device(tok.data_ptr(), pos.data_ptr(), B, True)
     e.sync()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     ev[0].record(stream)
     for _ in range(args.steps):
-        e.step_device(tok.data_ptr(), pos.data_ptr(), 1, True)
+        e.step_device(tok.data_ptr(), pos.data_ptr(), B, True)
     ev[1].record(stream)
     e.sync()
     ms = ev[0].elapsed_time(ev[1]) / args.steps
     e.profile(True)
-    cur, p = int(tok.item()), int(pos.item())
+    cur, p = [int(v) for v in tok.cpu()], int(pos[0].item())
     for _ in range(3):
-        _, am = e.step([cur], [p], want_logits=False)
-        cur, p = int(am[0]), p + 1
+        _, am = e.step(cur, [p] * B, want_logits=False)
+        cur, p = [int(a) for a in am], p + 1
     prof = e.profile_read()
     e.profile(False)
-    out = {"layers": args.layers, "context": args.prompt, "paged": args.paged,
+    out = {"layers": args.layers, "context": args.prompt, "paged": args.paged, "batch": B,
            "ms_per_step": round(ms, 4),
            "us_per_launch": {k: round(v["ms"] * 1e3 / v["launches"], 2)
                              for k, v in prof.items() if v["launches"]},
