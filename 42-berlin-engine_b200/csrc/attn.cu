@@ -90,8 +90,10 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim, half = hd >> 1;
   pdl_launch_dependents();
   pdl_wait();
+  PHASE_MARK(tid == 0 && layer == 1 && b == 0, 4 + blockIdx.x);
   if (blockIdx.x == 1) {
     paged_select_cta(kv, sb, layer, b);
+    PHASE_MARK(tid == 0 && layer == 1 && b == 0, 3);
     return;
   }
   const int pos = step_pos(sb, b);
@@ -199,6 +201,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
       meta[0] = count;
     }
   }
+  PHASE_MARK(tid == 0 && layer == 1 && b == 0, 6);
 }
 
 // ------------------------------------------------------------------------
