@@ -72,11 +72,60 @@ __device__ __forceinline__ void hnode_down(uint2* hp, float v, int vi) {
   hp[n] = make_uint2(__float_as_uint(v), (unsigned)vi);
 }
 
+// The same two operations run by a whole warp, for heaps of at most 63
+// nodes (D <= 6): the path an operation walks is found in parallel, then
+// every node on it moves in one store.
+//   up: lane k loads the (k+1)-th ancestor of position n; the ancestors
+//   before the first one that is not greater than v each move one level
+//   down, and v lands above them.
+//   down: lane i knows which child node i + 1 would send down (the left one
+//   unless the right is strictly smaller); the path from the root follows
+//   those choices; its nodes before the first one not smaller than v each
+//   move one level up, and v lands below them.
+// Both are heap_push's sift loops, step for step.  The caller __syncwarp()s
+// between operations.
+__device__ __forceinline__ void warp_heap_up(uint2* hp, int n, float v, int vi, int lane) {
+  const int a = n >> (lane + 1);  // this lane's ancestor (0: none)
+  const uint2 an = a >= 1 ? hp[a] : make_uint2(0u, 0u);
+  const unsigned gt = __ballot_sync(0xffffffffu, a >= 1 && !(__uint_as_float(an.x) <= v));
+  const int s = __ffs(~gt) - 1;  // ancestors that move down: up to the first that stays
+  if (lane < s) hp[n >> lane] = an;
+  if (lane == s) hp[n >> s] = make_uint2(__float_as_uint(v), (unsigned)vi);
+}
+
+// Returns the new root value.
+__device__ __forceinline__ float warp_heap_down(uint2* hp, float v, int vi, int lane) {
+  // node m = lane + 1 (internal nodes 1..31): its chosen child
+  const int m = lane + 1;
+  const uint4 pr = *reinterpret_cast<const uint4*>(hp + 2 * m);
+  const bool right = __uint_as_float(pr.z) < __uint_as_float(pr.x);
+  const unsigned cx = right ? pr.z : pr.x, cy = right ? pr.w : pr.y;
+  const int cpos = 2 * m + (right ? 1 : 0);
+  // the path p_0 = 1, p_{k+1} = child of p_k (levels 0..5); lane k keeps p_k
+  int p = 1, mine = 1;
+#pragma unroll
+  for (int k = 1; k <= 5; k++) {
+    p = __shfl_sync(0xffffffffu, cpos, p - 1);
+    if (lane == k) mine = p;
+  }
+  // lane k (k < 5): the child of p_k, i.e. node p_{k+1}
+  const int src = lane < 5 ? mine - 1 : 0;
+  const unsigned kx = __shfl_sync(0xffffffffu, cx, src);
+  const unsigned ky = __shfl_sync(0xffffffffu, cy, src);
+  const unsigned lt = __ballot_sync(0xffffffffu, lane < 5 && __uint_as_float(kx) < v);
+  const int s = __ffs(~lt) - 1;  // path nodes that move up: up to the first that stays
+  if (lane < s) hp[mine] = make_uint2(kx, ky);
+  if (lane == s) hp[mine] = make_uint2(__float_as_uint(v), (unsigned)vi);
+  const unsigned r0 = __shfl_sync(0xffffffffu, kx, 0);
+  return s >= 1 ? __uint_as_float(r0) : v;
+}
+
 // hp holds 2^(D+1) nodes.  `ready(j)` (whole warp, j non-decreasing) returns
 // once score[0..j] may be read, or false to give up.  idx == nullptr:
 // candidate i carries index i + idx_base.  Candidates go by windows of 32: a
 // ballot against the root at the window's start drops those that cannot be
-// taken (the root only grows); lane 0 runs the rest in order.
+// taken (the root only grows); the rest run in order -- by the whole warp
+// for heaps of up to 63 nodes, by lane 0 otherwise.
 template <int D, typename Ready>
 __device__ int warp_heap_select(const float* score, const int* idx, int idx_base, int n, int cap,
                                 uint2* hp, int lane, Ready ready) {
@@ -91,23 +140,41 @@ __device__ int warp_heap_select(const float* score, const int* idx, int idx_base
     const bool full = size >= cap;
     const float sv = i < n ? score[i] : 0.0f;
     unsigned pend = __ballot_sync(0xffffffffu, i < n && (!full || sv > root));
-    if (lane == 0) {
+    if constexpr (D <= 6) {
+      // every lane runs every operation (pend, size and root are uniform)
       while (pend) {
         const int k = base + __ffs(pend) - 1;
         pend &= pend - 1;
-        const float v = score[k];
+        const float v = __shfl_sync(0xffffffffu, sv, k - base);
         const int vi = idx ? idx[k] : k + idx_base;
         if (size < cap) {
-          hnode_up(hp, ++size, v, vi);
+          warp_heap_up(hp, ++size, v, vi, lane);
+          __syncwarp();
           if (size == cap) root = __uint_as_float(hp[1].x);
         } else if (v > root) {
-          hnode_down<D>(hp, v, vi);
-          root = __uint_as_float(hp[1].x);
+          root = warp_heap_down(hp, v, vi, lane);
+          __syncwarp();
         }
       }
+    } else {
+      if (lane == 0) {
+        while (pend) {
+          const int k = base + __ffs(pend) - 1;
+          pend &= pend - 1;
+          const float v = score[k];
+          const int vi = idx ? idx[k] : k + idx_base;
+          if (size < cap) {
+            hnode_up(hp, ++size, v, vi);
+            if (size == cap) root = __uint_as_float(hp[1].x);
+          } else if (v > root) {
+            hnode_down<D>(hp, v, vi);
+            root = __uint_as_float(hp[1].x);
+          }
+        }
+      }
+      size = __shfl_sync(0xffffffffu, size, 0);
+      root = __shfl_sync(0xffffffffu, root, 0);
     }
-    size = __shfl_sync(0xffffffffu, size, 0);
-    root = __shfl_sync(0xffffffffu, root, 0);
     __syncwarp();
   }
   return size;
