@@ -345,18 +345,14 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
 // are scored, so this runs concurrently with this step's append.  Writes
 // sel[b] / nsel[b] (nsel = -1: attend to every block).
 //
-// Warps 1..7 stage centroids in rounds of kChunk blocks (double-buffered bulk
-// copies) and score them, publishing how many are done; warp 0 replays the
-// heap over the scores as they arrive.  256 threads.
+// Warps 1..7 score the centroids in rounds, publishing how many are done;
+// warp 0 replays the heap over the scores as they arrive.  256 threads.
 // ------------------------------------------------------------------------
 __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int layer, int b) {
-  constexpr int kChunk = 32;  // centroids per staging round (16 KB at hd 128)
   constexpr int kScorers = 224;
   __shared__ __align__(16) float s_q[128];
-  __shared__ __align__(16) float s_c[2 * kChunk * 128];
   __shared__ __align__(16) float s_bsc[2048];
   __shared__ __align__(16) uint2 s_hp[128];
-  __shared__ __align__(8) uint64_t s_bar[2];
   __shared__ int s_ready;  // middle-block scores [0, s_ready) are written
   __shared__ int s_nsel;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -376,12 +372,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
     return;
   }
   PHASE_MARK(tid == 0 && layer == 1, 0);
-  if (tid == 0) {
-    mbar_init(&s_bar[0], 1);
-    mbar_init(&s_bar[1], 1);
-    fence_mbar_init();
-    s_ready = 0;
-  }
+  if (tid == 0) s_ready = 0;
   // query head 0, rotated here (the append CTA rotates its own copy)
   const float* q = sb.q_rotated ? sb.qrot + (long)b * H * hd : sb.qkv + (long)b * (H + 2 * KV) * hd;
   for (int j = tid; j < half; j += blockDim.x) {
@@ -420,47 +411,44 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
     PHASE_MARK(lane == 0 && layer == 1, 2);
     if (lane == 0) s_nsel = size;
   } else {
-    // -------------------------------------------- score_blocks, in rounds
+    // -------------------------------------------- score_blocks
     // 8 threads per block run the 8 lanes of simd_dot_f32_f32 and combine
-    // them in its horizontal-sum order
-    const int ct = tid - 32;
-    const int nround = (nmid + kChunk - 1) / kChunk;
-    auto issue = [&](int r) {
-      const int c0 = 1 + r * kChunk;
-      const int cn = min(kChunk, nb - 1 - c0);
-      float* dst = s_c + (r & 1) * kChunk * 128;
-      if (lane == 0) mbar_expect_tx(&s_bar[r & 1], (uint32_t)(cn * hd * 4));
-      __syncwarp();
-      for (int i = lane; i < cn; i += 32)
-        bulk_g2s(dst + i * hd, kv.centroid + (base + pt[c0 + i]) * hd, hd * 4, &s_bar[r & 1]);
-    };
-    if (warp == 1) {
-      issue(0);
-      if (nround > 1) issue(1);
-    }
-    bool ok = true;
-    for (int r = 0; r < nround; r++) {
-      if (ok) ok = mbar_wait(&s_bar[r & 1], (r >> 1) & 1, sb.err);
-      const int c0 = r * kChunk;  // middle index of the round's first block
-      const int cn = min(kChunk, nmid - c0);
-      const float* cb = s_c + (r & 1) * kChunk * 128;
-      for (int bb = 0; bb < cn; bb += kScorers / 8) {
-        const int blk = bb + (ct >> 3), l = ct & 7;
+    // them in its horizontal-sum order.  Each group of 8 scores kU blocks per
+    // round straight from global memory (page-table entries first, then every
+    // centroid load of the round at once: one memory round trip per round),
+    // and the round's scores are published for the heap.
+    constexpr int kGroups = kScorers / 8, kU = 3, kD = 16;  // kD: hd / 8 at most
+    const int ct = tid - 32, grp = ct >> 3, l = ct & 7, nd = hd >> 3;
+    for (int r0 = 0; r0 < nmid; r0 += kGroups * kU) {
+      const float* cp[kU];
+#pragma unroll
+      for (int u = 0; u < kU; u++) {
+        const int blk = r0 + grp + u * kGroups;
+        cp[u] = blk < nmid ? kv.centroid + (base + pt[1 + blk]) * hd : nullptr;
+      }
+      float cv[kU][kD];
+#pragma unroll
+      for (int u = 0; u < kU; u++)
+#pragma unroll
+        for (int j = 0; j < kD; j++) cv[u][j] = (cp[u] && j < nd) ? __ldcg(cp[u] + l + 8 * j) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < kU; u++) {
+        const int blk = r0 + grp + u * kGroups;
         float acc = 0.0f;
-        if (blk < cn && ok)
-          for (int d = l; d < hd; d += 8) acc = __fmaf_rn(s_q[d], cb[blk * hd + d], acc);
+#pragma unroll
+        for (int j = 0; j < kD; j++)
+          if (j < nd) acc = __fmaf_rn(s_q[l + 8 * j], cv[u][j], acc);
         // ((c0+c4)+(c1+c5)) + ((c2+c6)+(c3+c7))
         const float h4 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
         const float t2 = __fadd_rn(h4, __shfl_xor_sync(0xffffffffu, h4, 1));
         const float sum = __fadd_rn(t2, __shfl_xor_sync(0xffffffffu, t2, 2));
-        if (blk < cn && l == 0) s_bsc[c0 + blk] = sum;
+        if (blk < nmid && l == 0) s_bsc[blk] = sum;
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(kScorers));  // scores written, buffer free
+      asm volatile("bar.sync 1, %0;" ::"r"(kScorers));  // this round's scores written
       if (ct == 0) {
         __threadfence_block();
-        *reinterpret_cast<volatile int*>(&s_ready) = c0 + cn;
+        *reinterpret_cast<volatile int*>(&s_ready) = min(nmid, r0 + kGroups * kU);
       }
-      if (warp == 1 && r + 2 < nround) issue(r + 2);
     }
     PHASE_MARK(ct == 0 && layer == 1, 1);
   }
@@ -1222,9 +1210,11 @@ __global__ void __launch_bounds__(128 * HPG, 1)
   }
 }
 
+// Token capacity of one attention launch, a multiple of 4: the per-token
+// arrays and the transposed V rows it sizes are read as float4.
 static int attn_max_tok(const KvLayout& kv, const StepBuffers& sb) {
-  if (kv.paged) return kBlk * sb.sparse_blocks_k;
-  return sb.sparse_k > 0 ? sb.sparse_k : kv.seq_len;
+  const int t = kv.paged ? kBlk * sb.sparse_blocks_k : (sb.sparse_k > 0 ? sb.sparse_k : kv.seq_len);
+  return (t + 3) & ~3;
 }
 
 static size_t attn_smem(const KvLayout& kv, const StepBuffers& sb, int max_tok) {

@@ -178,8 +178,17 @@ class DeviceModel:
         return t.mul_(scale)
 
     def quant(self, w):
-        """INT8 per row with power-of-two scales (as quant_int8_rows)."""
+        """INT8 per row with power-of-two scales (as quant_int8_rows), or FP8
+        E4M3 with one power-of-two scale per tensor (as quant_fp8_tensor:
+        round to nearest even, codes 0x00..0x7E, -0 stored as +0)."""
         torch = self.torch
+        if self.kind == "fp8":
+            amax = float(w.abs().max()) or 1.0
+            s = torch.tensor([2.0 ** np.ceil(np.log2(amax / 448.0))], dtype=torch.float32,
+                             device=self.dev)
+            code = (w / s).to(torch.float8_e4m3fn).view(torch.uint8)
+            code = torch.where(code == 0x80, torch.zeros_like(code), code)
+            return code.contiguous(), s
         amax = w.abs().amax(dim=1).clamp_min(1e-30)
         s = torch.exp2(torch.ceil(torch.log2(amax / 127.0)))
         q = torch.round(w / s[:, None]).clamp_(-127, 127).to(torch.int8)

@@ -44,6 +44,7 @@ def _load(name):
 
 METRIC = "decode tok/s (Llama-3-8B-shaped INT8, b=1 per GPU, 2k context)"
 METRIC_B = "decode tok/s (Llama-3-8B-shaped INT8, b={} per GPU, 2k context)"
+METRIC_70B = "decode tok/s (70B-shaped FP8 per-tensor, b={} per GPU, {} context, LSH top-{})"
 PROMPT = 2048
 SEED = 1234
 
@@ -194,11 +195,20 @@ def run_cuda(args):
     dp.init("nccl", torch.device("cuda", local))
     eng = _load("engine")
     S = _load("synth")
-    cfg = S.LLAMA3_8B
     B = args.batch
-    tmb = args.tensor_min_batch if B >= args.tensor_min_batch > 0 else 0
-    e = eng.Engine(cfg, device=local, max_batch=B, tensor_min_batch=tmb)
-    src = S.DeviceModel(cfg, seed=SEED, device=local)
+    big = args.model == "70b"
+    if big:
+        # BASELINE config 5 on one GPU: FP8 E4M3 per-tensor weights (~70 GB),
+        # linear BF16 KV with the reference's LSH-routed top-K attention
+        cfg = S.LLAMA_70B
+        e = eng.Engine(cfg, device=local, max_batch=B, weight_kind=eng.EC_W_FP8,
+                       use_paged_kv=False, sparse_k=args.sparse_k)
+        src = S.DeviceModel(cfg, seed=SEED, device=local, kind="fp8")
+    else:
+        cfg = S.LLAMA3_8B
+        tmb = args.tensor_min_batch if B >= args.tensor_min_batch > 0 else 0
+        e = eng.Engine(cfg, device=local, max_batch=B, tensor_min_batch=tmb)
+        src = S.DeviceModel(cfg, seed=SEED, device=local)
 
     def sink(kind, layer, name, t, s):
         if kind == "emb":
@@ -277,27 +287,39 @@ def run_cuda(args):
         if d["launches"] and d["bytes"] else 0.0
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "roofline_traffic.json")
-    if os.path.exists(tpath):
-        tj = json.load(open(tpath))
+    if os.path.exists(tpath) and not big and B == 1:
+        tj = json.load(open(tpath))  # measured on the 8B b=1 chain launch
         if tj.get("kernel") == dom:
             traffic = tj["traffic_bytes_per_launch"]
     weight_bytes = (sum(int(np.prod(s)) for s in S.mat_shapes(cfg).values()) * cfg.n_layers
                     + cfg.vocab_size * cfg.dim)
-    kv_tok = cfg.n_layers * cfg.n_kv_heads * (cfg.head_dim * 2 + 8)
-    att_tokens = min(args.prompt + args.warmup + args.steps, 64 * 16)
+    if big:
+        # linear BF16 K and V of the attended top-K tokens (candidate scoring
+        # reads more K rows; not counted)
+        kv_tok = cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * 2
+        att_tokens = min(args.prompt + args.warmup + args.steps, args.sparse_k)
+    else:
+        kv_tok = cfg.n_layers * cfg.n_kv_heads * (cfg.head_dim * 2 + 8)
+        att_tokens = min(args.prompt + args.warmup + args.steps, 64 * 16)
     step_bytes = weight_bytes + B * kv_tok * att_tokens
 
     if rank == 0:
         line = {
-            "metric": METRIC if B == 1 else METRIC_B.format(B), "value": round(value, 3),
+            "metric": (METRIC_70B.format(B, args.prompt, args.sparse_k) if big else
+                       METRIC if B == 1 else METRIC_B.format(B)), "value": round(value, 3),
             "unit": "tok/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "fp8" if big else "int8",
             "data": "synthetic",
-            "config": {"workload": f"llama3-8b-shape decode b={B} per GPU", "global_batch": ws * B,
-                       "context": args.prompt, "weights": "int8 per-row pow2 scale",
-                       "kv": "paged int8", "parallelism": f"dp{ws} (replicas)",
-                       "gemm": "tcgen05 int8 (digit planes)" if tmb else "cuda-core gemv chain",
+            "config": {"workload": f"{'70b' if big else 'llama3-8b'}-shape decode b={B} per GPU",
+                       "global_batch": ws * B, "context": args.prompt,
+                       "weights": "fp8 e4m3 per-tensor pow2 scale" if big
+                       else "int8 per-row pow2 scale",
+                       "kv": f"linear bf16, LSH top-{args.sparse_k}" if big else "paged int8",
+                       "parallelism": f"dp{ws} (replicas)",
+                       "gemm": "tcgen05 int8 (digit planes)" if (not big and tmb)
+                       else "cuda-core gemv chain",
                        "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"},
             "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B * (cfg.vocab_size + 1)},
@@ -315,7 +337,12 @@ def run_cuda(args):
             "kernel_share": {k: round(v["ms"] / tot_ms, 4) for k, v in prof.items() if tot_ms},
             "clocks": clk.summary(),
         }
-        if not args.no_cpu_baseline:
+        if big:
+            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": os.cpu_count() or 1,
+                                    "kind": "reference",
+                                    "sample": "unavailable: the reference's BF16 copy of the "
+                                              "70B shape (~140 GB) exceeds host memory"}
+        elif not args.no_cpu_baseline:
             del src
             torch.cuda.empty_cache()
             threads = os.cpu_count() or 1
@@ -346,6 +373,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="tokens already in the cache")
     ap.add_argument("--batch", type=int, default=1,
                     help="sequences decoded together per GPU (b=64: the batched metric)")
+    ap.add_argument("--model", default="8b", choices=["8b", "70b"],
+                    help="8b: the headline INT8 config; 70b: FP8 config 5 on one GPU")
+    ap.add_argument("--sparse-k", type=int, default=511, help="70b: LSH top-K (engine max 511)")
     ap.add_argument("--tensor-min-batch", type=int, default=16,
                     help="batches this large run their GEMMs on the tensor cores (0: never)")
     args = ap.parse_args()

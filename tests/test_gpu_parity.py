@@ -228,6 +228,26 @@ def test_tiny_lsh_4x8(eng, torch, oracle, tiny_model):
     e.close()
 
 
+@pytest.mark.parametrize("sparse_k,steps", [(37, 200), (511, 640)])
+def test_linear_topk_not_multiple_of_4(eng, torch, oracle, tiny_model, sparse_k, steps):
+    """Linear-mode top-K sizes that are not a multiple of 4 (BASELINE config
+    5 attends 511-512 tokens): the attention's per-token arrays are padded;
+    every checked step bit-exact against the restatement."""
+    e = eng.Engine(tiny_model.cfg, use_paged_kv=False, sparse_k=sparse_k)
+    e.load(tiny_model)
+    pm = oracle.PortModel(tiny_model, use_paged_kv=False, sparse_k=sparse_k)
+    toks = list(G["tiny_linear_tokens"][:64])
+    for pos in range(steps):
+        check = pos % 40 == 0 or pos >= steps - 8
+        lg, am = e.step([toks[pos]], [pos], want_logits=True)
+        want = pm.forward(int(toks[pos]), pos)
+        if check:
+            assert np.array_equal(bits(lg[0]), bits(want)), f"step {pos}"
+        if pos >= 63:
+            toks.append(int(am[0]))
+    e.close()
+
+
 def test_paged_block_sparse(eng, torch, oracle, synth):
     """Context beyond SPARSE_BLOCKS_K * 16 = 1024 tokens: block-centroid
     scoring, first + last + min-heap top-62 selection in the reference's heap
