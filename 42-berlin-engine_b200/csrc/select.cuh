@@ -72,8 +72,8 @@ __device__ __forceinline__ void hnode_down(uint2* hp, float v, int vi) {
   hp[n] = make_uint2(__float_as_uint(v), (unsigned)vi);
 }
 
-// The same two operations run by a whole warp, for heaps of at most 63
-// nodes (D <= 6): the path an operation walks is found in parallel, then
+// The same two operations run by a whole warp, for heaps of at most 511
+// nodes (D <= 9): the path an operation walks is found in parallel, then
 // every node on it moves in one store.
 //   up: lane k loads the (k+1)-th ancestor of position n; the ancestors
 //   before the first one that is not greater than v each move one level
@@ -93,26 +93,65 @@ __device__ __forceinline__ void warp_heap_up(uint2* hp, int n, float v, int vi, 
   if (lane == s) hp[n >> s] = make_uint2(__float_as_uint(v), (unsigned)vi);
 }
 
-// Returns the new root value.
+// Returns the new root value.  Heaps of up to 2^D - 1 nodes, D <= 9: lanes
+// 0..30 settle the child choices of levels 0..4 (nodes 1..31) and a shuffle
+// chase walks them; below level 5 the path's subtree (levels 5..D-2, at most
+// 7 internal nodes) is settled the same way and walked on.
+template <int D>
 __device__ __forceinline__ float warp_heap_down(uint2* hp, float v, int vi, int lane) {
-  // node m = lane + 1 (internal nodes 1..31): its chosen child
-  const int m = lane + 1;
-  const uint4 pr = *reinterpret_cast<const uint4*>(hp + 2 * m);
-  const bool right = __uint_as_float(pr.z) < __uint_as_float(pr.x);
-  const unsigned cx = right ? pr.z : pr.x, cy = right ? pr.w : pr.y;
-  const int cpos = 2 * m + (right ? 1 : 0);
-  // the path p_0 = 1, p_{k+1} = child of p_k (levels 0..5); lane k keeps p_k
+  static_assert(D >= 6 && D <= 9, "warp_heap_down: 6 <= D <= 9");
+  // node m's chosen child: the left one unless the right is strictly smaller
+  auto choose = [&](int m, unsigned& cx, unsigned& cy, int& cpos) {
+    const uint4 pr = *reinterpret_cast<const uint4*>(hp + 2 * m);
+    const bool right = __uint_as_float(pr.z) < __uint_as_float(pr.x);
+    cx = right ? pr.z : pr.x;
+    cy = right ? pr.w : pr.y;
+    cpos = 2 * m + (right ? 1 : 0);
+  };
+  unsigned ax, ay, bx = 0, by = 0;
+  int apos, bpos = 0;
+  choose(lane + 1, ax, ay, apos);  // levels 0..4 (lane 31: node 32, unused)
+  // the path p_0 = 1, p_{k+1} = chosen child of p_k; lane k keeps p_k
   int p = 1, mine = 1;
 #pragma unroll
   for (int k = 1; k <= 5; k++) {
-    p = __shfl_sync(0xffffffffu, cpos, p - 1);
+    p = __shfl_sync(0xffffffffu, apos, p - 1);
     if (lane == k) mine = p;
   }
-  // lane k (k < 5): the child of p_k, i.e. node p_{k+1}
-  const int src = lane < 5 ? mine - 1 : 0;
-  const unsigned kx = __shfl_sync(0xffffffffu, cx, src);
-  const unsigned ky = __shfl_sync(0xffffffffu, cy, src);
-  const unsigned lt = __ballot_sync(0xffffffffu, lane < 5 && __uint_as_float(kx) < v);
+  constexpr int kDeep = D - 6;  // path steps below level 5
+  int sub0 = 0;
+  if constexpr (kDeep > 0) {
+    // subtree of p_5: lane i < 2^kDeep - 1 takes its i-th internal node in
+    // level order (p5; 2p5, 2p5+1; 4p5 .. 4p5+3)
+    sub0 = p;
+    const int lvl = 31 - __clz(lane + 1);  // 0, 1, 1, 2, 2, 2, 2
+    const int node = (p << lvl) + (lane + 1 - (1 << lvl));
+    if (lane < (1 << kDeep) - 1) choose(node, bx, by, bpos);
+#pragma unroll
+    for (int k = 6; k <= 5 + kDeep; k++) {
+      const int l = k - 6;  // level of p_{k-1} inside the subtree
+      p = __shfl_sync(0xffffffffu, bpos, (1 << l) - 1 + (p - (sub0 << l)));
+      if (lane == k) mine = p;
+    }
+  }
+  // lane k (k < D - 1): the node p_{k+1} (child of p_k), from the lane that
+  // settled p_k
+  constexpr int kSteps = D - 1;
+  int src = 0;
+  bool deep = false;
+  if (lane < 5) {
+    src = mine - 1;
+  } else if (lane < kSteps) {
+    const int l = lane - 5;
+    src = (1 << l) - 1 + (mine - (sub0 << l));
+    deep = true;
+  }
+  const unsigned kxa = __shfl_sync(0xffffffffu, ax, src);
+  const unsigned kya = __shfl_sync(0xffffffffu, ay, src);
+  const unsigned kxb = __shfl_sync(0xffffffffu, bx, src);
+  const unsigned kyb = __shfl_sync(0xffffffffu, by, src);
+  const unsigned kx = deep ? kxb : kxa, ky = deep ? kyb : kya;
+  const unsigned lt = __ballot_sync(0xffffffffu, lane < kSteps && __uint_as_float(kx) < v);
   const int s = __ffs(~lt) - 1;  // path nodes that move up: up to the first that stays
   if (lane < s) hp[mine] = make_uint2(kx, ky);
   if (lane == s) hp[mine] = make_uint2(__float_as_uint(v), (unsigned)vi);
@@ -125,7 +164,7 @@ __device__ __forceinline__ float warp_heap_down(uint2* hp, float v, int vi, int 
 // candidate i carries index i + idx_base.  Candidates go by windows of 32: a
 // ballot against the root at the window's start drops those that cannot be
 // taken (the root only grows); the rest run in order -- by the whole warp
-// for heaps of up to 63 nodes, by lane 0 otherwise.
+// for 6 <= D <= 9, by lane 0 otherwise.
 template <int D, typename Ready>
 __device__ int warp_heap_select(const float* score, const int* idx, int idx_base, int n, int cap,
                                 uint2* hp, int lane, Ready ready) {
@@ -140,7 +179,7 @@ __device__ int warp_heap_select(const float* score, const int* idx, int idx_base
     const bool full = size >= cap;
     const float sv = i < n ? score[i] : 0.0f;
     unsigned pend = __ballot_sync(0xffffffffu, i < n && (!full || sv > root));
-    if constexpr (D <= 6) {
+    if constexpr (D >= 6 && D <= 9) {
       // every lane runs every operation (pend, size and root are uniform)
       while (pend) {
         const int k = base + __ffs(pend) - 1;
@@ -152,7 +191,7 @@ __device__ int warp_heap_select(const float* score, const int* idx, int idx_base
           __syncwarp();
           if (size == cap) root = __uint_as_float(hp[1].x);
         } else if (v > root) {
-          root = warp_heap_down(hp, v, vi, lane);
+          root = warp_heap_down<D>(hp, v, vi, lane);
           __syncwarp();
         }
       }
