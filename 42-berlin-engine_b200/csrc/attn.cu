@@ -205,22 +205,23 @@ __global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout l
 }
 
 // ------------------------------------------------------------------------
-// Linear-mode selection (inference.c:228-423): one CTA per sequence.
+// Linear-mode selection (inference.c:228-423) in three launches: candidates
+// (one CTA per sequence: LSH query hash, lsh_find_candidates, window),
+// scores (CTAs over candidates x KV heads), heap (one warp per sequence).
 // sel[b] receives the top-K positions in the reference's heap order.
 // ------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayout lsh,
-                                                            StepBuffers sb, int layer) {
+__global__ void __launch_bounds__(256) linear_cand_kernel(KvLayout kv, LshLayout lsh,
+                                                          StepBuffers sb, int layer) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const int b = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim;
-  const int cap_c = sb.window + lsh.max_cand * lsh.unit;  // candidate capacity
-  int* cand = reinterpret_cast<int*>(smem);               // [cap_c]
-  float* cscore = reinterpret_cast<float*>(cand + cap_c);  // [cap_c]
-  uint2* hp = reinterpret_cast<uint2*>(cscore + cap_c);  // [1024] heap nodes, 1-based
-  float* qm = reinterpret_cast<float*>(hp + 1024);         // [hd]
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int H = kv.n_heads, hd = kv.head_dim;
+  const int cap_c = linear_cand_cap(sb, lsh);             // candidate capacity
+  int* cand = sb.lcand + (long)b * cap_c;                  // [cap_c], global
+  float* qm = reinterpret_cast<float*>(smem);              // [hd]
   __shared__ uint32_t s_code[16];
   __shared__ int s_units[64];
   __shared__ int s_nu, s_nc, s_wcount;
+  __shared__ int s_uoff[64], s_ust[64], s_ulen[64];
   __shared__ unsigned s_seen[4096 / 32];
   pdl_launch_dependents();
   pdl_wait();
@@ -228,7 +229,10 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
   const int kv_len = min(pos + 1, kv.seq_len);
   const float* q = sb.qrot + (long)b * H * hd;
   if (!(sb.sparse_k > 0 && kv_len > sb.sparse_k)) {
-    if (tid == 0) sb.nsel[b] = -1;  // dense attention over [0, kv_len)
+    if (tid == 0) {
+      sb.nsel[b] = -1;  // dense attention over [0, kv_len)
+      sb.lnc[b] = 0;
+    }
     return;
   }
   const int ws = kv_len > sb.window ? kv_len - sb.window : 0;
@@ -293,47 +297,88 @@ __global__ void __launch_bounds__(256) linear_select_kernel(KvLayout kv, LshLayo
     }
     __syncthreads();
   }
+  // the units' tokens before the window, in unit order (offsets by thread 0,
+  // the copies by one warp per unit)
   if (tid == 0) {
     int n = 0;
     for (int i = 0; i < s_nu; i++) {
       const int u = s_units[i];
       const int st = lsh.unit_start[(long)b * lsh.max_units + u];
       const int ln = lsh.unit_len[(long)b * lsh.max_units + u];
-      for (int p = 0; p < ln && n < cap_c; p++)
-        if (st + p < ws) cand[n++] = st + p;
+      int take = ws - st < ln ? ws - st : ln;
+      if (take < 0) take = 0;
+      if (take > cap_c - n) take = cap_c - n;
+      s_uoff[i] = n;
+      s_ust[i] = st;
+      s_ulen[i] = take;
+      n += take;
     }
     s_wcount = n;
   }
   __syncthreads();
+  for (int i = tid >> 5; i < s_nu; i += blockDim.x >> 5)
+    for (int p = tid & 31; p < s_ulen[i]; p += 32) cand[s_uoff[i] + p] = s_ust[i] + p;
   {
     const int n0 = s_wcount;
     for (int i = tid; i < kv_len - ws && n0 + i < cap_c; i += blockDim.x) cand[n0 + i] = ws + i;
     if (tid == 0) s_nc = min(n0 + (kv_len - ws), cap_c);
   }
   __syncthreads();
-  const int nc = s_nc;
-  // candidate scores (inference.c:341-353)
-  const int grp = H / KV;
+  if (tid == 0) sb.lnc[b] = s_nc;
+}
+
+// Candidate scores (inference.c:341-353): thread (candidate, KV head) runs
+// simd_dot_bf16_f32 of the candidate's key row with the group's first query
+// head; the candidate's score adds the heads' dots in head order.
+__global__ void __launch_bounds__(256) linear_score_kernel(KvLayout kv, StepBuffers sb, int layer,
+                                                           int cap_c) {
+  __shared__ float part[256];
+  const int b = blockIdx.y, tid = threadIdx.x;
+  const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim, grp = H / KV;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int nc = sb.lnc[b];
+  const int cpb = 256 / KV;  // candidates per CTA
+  const int c = blockIdx.x * cpb + tid / KV, kh = tid % KV;
+  if (blockIdx.x * cpb >= nc) return;
+  const bool live = tid < cpb * KV && c < nc;
+  const float* q = sb.qrot + (long)b * H * hd;
   const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;
-  for (int i = tid; i < nc; i += blockDim.x) {
-    const uint16_t* kr = kv.lk + (lrow + cand[i]) * KV * hd;
-    float s = 0.0f;
-    for (int kh = 0; kh < KV; kh++) s = __fadd_rn(s, dot_bf16_ref(kr + kh * hd, q + kh * grp * hd, hd));
-    cscore[i] = s;
+  if (live) {
+    const int pos = sb.lcand[(long)b * cap_c + c];
+    part[tid] = dot_bf16_ref(kv.lk + ((lrow + pos) * KV + kh) * hd, q + kh * grp * hd, hd);
   }
   __syncthreads();
-  if (warp == 0) {
-    const int cap = nc < sb.sparse_k ? nc : sb.sparse_k;
-    auto all = [](int) { return true; };
-    const int size = cap < 64 ? warp_heap_select<6>(cscore, cand, 0, nc, cap, hp, lane, all)
-                              : warp_heap_select<9>(cscore, cand, 0, nc, cap, hp, lane, all);
-    int* out = sb.sel + (long)b * sb.max_sel;
-    for (int i = lane; i < size; i += 32) out[i] = (int)hp[i + 1].y;
-    if (lane == 0) {
-      sb.nsel[b] = size;
-      lsh.counters[b * 2] += 1ull;
-      lsh.counters[b * 2 + 1] += (unsigned long long)size;
-    }
+  if (live && kh == 0) {
+    float sc = 0.0f;
+    for (int h = 0; h < KV; h++) sc = __fadd_rn(sc, part[tid + h]);
+    sb.lscore[(long)b * cap_c + c] = sc;
+  }
+}
+
+// The top-K of the scored candidates (heap_push, inference.c:356-423): one
+// warp per sequence replays the heap; sel[b] receives the positions in the
+// reference's heap array order.
+__global__ void __launch_bounds__(32) linear_heap_kernel(LshLayout lsh, StepBuffers sb,
+                                                         int cap_c) {
+  __shared__ __align__(16) uint2 hp[1024];  // heap nodes, 1-based
+  const int b = blockIdx.x, lane = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int nc = sb.lnc[b];
+  if (nc <= 0) return;  // dense attention (nsel = -1 already)
+  const int cap = nc < sb.sparse_k ? nc : sb.sparse_k;
+  auto all = [](int) { return true; };
+  const float* cscore = sb.lscore + (long)b * cap_c;
+  const int* cand = sb.lcand + (long)b * cap_c;
+  const int size = cap < 64 ? warp_heap_select<6>(cscore, cand, 0, nc, cap, hp, lane, all)
+                            : warp_heap_select<9>(cscore, cand, 0, nc, cap, hp, lane, all);
+  int* out = sb.sel + (long)b * sb.max_sel;
+  for (int i = lane; i < size; i += 32) out[i] = (int)hp[i + 1].y;
+  if (lane == 0) {
+    sb.nsel[b] = size;
+    lsh.counters[b * 2] += 1ull;
+    lsh.counters[b * 2 + 1] += (unsigned long long)size;
   }
 }
 
@@ -1320,11 +1365,6 @@ cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuf
   if (!e) e = opt_in_max_smem(attention_kernel<false, true>);
   if (!e) e = opt_in_max_smem(attention_kernel<true, false>);
   if (!e) e = opt_in_max_smem(attention_kernel<false, false>);
-  const int cap_c = sb.window + lsh.max_cand * lsh.unit;
-  const int ssel = cap_c * 8 + 1024 * 8 + 256 * 4;
-  if (!e && ssel <= 227 * 1024)
-    e = cudaFuncSetAttribute(linear_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             ssel);
   return e;
 }
 
@@ -1361,9 +1401,15 @@ cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const Ste
 
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                                  int layer, int B, cudaStream_t s, bool pdl) {
-  const int cap_c = sb.window + lsh.max_cand * lsh.unit;
-  const size_t smem = (size_t)cap_c * 8 + 1024 * 8 + 256 * 4;
-  return launch_ex(linear_select_kernel, dim3(B), dim3(256), smem, s, pdl, kv, lsh, sb, layer);
+  const int cap_c = linear_cand_cap(sb, lsh);
+  cudaError_t e = launch_ex(linear_cand_kernel, dim3(B), dim3(256), (size_t)kv.head_dim * 4, s, pdl,
+                            kv, lsh, sb, layer);
+  const int cpb = 256 / kv.n_kv_heads;
+  if (!e)
+    e = launch_ex(linear_score_kernel, dim3((cap_c + cpb - 1) / cpb, B), dim3(256), 0, s, pdl, kv,
+                  sb, layer, cap_c);
+  if (!e) e = launch_ex(linear_heap_kernel, dim3(B), dim3(32), 0, s, pdl, lsh, sb, cap_c);
+  return e;
 }
 
 bool use_group_attention(const KvLayout& kv, const StepBuffers& sb, int B) {

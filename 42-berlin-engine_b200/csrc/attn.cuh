@@ -52,7 +52,19 @@ struct StepBuffers {
   int pos_fixed;        // position when pos == nullptr (per-op entry points)
   int q_rotated;        // selection reads qrot (already rotated) instead of qkv
   int list_dense;       // selection also lists every block when attending all
+  // linear mode: candidates and their scores between the selection's
+  // kernels ([B][linear_cand_cap] each) and the candidate count ([B])
+  int* lcand;
+  float* lscore;
+  int* lnc;
 };
+
+// Linear-mode candidate capacity per sequence: the window plus max_cand
+// units of `unit` tokens; the selection runs as kLinearSelectLaunches kernels.
+constexpr int kLinearSelectLaunches = 3;
+inline __host__ __device__ int linear_cand_cap(const StepBuffers& sb, const LshLayout& lsh) {
+  return sb.window + lsh.max_cand * lsh.unit;
+}
 
 inline __host__ __device__ int step_pos(const StepBuffers& sb, int b) {
   return sb.pos ? sb.pos[b] : sb.pos_fixed;

@@ -59,6 +59,9 @@ struct ec_ctx {
   float *x = nullptr, *qkvb = nullptr, *qrot = nullptr, *att = nullptr, *hbuf = nullptr,
         *logits = nullptr;
   int *argmax = nullptr, *tokens = nullptr, *pos = nullptr, *sel = nullptr, *nsel = nullptr;
+  int *lcand = nullptr, *lnc = nullptr;  // linear mode: selection candidates per sequence
+  float* lscore = nullptr;
+  int cap_c = 0;
   int* err = nullptr;
   int* chain_ctr = nullptr;  // [layers][packs][kMaxChainPhases + 1]
   float* xn = nullptr;       // batched chain: RMSNorm'd rows [max_batch][dim]
@@ -319,6 +322,10 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   } else {
     TRY(dalloc(ctx, &kv.lk, (size_t)S * L * c.seq_len * KV * hd));
     TRY(dalloc(ctx, &kv.lv, (size_t)S * L * c.seq_len * KV * hd));
+    ctx->cap_c = c.window + c.lsh_max_cand * c.lsh_unit;
+    TRY(dalloc(ctx, &ctx->lcand, (size_t)S * ctx->cap_c));
+    TRY(dalloc(ctx, &ctx->lscore, (size_t)S * ctx->cap_c));
+    TRY(dalloc(ctx, &ctx->lnc, (size_t)S));
   }
   // RoPE tables (rope_cache_init, ops_rope.c:30-96) on the host
   {
@@ -620,6 +627,9 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   sb.att = ctx->att;
   sb.sel = ctx->sel;
   sb.nsel = ctx->nsel;
+  sb.lcand = ctx->lcand;
+  sb.lscore = ctx->lscore;
+  sb.lnc = ctx->lnc;
   auto phase = [&](const Mat& m, int pro, int epi, const float* x, int xs, const uint16_t* nw,
                    float* y, int ys) {
     ec::ChainPhase ph = chain_phase(m, pro, epi, x, nw, y);
@@ -682,7 +692,7 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
     if (!ctx->kv.paged) {
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
       if ((e = ec::launch_linear_select(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
-      ctx->launches++;
+      ctx->launches += ec::kLinearSelectLaunches;
     }
     {
       ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
@@ -759,6 +769,9 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
   sb.att = ctx->att;
   sb.sel = ctx->sel;
   sb.nsel = ctx->nsel;
+  sb.lcand = ctx->lcand;
+  sb.lscore = ctx->lscore;
+  sb.lnc = ctx->lnc;
   // one projection of nb rows: x [nb][K] (x_stride apart) -> y per epi
   auto proj = [&](const Mat& m, const float* x, int xs, const uint16_t* nw, float* y, int ys,
                   int epi, int nb) -> cudaError_t {
@@ -820,7 +833,7 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
     if (!ctx->kv.paged) {
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
       if ((e = ec::launch_linear_select(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
-      ctx->launches++;
+      ctx->launches += ec::kLinearSelectLaunches;
     }
     {
       ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
@@ -883,6 +896,11 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
     sb.att = ctx->att + (size_t)b * H * hd;
     sb.sel = ctx->sel + (size_t)b * ctx->max_sel;
     sb.nsel = ctx->nsel + b;
+    if (ctx->lcand) {
+      sb.lcand = ctx->lcand + (size_t)b * ctx->cap_c;
+      sb.lscore = ctx->lscore + (size_t)b * ctx->cap_c;
+      sb.lnc = ctx->lnc + b;
+    }
     ec::KvLayout kv = ctx->kv;
     ec::LshLayout lsh = ctx->lsh;
     const size_t per = (size_t)kv.n_layers * kv.max_blocks;
@@ -931,7 +949,7 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
       if (!kv.paged) {
         ProfScope ps(ctx, EC_K_SELECT, 0.0);
         if ((e = ec::launch_linear_select(kv, lsh, sb, l, 1, ctx->stream, true))) return e;
-        ctx->launches++;
+        ctx->launches += ec::kLinearSelectLaunches;
       }
       {
         ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
@@ -1120,7 +1138,7 @@ extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
   // embed, [QKV(0)], per layer: QKV, append, [select], attention, o, gate/up,
   // down -- or with the chain: append, [select], attention, chain -- then
   // [LM head] and argmax
-  const int sel = ctx->kv.paged ? 0 : 1;
+  const int sel = ctx->kv.paged ? 0 : ec::kLinearSelectLaunches;
   if (ctx->tc && B >= ctx->c.tensor_min_batch) {
     // embed, per pass QKV(0) (quant, GEMM, combine), per layer append,
     // [select], attention and 4 projections per pass, argmax per sequence
