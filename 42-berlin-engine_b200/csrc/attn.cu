@@ -82,20 +82,21 @@ __device__ float warp_quant_int8(const float* in, int8_t* out, int n, int lane, 
 // ------------------------------------------------------------------------
 __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int layer, int b);
 
-__global__ void __launch_bounds__(256) kv_append_kernel(KvLayout kv, LshLayout lsh, StepBuffers sb,
+__global__ void __launch_bounds__(256, 4) kv_append_kernel(KvLayout kv, LshLayout lsh, StepBuffers sb,
                                                         int layer) {
   const int b = blockIdx.y;
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim, half = hd >> 1;
   pdl_launch_dependents();
-  pdl_wait();
-  PHASE_MARK(tid == 0 && layer == 1 && b == 0, 4 + blockIdx.x);
   if (blockIdx.x == 1) {
+    // waits for the previous kernel itself, after loads that do not depend on it
     paged_select_cta(kv, sb, layer, b);
     PHASE_MARK(tid == 0 && layer == 1 && b == 0, 3);
     return;
   }
+  pdl_wait();
+  PHASE_MARK(tid == 0 && layer == 1 && b == 0, 4);
   const int pos = step_pos(sb, b);
   const float* q = sb.qkv + (long)b * (H + 2 * KV) * hd;
   float* qo = sb.qrot + (long)b * H * hd;
@@ -408,6 +409,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
   const int nb = (n_tok + kBlk - 1) / kBlk;
   if (nb <= sb.sparse_blocks_k || nb > 2048 || hd > 128) {
     // every block in order (listed explicitly when asked to, same result)
+    pdl_wait();
     const bool list = sb.list_dense && nb <= sb.max_sel;
     if (list) {
       int* out = sb.sel + (long)b * sb.max_sel;
@@ -416,6 +418,21 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
     if (tid == 0) sb.nsel[b] = list ? nb : -1;
     return;
   }
+  // Page table and centroids of the full middle blocks were written in
+  // earlier steps, not by the kernel this one follows: pull the centroids
+  // into L2 before waiting for it (griddepcontrol.wait), while the previous
+  // layer still runs.
+  constexpr int kGroups = kScorers / 8, kU = 3, kD = 16;  // kD: hd / 8 at most
+  const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
+  const int* pt = kv.page_table + base;
+  const int nmid = nb - 2;
+  for (int i = tid; i < nmid * (hd >> 5); i += blockDim.x) {
+    const int blk = i / (hd >> 5), line = i - blk * (hd >> 5);
+    const float* cp = kv.centroid + (base + pt[1 + blk]) * hd + line * 32;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(cp));
+  }
+  pdl_wait();
+  PHASE_MARK(tid == 0 && layer == 1 && b == 0, 5);
   PHASE_MARK(tid == 0 && layer == 1, 0);
   if (tid == 0) s_ready = 0;
   // query head 0, rotated here (the append CTA rotates its own copy)
@@ -432,9 +449,6 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
     }
   }
   __syncthreads();
-  const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
-  const int* pt = kv.page_table + base;
-  const int nmid = nb - 2;
   int m = sb.sparse_blocks_k - 2;
   if (m > nmid) m = nmid;
   if (m > 62) m = 62;
@@ -445,6 +459,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
       for (uint32_t it = 0; it < kWaitLimit; it++) {
         if (*reinterpret_cast<volatile int*>(&s_ready) > j) {
           __threadfence_block();
+          PHASE_MARK(lane == 0 && layer == 1 && b == 0 && (j >> 5) < 16, 16 + (j >> 5));
           return true;
         }
         __nanosleep(32);
@@ -462,7 +477,6 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
     // round straight from global memory (page-table entries first, then every
     // centroid load of the round at once: one memory round trip per round),
     // and the round's scores are published for the heap.
-    constexpr int kGroups = kScorers / 8, kU = 3, kD = 16;  // kD: hd / 8 at most
     const int ct = tid - 32, grp = ct >> 3, l = ct & 7, nd = hd >> 3;
     for (int r0 = 0; r0 < nmid; r0 += kGroups * kU) {
       const float* cp[kU];
@@ -493,6 +507,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
       if (ct == 0) {
         __threadfence_block();
         *reinterpret_cast<volatile int*>(&s_ready) = min(nmid, r0 + kGroups * kU);
+        PHASE_MARK(layer == 1 && b == 0 && r0 / (kGroups * kU) < 8, 40 + r0 / (kGroups * kU));
       }
     }
     PHASE_MARK(ct == 0 && layer == 1, 1);
