@@ -975,10 +975,10 @@ __global__ void __launch_bounds__(kAttnThreads, VF ? 1 : 3)
 //   2. each K row is read once and decoded once for all query heads of the
 //      group; the dots keep the reference's 8-lane order per head;
 //   3. running max per head by a 128-thread max-scan, both exponentials;
-//   4. thread (head j, dimensions 4c..4c+3) runs four output recurrences
-//      o_t = fma(e_t, v_t, o_{t-1} * f_t) as paired f32x2 operations, the
-//      first thread of each head also the denominator.
-// 128 threads per query head of the group; hd / 4 of them run recurrences.
+//   4. thread d runs dimension d of every query head's output recurrence
+//      o_t = fma(e_t, v_t, o_{t-1} * f_t), dequantising each V element once
+//      for all of them; thread 0 also runs the denominators.
+// 128 threads per query head of the group; hd of them run recurrences.
 struct GroupSmemLayout {
   size_t qs, sc, sf, tks, tvs, trow, boff, bphys, bfill, ones, vraw, total;
   int ld;
@@ -1051,6 +1051,9 @@ __global__ void __launch_bounds__(128 * HPG, 1)
   }
   pdl_launch_dependents();
   pdl_wait();
+  const bool mk = g == 0 && b == 0 && layer == 0;
+  (void)mk;
+  PHASE_MARK(mk && tid == 0, 48);
   const int pos = step_pos(sb, b);
   const float* qg = sb.qrot + (long)b * H * hd + (long)h0 * hd;
   for (int d = tid; d < hpg * hd; d += blockDim.x) qs[d] = qg[d];
@@ -1100,6 +1103,10 @@ __global__ void __launch_bounds__(128 * HPG, 1)
       trow[i] = row;
       tks[i] = kv.ks[row];
       tvs[i] = kv.vs[row];
+      // the K row (hd bytes) on its way to L2 while V copies and the table finish
+      for (int off = 0; off < hd; off += 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(
+            reinterpret_cast<const uint8_t*>(kv.kq) + (size_t)row * hd + off));
     }
   }
   // padding tokens [T, Tp): e = 0, f = 1 leave every recurrence unchanged
@@ -1116,6 +1123,7 @@ __global__ void __launch_bounds__(128 * HPG, 1)
     cp_async_arrive(&vbar);
   }
 
+  PHASE_MARK(mk && tid == 0, 49);
   // ------------------------------------- scores: one K row, every head
   {
     const int npc = hd >> 4;
@@ -1132,9 +1140,16 @@ __global__ void __launch_bounds__(128 * HPG, 1)
         for (int j = 0; j < JB; j++)
 #pragma unroll
           for (int l = 0; l < 4; l++) acc[j][l] = 0;
-        for (int c = 0; c < npc; c++) {
-          // piece c of this token's row sits at (c + t) mod npc (stored rotated)
-          const uint4 u = ldg_nc16(kr + (((c + t) & (npc - 1)) << 4));
+        // the whole K row first (piece c sits at (c + t) mod npc: stored
+        // rotated), so its loads overlap
+        uint4 ur[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+          if (c < npc) ur[c] = ldg_nc16(kr + (((c + t) & (npc - 1)) << 4));
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          if (c >= npc) break;
+          const uint4 u = ur[c];
           const uint32_t wv[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
           for (int gq = 0; gq < 4; gq++) {
@@ -1166,6 +1181,7 @@ __global__ void __launch_bounds__(128 * HPG, 1)
   }
   __syncthreads();
 
+  PHASE_MARK(mk && tid == 0, 50);
   // ------------- running max per head (threads 128j .. 128j + 127), exps
   {
     const int j = tid >> 7, ht = tid & 127;
@@ -1201,6 +1217,7 @@ __global__ void __launch_bounds__(128 * HPG, 1)
     }
   }
   __syncthreads();
+  PHASE_MARK(mk && tid == 0, 51);
   // flag per head per 32 tokens: every scale factor is 1
   for (int w = tid; w < hpg * (Tp >> 5); w += blockDim.x) {
     const int j = w / (Tp >> 5), gq = w - j * (Tp >> 5);
@@ -1210,63 +1227,66 @@ __global__ void __launch_bounds__(128 * HPG, 1)
   }
   const bool ok = __syncthreads_and(mbar_wait(&vbar, 0, sb.err));
 
+  PHASE_MARK(mk && tid == 0, 52);
   // --------------------------------------------------------- recurrences
-  const int q4 = hd >> 2;  // threads per head
-  const bool chainer = tid < hpg * q4 && ok;
-  const int j = tid / q4, d0 = (tid - j * q4) * 4;
-  const bool lead = d0 == 0;
-  uint64_t o01 = 0, o23 = 0;
-  if (chainer) {
-    const float* scj = sc + j * ld;
-    const float* sfj = sf + j * ld;
-    const int* onej = ones + j * (ld / 32);
-    float sum = 0.0f;
-    for (int i0 = 0; i0 < Tp; i0 += 32) {
-      const bool one = onej[i0 >> 5] != 0;
-#pragma unroll 2
-      for (int i = i0; i < i0 + 32; i += 4) {
-        const float4 e4 = *reinterpret_cast<const float4*>(scj + i);
-        const float4 t4 = *reinterpret_cast<const float4*>(tvs + i);
-        const float4 f4 = *reinterpret_cast<const float4*>(sfj + i);
-        uint32_t w[4];
+  // thread d (< hd) runs dimension d of every query head of the group: the
+  // V element is dequantised once per token (v * scale_t, exact) and feeds
+  // hpg independent chains o_t = fma(e_t, v_t, o_{t-1} * f_t); thread 0 also
+  // runs the denominators
+  const bool chainer = tid < hd && ok;
+  const int d = tid;
+  const bool lead = d == 0;
+  float o[HPG], sum[HPG];
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-          w[k] = *reinterpret_cast<const uint32_t*>(vraw + (size_t)(i + k) * hd + d0);
-        const float ev[4] = {e4.x, e4.y, e4.z, e4.w};
+  for (int jj = 0; jj < HPG; jj++) o[jj] = sum[jj] = 0.0f;
+  if (chainer) {
+    for (int i0 = 0; i0 < Tp; i0 += 32) {
+      bool one[HPG];
+#pragma unroll
+      for (int jj = 0; jj < HPG; jj++) one[jj] = ones[jj * (ld / 32) + (i0 >> 5)] != 0;
+      // this chunk's V bytes first, so no load sits on the chains
+      uint32_t wc[32];
+#pragma unroll
+      for (int k = 0; k < 32; k++) wc[k] = vraw[(size_t)(i0 + k) * hd + d];
+#pragma unroll
+      for (int i = i0; i < i0 + 32; i += 4) {
+        const float4 t4 = *reinterpret_cast<const float4*>(tvs + i);
         const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
-        const float fv[4] = {f4.x, f4.y, f4.z, f4.w};
+        float ev[HPG][4], fv[HPG][4];
+#pragma unroll
+        for (int jj = 0; jj < HPG; jj++) {
+          const float4 e4 = *reinterpret_cast<const float4*>(sc + jj * ld + i);
+          const float4 f4 = *reinterpret_cast<const float4*>(sf + jj * ld + i);
+          ev[jj][0] = e4.x; ev[jj][1] = e4.y; ev[jj][2] = e4.z; ev[jj][3] = e4.w;
+          fv[jj][0] = f4.x; fv[jj][1] = f4.y; fv[jj][2] = f4.z; fv[jj][3] = f4.w;
+        }
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-          uint64_t v01, v23;
-          decode_pairs<EC_W_INT8>(w[k], v01, v23);
-          const uint64_t t2 = pack2(__float_as_uint(tv[k]), __float_as_uint(tv[k]));
-          v01 = mul2(v01, t2);
-          v23 = mul2(v23, t2);
-          const uint64_t e2 = pack2(__float_as_uint(ev[k]), __float_as_uint(ev[k]));
-          if (!one) {
-            const uint64_t f2 = pack2(__float_as_uint(fv[k]), __float_as_uint(fv[k]));
-            o01 = mul2(o01, f2);
-            o23 = mul2(o23, f2);
+          const float v = __fmul_rn(s8_to_f32(wc[i - i0 + k]), tv[k]);
+#pragma unroll
+          for (int jj = 0; jj < HPG; jj++) {
+            const float prev = one[jj] ? o[jj] : __fmul_rn(o[jj], fv[jj][k]);
+            o[jj] = __fmaf_rn(ev[jj][k], v, prev);
+            if (lead) sum[jj] = __fmaf_rn(sum[jj], fv[jj][k], ev[jj][k]);
           }
-          fma2(o01, e2, v01);
-          fma2(o23, e2, v23);
-          if (lead) sum = __fmaf_rn(sum, fv[k], ev[k]);
         }
       }
     }
-    if (lead) s_sum[j] = sum;
-  }
-  __syncthreads();
-  if (chainer) {
-    const float sm = s_sum[j];
-    float r4[4] = {lo_f(o01), hi_f(o01), lo_f(o23), hi_f(o23)};
-    if (sm > 0.0f) {
-      const float inv = __fdiv_rn(1.0f, sm);
+    if (lead)
 #pragma unroll
-      for (int k = 0; k < 4; k++) r4[k] = __fmul_rn(r4[k], inv);
+      for (int jj = 0; jj < HPG; jj++) s_sum[jj] = sum[jj];
+  }
+  PHASE_MARK(mk && tid == 0, 53);
+  __syncthreads();
+  PHASE_MARK(mk && tid == 0, 54);
+  if (chainer) {
+#pragma unroll
+    for (int jj = 0; jj < HPG; jj++) {
+      const float sm = s_sum[jj];
+      float r = o[jj];
+      if (sm > 0.0f) r = __fmul_rn(r, __fdiv_rn(1.0f, sm));
+      sb.att[(long)b * H * hd + (long)(h0 + jj) * hd + d] = r;
     }
-    *reinterpret_cast<float4*>(sb.att + (long)b * H * hd + (long)(h0 + j) * hd + d0) =
-        make_float4(r4[0], r4[1], r4[2], r4[3]);
   }
 }
 
