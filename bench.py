@@ -280,17 +280,6 @@ def run_cuda(args):
     # roofline of the dominant kernel: its algorithmic bytes per launch over its
     # event-timed average launch duration
     tot_ms = sum(v["ms"] for v in prof.values())
-    dom = max(prof, key=lambda k: prof[k]["ms"])
-    d = prof[dom]
-    peak, peak_kind = peaks()
-    achieved = (d["bytes"] / d["launches"]) / (d["ms"] / d["launches"] * 1e-3) / 1e9 \
-        if d["launches"] and d["bytes"] else 0.0
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "roofline_traffic.json")
-    if os.path.exists(tpath) and not big and B == 1:
-        tj = json.load(open(tpath))  # measured on the 8B b=1 chain launch
-        if tj.get("kernel") == dom:
-            traffic = tj["traffic_bytes_per_launch"]
     weight_bytes = (sum(int(np.prod(s)) for s in S.mat_shapes(cfg).values()) * cfg.n_layers
                     + cfg.vocab_size * cfg.dim)
     if big:
@@ -301,6 +290,22 @@ def run_cuda(args):
     else:
         kv_tok = cfg.n_layers * cfg.n_kv_heads * (cfg.head_dim * 2 + 8)
         att_tokens = min(args.prompt + args.warmup + args.steps, 64 * 16)
+    dom = max(prof, key=lambda k: prof[k]["ms"])
+    d = dict(prof[dom])
+    if dom == "attention" and not d["bytes"] and d["launches"]:
+        # the attention launches record no bytes: K and V (with scales) of
+        # the attended tokens of every sequence, one layer per launch
+        d["bytes"] = d["launches"] * B * (kv_tok / cfg.n_layers) * att_tokens
+    peak, peak_kind = peaks()
+    achieved = (d["bytes"] / d["launches"]) / (d["ms"] / d["launches"] * 1e-3) / 1e9 \
+        if d["launches"] and d["bytes"] else 0.0
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(tpath) and not big:
+        # ncu DRAM bytes per launch of the same kernel at the same batch (8B shape)
+        tj = json.load(open(tpath)).get(f"{dom}@{B}")
+        if tj:
+            traffic = tj["traffic_bytes_per_launch"]
     step_bytes = weight_bytes + B * kv_tok * att_tokens
 
     if rank == 0:
