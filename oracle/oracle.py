@@ -143,7 +143,7 @@ def ref_available():
 
 
 def ref():
-    """The reference engine's own code (built here from /root/reference)."""
+    """The reference engine's own code, compiled from its sources by oracle/Makefile."""
     global _ref
     if _ref is None:
         lib = C.CDLL(REF_SO)
