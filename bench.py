@@ -116,9 +116,31 @@ def dist_setup():
     return _load("dp").rank_env()
 
 
+class _StdoutToStderr:
+    """Send file descriptor 1 to stderr while the reference's C code runs (it
+    prints its own progress lines), so stdout carries only the JSON line."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self._saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self._saved, 1)
+        os.close(self._saved)
+        return False
+
+
 def cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads):
     """The reference's transformer_forward on the host (oracle/_ref), or the
     C restatement when the reference was not built here."""
+    with _StdoutToStderr():
+        return _cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads)
+
+
+def _cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads):
     os.environ["OMP_NUM_THREADS"] = str(threads)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # CPU baseline leg only
