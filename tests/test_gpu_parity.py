@@ -422,13 +422,15 @@ def test_batched_chain_matches_oracle(eng, torch, oracle, synth, B):
     e.close()
 
 
-def test_group_attention_hd128_sparse(eng, torch, oracle, synth):
+@pytest.mark.parametrize("heads,hd", [(4, 128), (8, 64)])
+def test_group_attention_sparse(eng, torch, oracle, synth, heads, hd):
     """Batched steps (B >= 4) run one attention CTA per (KV head, sequence)
     for all query heads of the group.  Llama-like geometry (4 query heads per
-    KV head, head_dim 128), past SPARSE_BLOCKS_K blocks so the block-sparse
-    order matters: every checked step's logits bit-identical per sequence."""
-    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=4, n_kv_heads=1,
-                            vocab_size=2048, seq_len=2048, head_dim=128, rope_theta=5e5)
+    KV head, head_dim 128) and the 70B shape's 8 query heads per KV head,
+    past SPARSE_BLOCKS_K blocks so the block-sparse order matters: every
+    checked step's logits bit-identical per sequence."""
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=heads, n_kv_heads=1,
+                            vocab_size=2048, seq_len=2048, head_dim=hd, rope_theta=5e5)
     model = synth.make_model(cfg, seed=31)
     B = 4
     e = eng.Engine(cfg, max_batch=B)
