@@ -369,7 +369,7 @@ def run_cuda(args):
                                     "kind": "reference",
                                     "sample": "unavailable: the reference's BF16 copy of the "
                                               "70B shape (~140 GB) exceeds host memory"}
-        elif not args.no_cpu_baseline:
+        elif not args.no_cpu_baseline and ws == 1:  # rank 0, one GPU only
             del src
             torch.cuda.empty_cache()
             threads = os.cpu_count() or 1
