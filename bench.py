@@ -116,6 +116,19 @@ def dist_setup():
     return _load("dp").rank_env()
 
 
+_JSON_FD = None  # the process's original stdout; everything else goes to stderr
+
+
+def emit(line):
+    """The bench's one JSON line, on the original stdout."""
+    data = (json.dumps(line) + "\n").encode()
+    if _JSON_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, data)
+
+
 class _StdoutToStderr:
     """Send file descriptor 1 to stderr while the reference's C code runs (it
     prints its own progress lines), so stdout carries only the JSON line."""
@@ -196,7 +209,7 @@ def run_reference(args):
                              "kind": kind, "sample": sample},
             "e2e": {"value": round(val, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 class _HostWeights:
@@ -385,12 +398,19 @@ def run_cuda(args):
             except Exception as exc:
                 line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": threads,
                                         "kind": "reference", "sample": f"failed: {exc}"}
-        print(json.dumps(line), flush=True)
+        emit(line)
     e.close()
     dp.finish()
 
 
 def main():
+    # libraries and the reference engine print to stdout (NCCL's banner, the
+    # reference's progress lines): send file descriptor 1 to stderr for the
+    # whole run and keep the original for the JSON line
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
