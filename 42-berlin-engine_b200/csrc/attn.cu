@@ -82,6 +82,18 @@ __device__ float warp_quant_int8(const float* in, int8_t* out, int n, int lane, 
 // ------------------------------------------------------------------------
 __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int layer, int b);
 
+// calc_block_centroid_int8 (paged.c:350-393): KV head 0 mean of a full block
+__device__ __forceinline__ void block_centroid(const KvLayout& kv, long blk, int tid, int nt) {
+  const int KV = kv.n_kv_heads, hd = kv.head_dim;
+  for (int d = tid; d < hd; d += nt) {
+    float c = 0.0f;
+    for (int t = 0; t < kBlk; t++)
+      c = __fadd_rn(c, __fmul_rn((float)kv.kq[((blk * KV) * kBlk + t) * hd + kswz(t, d, hd)],
+                                 kv.ks[(blk * KV) * kBlk + t]));
+    kv.centroid[blk * hd + d] = __fmul_rn(c, __fdiv_rn(1.0f, (float)kBlk));
+  }
+}
+
 __global__ void __launch_bounds__(256, 4) kv_append_kernel(KvLayout kv, LshLayout lsh, StepBuffers sb,
                                                         int layer) {
   const int b = blockIdx.y;
@@ -123,7 +135,7 @@ __global__ void __launch_bounds__(256, 4) kv_append_kernel(KvLayout kv, LshLayou
   if (kv.paged) {
     const int lb = pos / kBlk, off = pos - lb * kBlk;
     if (lb < kv.max_blocks) {
-      const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
+      const long base = ((long)kv_seq(kv, b) * kv.n_layers + layer) * kv.max_blocks;
       const long blk = base + kv.page_table[base + lb];
       for (int h = warp; h < 2 * KV; h += nwarps) {
         const bool isv = h >= KV;
@@ -133,16 +145,7 @@ __global__ void __launch_bounds__(256, 4) kv_append_kernel(KvLayout kv, LshLayou
         if (lane == 0) (isv ? kv.vs : kv.ks)[(blk * KV + kh) * kBlk + off] = sc;
       }
       __syncthreads();
-      if (off == kBlk - 1) {
-        // calc_block_centroid_int8 (paged.c:350-393): KV head 0 mean
-        for (int d = tid; d < hd; d += blockDim.x) {
-          float c = 0.0f;
-          for (int t = 0; t < kBlk; t++)
-            c = __fadd_rn(c, __fmul_rn((float)kv.kq[((blk * KV) * kBlk + t) * hd + kswz(t, d, hd)],
-                                       kv.ks[(blk * KV) * kBlk + t]));
-          kv.centroid[blk * hd + d] = __fmul_rn(c, __fdiv_rn(1.0f, (float)kBlk));
-        }
-      }
+      if (off == kBlk - 1 && !sb.defer_centroid) block_centroid(kv, blk, tid, blockDim.x);
     }
   } else if (pos < kv.seq_len) {
     // kv_cache_append with F32 -> BF16 (kv_cache.c:55-75)
@@ -423,7 +426,7 @@ __device__ void paged_select_cta(const KvLayout& kv, const StepBuffers& sb, int 
   // into L2 before waiting for it (griddepcontrol.wait), while the previous
   // layer still runs.
   constexpr int kGroups = kScorers / 8, kU = 3, kD = 16;  // kD: hd / 8 at most
-  const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
+  const long base = ((long)kv_seq(kv, b) * kv.n_layers + layer) * kv.max_blocks;
   const int* pt = kv.page_table + base;
   const int nmid = nb - 2;
   for (int i = tid; i < nmid * (hd >> 5); i += blockDim.x) {
@@ -656,7 +659,7 @@ __global__ void __launch_bounds__(kAttnThreads, VF ? 1 : 3)
   if constexpr (PAGED) {
     const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
     const int nb = (n_tok + kBlk - 1) / kBlk;
-    const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
+    const long base = ((long)kv_seq(kv, b) * kv.n_layers + layer) * kv.max_blocks;
     const int* pt = kv.page_table + base;
     const int ns = sb.nsel[b];
     const int* sel = sb.sel + (long)b * sb.max_sel;
@@ -1062,7 +1065,7 @@ __global__ void __launch_bounds__(128 * HPG, 1)
   // ------------------------------------------------------ token table
   const int n_tok = min(pos + 1, kv.max_blocks * kBlk);
   const int nb = (n_tok + kBlk - 1) / kBlk;
-  const long base = ((long)b * kv.n_layers + layer) * kv.max_blocks;
+  const long base = ((long)kv_seq(kv, b) * kv.n_layers + layer) * kv.max_blocks;
   const int* pt = kv.page_table + base;
   const int ns = sb.nsel[b];
   const int* sel = sb.sel + (long)b * sb.max_sel;
@@ -1430,8 +1433,42 @@ cudaError_t launch_attention_n(const KvLayout& kv, const StepBuffers& sb, int ma
 
 cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                              int layer, int B, cudaStream_t s, bool pdl) {
-  return launch_ex(kv_append_kernel, dim3(kv.paged ? 2 : 1, B), dim3(256), 0, s, pdl, kv, lsh, sb,
+  // CTA 1 of each row selects blocks; a prefill launch selects after the
+  // centroids instead (launch_paged_select_rows)
+  return launch_ex(kv_append_kernel, dim3(kv.paged && !sb.defer_centroid ? 2 : 1, B), dim3(256), 0,
+                   s, pdl, kv, lsh, sb,
                    layer);
+}
+
+// One CTA per full block of the range.
+__global__ void __launch_bounds__(128) paged_centroid_kernel(KvLayout kv, int layer, int seq,
+                                                             int lb0) {
+  const int lb = lb0 + blockIdx.x;
+  const long base = ((long)seq * kv.n_layers + layer) * kv.max_blocks;
+  block_centroid(kv, base + kv.page_table[base + lb], threadIdx.x, blockDim.x);
+}
+
+// Block selection of batch row blockIdx.y at `layer`.
+__global__ void __launch_bounds__(256) paged_select_layer_kernel(KvLayout kv, StepBuffers sb,
+                                                                 int layer) {
+  paged_select_cta(kv, sb, layer, blockIdx.y);
+}
+
+cudaError_t launch_paged_centroids(const KvLayout& kv, int layer, int seq, int first_pos, int n,
+                                   cudaStream_t s) {
+  // blocks lb with first_pos <= 16 lb + 15 < first_pos + n
+  const int lb0 = first_pos / kBlk;                   // ceil((first_pos - 15) / 16)
+  const int lb1 = (first_pos + n) / kBlk;             // exclusive: 16 lb + 15 <= first_pos + n - 1
+  const int nblk = min(lb1, kv.max_blocks) - lb0;
+  if (nblk <= 0) return cudaSuccess;
+  paged_centroid_kernel<<<nblk, 128, 0, s>>>(kv, layer, seq, lb0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_select_rows(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
+                                     cudaStream_t s) {
+  paged_select_layer_kernel<<<dim3(1, B), 256, 0, s>>>(kv, sb, layer);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,

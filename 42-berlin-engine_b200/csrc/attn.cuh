@@ -21,7 +21,14 @@ struct KvLayout {
   uint16_t* lk;
   uint16_t* lv;
   int shared_cache;     // linear: every sequence index reads sequence 0's cache
+  int seq_plus1;        // paged prefill: every batch row addresses sequence
+                        // seq_plus1 - 1 (0: row b addresses sequence b)
 };
+
+// The sequence whose paged KV cache batch row b reads and writes.
+inline __host__ __device__ int kv_seq(const KvLayout& kv, int b) {
+  return kv.seq_plus1 ? kv.seq_plus1 - 1 : b;
+}
 
 struct LshLayout {
   int tables, bits, unit, max_units, radius, max_cand;
@@ -57,6 +64,8 @@ struct StepBuffers {
   int* lcand;
   float* lscore;
   int* lnc;
+  int defer_centroid;   // paged prefill: the append leaves block centroids to
+                        // launch_paged_centroids (rows of one launch share a block)
 };
 
 // Linear-mode candidate capacity per sequence: the window plus max_cand
@@ -77,6 +86,13 @@ cudaError_t attn_prepare(const KvLayout& kv, const LshLayout& lsh, const StepBuf
 // blocks to attend (it only reads blocks that this step does not change).
 cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                              int layer, int B, cudaStream_t s, bool pdl);
+// Paged prefill: block centroids of sequence `seq`, layer `layer`, for the
+// blocks whose last token lies in [first_pos, first_pos + n); then the block
+// selection of every batch row (after the centroids, unlike kv_append's CTA 1).
+cudaError_t launch_paged_centroids(const KvLayout& kv, int layer, int seq, int first_pos, int n,
+                                   cudaStream_t s);
+cudaError_t launch_paged_select_rows(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
+                                     cudaStream_t s);
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                                  int layer, int B, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int layer, int B,

@@ -436,6 +436,12 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
   if (!ctx || !data) return fail(EC_ERR_ARG, "null argument");
   const ec_model_config& c = ctx->c;
   cudaSetDevice(ctx->device);
+  // device data may still be in flight on the caller's streams (ctx->stream
+  // does not wait for them): let every prior device operation finish first
+  if (on_device) {
+    const cudaError_t e0 = cudaDeviceSynchronize();
+    if (e0 != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e0));
+  }
   const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   const cudaMemcpyKind skind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   const int D = c.dim, F = c.hidden_dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads;
@@ -607,7 +613,7 @@ ec::ChainPhase chain_phase(const Mat& m, int pro, int epi, const float* x, const
 // once for all B sequences; the weight-streaming GEMVs run as one batched
 // chain per layer per pack of up to kPack sequences.
 cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos, int B,
-                                 bool feedback) {
+                                 bool feedback, int prefill_seq = -1, int prefill_pos0 = 0) {
   const ec_model_config& c = ctx->c;
   const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
   const int V = c.vocab_size, L = c.n_layers, QW = (H + 2 * KV) * hd;
@@ -630,6 +636,12 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   sb.lcand = ctx->lcand;
   sb.lscore = ctx->lscore;
   sb.lnc = ctx->lnc;
+  // prefill: the B rows are consecutive tokens of one sequence (paged KV)
+  ec::KvLayout kv = ctx->kv;
+  if (prefill_seq >= 0) {
+    kv.seq_plus1 = prefill_seq + 1;
+    sb.defer_centroid = 1;
+  }
   auto phase = [&](const Mat& m, int pro, int epi, const float* x, int xs, const uint16_t* nw,
                    float* y, int ys) {
     ec::ChainPhase ph = chain_phase(m, pro, epi, x, nw, y);
@@ -686,17 +698,26 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   for (int l = 0; l < L; l++) {
     {
       ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
-      if ((e = ec::launch_kv_append(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
+      if ((e = ec::launch_kv_append(kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
       ctx->launches++;
     }
-    if (!ctx->kv.paged) {
+    if (prefill_seq >= 0) {
+      // every row's token is in the cache: the centroids of the blocks this
+      // chunk filled, then each row's block selection
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
-      if ((e = ec::launch_linear_select(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
+      if ((e = ec::launch_paged_centroids(kv, l, prefill_seq, prefill_pos0, B, ctx->stream)))
+        return e;
+      if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
+      ctx->launches += 2;
+    }
+    if (!kv.paged) {
+      ProfScope ps(ctx, EC_K_SELECT, 0.0);
+      if ((e = ec::launch_linear_select(kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
       ctx->launches += ec::kLinearSelectLaunches;
     }
     {
       ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
-      if ((e = ec::launch_attention(ctx->kv, sb, l, B, ctx->stream, true))) return e;
+      if ((e = ec::launch_attention(kv, sb, l, B, ctx->stream, true))) return e;
       ctx->launches++;
     }
     const bool last = l + 1 == L;
@@ -1091,6 +1112,42 @@ extern "C" int ec_decode_step(ec_ctx* ctx, const int* tokens, const int* pos, in
                                 cudaMemcpyDeviceToHost, ctx->stream));
   if (argmax_host)
     EC_CUDA_TRY(cudaMemcpyAsync(argmax_host, ctx->argmax, B * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (ctx->prof) prof_collect(ctx);
+  return check_err(ctx);
+}
+
+extern "C" int ec_prefill(ec_ctx* ctx, int seq, const int* tokens, int n, int pos0,
+                          float* logits_host, int* argmax_host) {
+  if (!ctx || !tokens || n <= 0) return fail(EC_ERR_ARG, "null argument or n <= 0");
+  const ec_model_config& c = ctx->c;
+  if (seq < 0 || seq >= c.max_batch) return fail(EC_ERR_ARG, "bad sequence");
+  if (pos0 < 0 || (long)pos0 + n > c.seq_len) return fail(EC_ERR_ARG, "positions past seq_len");
+  if (!ctx->kv.paged || !ctx->chain)
+    return fail(EC_ERR_UNSUPPORTED, "prefill needs paged KV and the chain GEMV layout");
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab_size) return fail(EC_ERR_ARG, "token out of range");
+  cudaSetDevice(ctx->device);
+  const int S = c.max_batch;
+  std::vector<int> pos(S);
+  int last_rows = 0;
+  for (int c0 = 0; c0 < n; c0 += S) {
+    const int C = n - c0 < S ? n - c0 : S;
+    for (int i = 0; i < C; i++) pos[i] = pos0 + c0 + i;
+    EC_CUDA_TRY(cudaMemcpyAsync(ctx->tokens, tokens + c0, C * 4, cudaMemcpyHostToDevice, ctx->stream));
+    EC_CUDA_TRY(cudaMemcpyAsync(ctx->pos, pos.data(), C * 4, cudaMemcpyHostToDevice, ctx->stream));
+    cudaError_t e = enqueue_step_batched(ctx, ctx->tokens, ctx->pos, C, false, seq, pos0 + c0);
+    if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+    // the host vectors above are read before the next chunk overwrites them
+    EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    last_rows = C;
+  }
+  if (logits_host)
+    EC_CUDA_TRY(cudaMemcpyAsync(logits_host, ctx->logits + (size_t)(last_rows - 1) * c.vocab_size,
+                                (size_t)c.vocab_size * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  if (argmax_host)
+    EC_CUDA_TRY(cudaMemcpyAsync(argmax_host, ctx->argmax + (last_rows - 1), 4,
+                                cudaMemcpyDeviceToHost, ctx->stream));
   EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   if (ctx->prof) prof_collect(ctx);
   return check_err(ctx);

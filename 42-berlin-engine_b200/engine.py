@@ -32,7 +32,7 @@ EXPORTS = [
     "ec_transformer_forward", "ec_transformer_argmax", "ec_transformer_reset",
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read", "ec_lsh_attn_create",
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
-    "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc",
+    "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
@@ -98,6 +98,7 @@ def lib():
             "ec_gemm_tc_bytes": (C.c_size_t, [i, i]),
             "ec_gemm_tc_pack": (i, [vp, vp, i, i, vp]),
             "ec_op_gemm_tc": (i, [vp, vp, vp, vp, i, i, i, vp]),
+            "ec_prefill": (i, [vp, i, vp, i, i, vp, vp]),
             "ec_op_gemv_packed": (i, [i, vp, vp, vp, vp, i, i, vp]),
             "ec_op_gemv_packed_batch": (i, [i, vp, vp, vp, vp, i, i, i, vp]),
             "ec_op_rmsnorm": (i, [vp, vp, vp, i, f, vp]),
@@ -239,6 +240,16 @@ class Engine:
             check(lib().ec_profile_read(self.h, k, C.byref(ms), C.byref(n), C.byref(by)))
             out[name] = dict(ms=ms.value, launches=n.value, bytes=by.value)
         return out
+
+    def prefill(self, seq, tokens, pos0=0):
+        """Tokens of one sequence as rows of batched steps; returns the last
+        token's logits and greedy token."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        lg = np.empty(self.c.vocab_size, np.float32)
+        am = np.empty(1, np.int32)
+        check(lib().ec_prefill(self.h, int(seq), _ptr(tokens), tokens.size, int(pos0), _ptr(lg),
+                               _ptr(am)))
+        return lg, int(am[0])
 
     def step_device(self, tokens_ptr, pos_ptr, B, feedback=True):
         check(lib().ec_decode_step_device(self.h, C.c_void_p(tokens_ptr), C.c_void_p(pos_ptr),

@@ -191,6 +191,18 @@ int		ec_gemv_pack(const void *w_rowmajor, void *w_packed, int m, int k,
 int		ec_op_gemv_packed(int wkind, const void *w_packed, const float *scale,
 			const float *x, float *y, int m, int k, void *stream);
 
+/* Prompt prefill for sequence `seq` (forward_prefill_batch,
+** src/inference/inference.c:718-1112): tokens[0..n) at positions
+** pos0..pos0+n-1 go through the model max_batch at a time as rows of one
+** batched step (each weight pass serves every row of a chunk), with every row
+** addressing `seq`'s paged KV cache; each row's KV append, block selection
+** and attention keep the decode step's arithmetic, so the cache and the
+** logits are bit-identical to decoding the tokens one at a time.  The last
+** token's logits and greedy token go to logits_host / argmax_host (either
+** may be NULL).  Paged KV mode only. */
+int		ec_prefill(ec_ctx *ctx, int seq, const int *tokens, int n, int pos0,
+			float *logits_host, int *argmax_host);
+
 /* op_matmul (src/compute/ops.h:33) for nb activation rows at once on the
 ** tensor cores, INT8 weights only (the large-batch decode and prefill path;
 ** the reference runs op_matmul once per row).  ec_gemm_tc_bytes gives the

@@ -445,3 +445,32 @@ def test_group_attention_sparse(eng, torch, oracle, synth, heads, hd):
             if check:
                 assert np.array_equal(bits(lg[b]), bits(want)), f"step {t} sequence {b}"
     e.close()
+
+
+@pytest.mark.parametrize("max_batch", [8, 3])
+def test_prefill_matches_sequential_decode(eng, torch, synth, max_batch):
+    """ec_prefill runs a 100-token prompt as rows of batched steps (chunks of
+    max_batch rows into one sequence's paged cache; the block selection is
+    active past 4 blocks) -- the last token's logits, and every decode step
+    after it, bit-identical to feeding the tokens one at a time."""
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4,
+                            vocab_size=2048, seq_len=512, head_dim=64, rope_theta=1e4)
+    model = synth.make_model(cfg, seed=41)
+    a = eng.Engine(cfg, max_batch=max_batch, sparse_blocks_k=4)
+    b = eng.Engine(cfg, max_batch=1, sparse_blocks_k=4)
+    a.load(model)
+    b.load(model)
+    prompt = [int(t) for t in synth.prompt(cfg, 100, seed=9)]
+    lg_a, tok_a = a.prefill(0, prompt)
+    for p, t in enumerate(prompt):
+        lg_b, am_b = b.step([t], [p])
+    assert np.array_equal(bits(lg_a), bits(lg_b[0])), "prompt logits"
+    assert tok_a == int(am_b[0])
+    tok = tok_a
+    for p in range(100, 106):
+        la, ama = a.step([tok], [p])
+        lb, amb = b.step([tok], [p])
+        assert np.array_equal(bits(la[0]), bits(lb[0])), f"decode step {p}"
+        tok = int(ama[0])
+    a.close()
+    b.close()
