@@ -94,6 +94,59 @@ __device__ __forceinline__ void block_centroid(const KvLayout& kv, long blk, int
   }
 }
 
+// lsh_update (ops_lsh.c:296-349) of sequence `seq` with one post-RoPE key
+// (layer 0, KV head 0) at position pos, by the whole CTA.
+__device__ void lsh_update_token(const LshLayout& lsh, int seq, const float* k, int pos, int hd) {
+  const int tid = threadIdx.x;
+  float* acc = lsh.acc + (long)seq * hd;
+  int* meta = lsh.meta + seq * 4;
+  __shared__ int s_count;
+  __shared__ uint32_t s_code[16];
+  if (tid == 0) {
+    if (meta[0] == 0) meta[1] = pos;
+    s_count = meta[0] + 1;
+  }
+  for (int d = tid; d < hd; d += blockDim.x) acc[d] = __fadd_rn(acc[d], k[d]);
+  __syncthreads();
+  const int count = s_count;
+  if (count >= lsh.unit) {
+    const float sc = __fdiv_rn(1.0f, (float)count);
+    for (int d = tid; d < hd; d += blockDim.x) acc[d] = __fmul_rn(acc[d], sc);
+    if (tid < 16) s_code[tid] = 0;
+    __syncthreads();
+    for (int tb = tid; tb < lsh.tables * lsh.bits; tb += blockDim.x) {
+      const int t = tb / lsh.bits, hbit = tb - t * lsh.bits;
+      const float* hp = lsh.hp + ((long)t * lsh.bits + hbit) * hd;
+      float a = 0.0f;
+      for (int d = 0; d < hd; d++) a = __fmaf_rn(acc[d], hp[d], a);
+      if (a > 0.0f) atomicOr(&s_code[t], 1u << hbit);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      const int nu = meta[2];
+      if (nu < lsh.max_units) {
+        lsh.unit_start[(long)seq * lsh.max_units + nu] = meta[1];
+        lsh.unit_len[(long)seq * lsh.max_units + nu] = count;
+        for (int t = 0; t < lsh.tables; t++) {
+          const long tb = (long)seq * lsh.tables + t;
+          const uint32_t code = s_code[t];
+          lsh.unit_hash[tb * lsh.max_units + nu] = code;
+          int* head = lsh.heads + (tb << lsh.bits) + code;
+          lsh.next[tb * lsh.max_units + nu] = *head;
+          *head = nu;
+        }
+        meta[2] = nu + 1;
+      }
+      meta[0] = 0;
+    }
+    __syncthreads();
+    for (int d = tid; d < hd; d += blockDim.x) acc[d] = 0.0f;
+  } else if (tid == 0) {
+    meta[0] = count;
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(256, 4) kv_append_kernel(KvLayout kv, LshLayout lsh, StepBuffers sb,
                                                         int layer) {
   const int b = blockIdx.y;
@@ -156,55 +209,9 @@ __global__ void __launch_bounds__(256, 4) kv_append_kernel(KvLayout kv, LshLayou
     }
   }
 
-  // lsh_update (ops_lsh.c:296-349), layer 0, KV head 0 key
-  if (layer == 0 && lsh.tables > 0) {
-    float* acc = lsh.acc + (long)b * hd;
-    int* meta = lsh.meta + b * 4;
-    __shared__ int s_count;
-    __shared__ uint32_t s_code[16];
-    if (tid == 0) {
-      if (meta[0] == 0) meta[1] = pos;
-      s_count = meta[0] + 1;
-    }
-    for (int d = tid; d < hd; d += blockDim.x) acc[d] = __fadd_rn(acc[d], k[d]);
-    __syncthreads();
-    const int count = s_count;
-    if (count >= lsh.unit) {
-      const float sc = __fdiv_rn(1.0f, (float)count);
-      for (int d = tid; d < hd; d += blockDim.x) acc[d] = __fmul_rn(acc[d], sc);
-      if (tid < 16) s_code[tid] = 0;
-      __syncthreads();
-      for (int tb = tid; tb < lsh.tables * lsh.bits; tb += blockDim.x) {
-        const int t = tb / lsh.bits, hbit = tb - t * lsh.bits;
-        const float* hp = lsh.hp + ((long)t * lsh.bits + hbit) * hd;
-        float a = 0.0f;
-        for (int d = 0; d < hd; d++) a = __fmaf_rn(acc[d], hp[d], a);
-        if (a > 0.0f) atomicOr(&s_code[t], 1u << hbit);
-      }
-      __syncthreads();
-      if (tid == 0) {
-        const int nu = meta[2];
-        if (nu < lsh.max_units) {
-          lsh.unit_start[(long)b * lsh.max_units + nu] = meta[1];
-          lsh.unit_len[(long)b * lsh.max_units + nu] = count;
-          for (int t = 0; t < lsh.tables; t++) {
-            const long tb = (long)b * lsh.tables + t;
-            const uint32_t code = s_code[t];
-            lsh.unit_hash[tb * lsh.max_units + nu] = code;
-            int* head = lsh.heads + (tb << lsh.bits) + code;
-            lsh.next[tb * lsh.max_units + nu] = *head;
-            *head = nu;
-          }
-          meta[2] = nu + 1;
-        }
-        meta[0] = 0;
-      }
-      __syncthreads();
-      for (int d = tid; d < hd; d += blockDim.x) acc[d] = 0.0f;
-    } else if (tid == 0) {
-      meta[0] = count;
-    }
-  }
+  // lsh_update (ops_lsh.c:296-349), layer 0, KV head 0 key.  Prefill rows
+  // are tokens of one sequence: lsh_update_rows_kernel applies them in order.
+  if (layer == 0 && lsh.tables > 0 && !kv.seq_plus1) lsh_update_token(lsh, b, k, pos, hd);
   PHASE_MARK(tid == 0 && layer == 1 && b == 0, 6);
 }
 
@@ -1462,6 +1469,23 @@ cudaError_t launch_paged_centroids(const KvLayout& kv, int layer, int seq, int f
   const int nblk = min(lb1, kv.max_blocks) - lb0;
   if (nblk <= 0) return cudaSuccess;
   paged_centroid_kernel<<<nblk, 128, 0, s>>>(kv, layer, seq, lb0);
+  return cudaGetLastError();
+}
+
+// Prefill: the LSH update of every row (consecutive tokens of sequence
+// seq_plus1 - 1) in row order, by one CTA, after the append rotated the keys.
+__global__ void __launch_bounds__(256) lsh_update_rows_kernel(KvLayout kv, LshLayout lsh,
+                                                              StepBuffers sb, int B) {
+  const int H = kv.n_heads, KV = kv.n_kv_heads, hd = kv.head_dim;
+  for (int r = 0; r < B; r++)
+    lsh_update_token(lsh, kv_seq(kv, r), sb.qkv + (long)r * (H + 2 * KV) * hd + H * hd,
+                     step_pos(sb, r), hd);
+}
+
+cudaError_t launch_lsh_update_rows(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
+                                   int B, cudaStream_t s) {
+  if (lsh.tables <= 0) return cudaSuccess;
+  lsh_update_rows_kernel<<<1, 256, 0, s>>>(kv, lsh, sb, B);
   return cudaGetLastError();
 }
 

@@ -91,6 +91,10 @@ cudaError_t launch_kv_append(const KvLayout& kv, const LshLayout& lsh, const Ste
 // selection of every batch row (after the centroids, unlike kv_append's CTA 1).
 cudaError_t launch_paged_centroids(const KvLayout& kv, int layer, int seq, int first_pos, int n,
                                    cudaStream_t s);
+// Paged prefill, layer 0: the LSH index update of every batch row in row
+// order (kv_append skips it when rows share a sequence).
+cudaError_t launch_lsh_update_rows(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
+                                   int B, cudaStream_t s);
 cudaError_t launch_paged_select_rows(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
                                      cudaStream_t s);
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,

@@ -707,6 +707,10 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
       if ((e = ec::launch_paged_centroids(kv, l, prefill_seq, prefill_pos0, B, ctx->stream)))
         return e;
+      if (l == 0) {
+        if ((e = ec::launch_lsh_update_rows(kv, ctx->lsh, sb, B, ctx->stream))) return e;
+        if (ctx->lsh.tables > 0) ctx->launches++;
+      }
       if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
       ctx->launches += 2;
     }

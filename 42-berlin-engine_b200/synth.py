@@ -226,7 +226,9 @@ class DeviceModel:
 
         def sink(kind, layer, name, t, s):
             if kind == "mat":
-                v = host_bf16((t.to(torch.float32) * s[:, None]).to(torch.bfloat16))
+                w = (t.view(torch.float8_e4m3fn).to(torch.float32) if self.kind == "fp8"
+                     else t.to(torch.float32))
+                v = host_bf16((w * s[:, None]).to(torch.bfloat16))
             else:
                 v = host_bf16(t)
             if layer < 0:

@@ -8,7 +8,7 @@ copies that every launch reads its matrix from HBM (> 126 MB of L2), and report
 GB/s of algorithmic bytes (N*K weights + scales + 4K x + 4N y) against the
 measured HBM peak.  One JSON line per case.
 
-  python 42-berlin-engine_b200/gemv_sweep.py [--kinds int8,fp8] [--shapes 4096x4096,...]
+  python gemv_sweep.py [--kinds int8,fp8] [--shapes 4096x4096,...]
         [--iters 50] [--warmup 5]
 """
 import argparse
@@ -17,15 +17,15 @@ import json
 import os
 import sys
 
-HERE = os.path.dirname(os.path.abspath(__file__))
-ROOT = os.path.dirname(HERE)
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "42-berlin-engine_b200")
 
 
 def _load(name):
     key = "ec_" + name
     if key in sys.modules:
         return sys.modules[key]
-    spec = importlib.util.spec_from_file_location(key, os.path.join(HERE, name + ".py"))
+    spec = importlib.util.spec_from_file_location(key, os.path.join(PKG, name + ".py"))
     mod = importlib.util.module_from_spec(spec)
     sys.modules[key] = mod
     spec.loader.exec_module(mod)

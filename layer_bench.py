@@ -2,7 +2,7 @@
 but few layers and a small vocabulary (a small case for profilers: a few
 hundred MB on the device).
 
-  python 42-berlin-engine_b200/layer_bench.py [--layers 2] [--prompt 2048]
+  python layer_bench.py [--layers 2] [--prompt 2048]
         [--steps 20] [--paged 1] [--vocab 4096] [--batch 1] [--tensor-min-batch 16]
 
 Prints one JSON line: ms per step (graph replay, CUDA events) and the
@@ -14,14 +14,15 @@ import json
 import os
 import sys
 
-HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "42-berlin-engine_b200")
 
 
 def _load(name):
     key = "ec_" + name
     if key in sys.modules:
         return sys.modules[key]
-    spec = importlib.util.spec_from_file_location(key, os.path.join(HERE, name + ".py"))
+    spec = importlib.util.spec_from_file_location(key, os.path.join(PKG, name + ".py"))
     mod = importlib.util.module_from_spec(spec)
     sys.modules[key] = mod
     spec.loader.exec_module(mod)

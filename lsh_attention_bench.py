@@ -13,7 +13,7 @@ stream, L2 flushed between calls), queries/s, recall, and algorithmic bytes
 per query over time: code reads (tables x 4 bytes per unit) + candidate K
 reads (candidates x KV x hd x 2) + selected K and V (2 x top_k x KV x hd x 2).
 
-  python 42-berlin-engine_b200/lsh_attention_bench.py [--tokens 4096,32768,131072]
+  python lsh_attention_bench.py [--tokens 4096,32768,131072]
         [--queries 1,32] [--iters 10] [--cpu]   # --cpu: the restatement on one query
 """
 import argparse
@@ -26,15 +26,15 @@ import time
 
 import numpy as np
 
-HERE = os.path.dirname(os.path.abspath(__file__))
-ROOT = os.path.dirname(HERE)
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "42-berlin-engine_b200")
 
 
 def _load(name):
     key = "ec_" + name
     if key in sys.modules:
         return sys.modules[key]
-    spec = importlib.util.spec_from_file_location(key, os.path.join(HERE, name + ".py"))
+    spec = importlib.util.spec_from_file_location(key, os.path.join(PKG, name + ".py"))
     mod = importlib.util.module_from_spec(spec)
     sys.modules[key] = mod
     spec.loader.exec_module(mod)

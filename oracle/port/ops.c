@@ -5,8 +5,9 @@
 ** fmaf(), placed exactly where the reference's AVX2 intrinsics (or gcc's
 ** contraction of its scalar C under -O3 -mfma) fuse.  The placement of the
 ** compiler-contracted ones was established by input/output comparison with
-** the reference build (tests/test_oracle_pin.py), not by reading its
-** generated code.
+** the reference build (the golden vectors that tests/golden/make_golden.py
+** writes from oracle/_ref, checked by tests/test_golden.py), not by reading
+** its generated code.
 */
 #include "port.h"
 #include <math.h>

@@ -5,7 +5,7 @@ Llama-3-8B shape, INT8, paged KV: a P-token random prompt for sequence 0 run
 decode), and (2) one token per ec_decode_step.  Prints one JSON line with
 tokens/s of each and the check that the last logits agree bit for bit.
 
-  python 42-berlin-engine_b200/prefill_bench.py [--prompt 2048] [--rows 64]
+  python prefill_bench.py [--prompt 2048] [--rows 64]
 """
 import argparse
 import importlib.util
@@ -16,14 +16,15 @@ import time
 
 import numpy as np
 
-HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "42-berlin-engine_b200")
 
 
 def _load(name):
     key = "ec_" + name
     if key in sys.modules:
         return sys.modules[key]
-    spec = importlib.util.spec_from_file_location(key, os.path.join(HERE, name + ".py"))
+    spec = importlib.util.spec_from_file_location(key, os.path.join(PKG, name + ".py"))
     mod = importlib.util.module_from_spec(spec)
     sys.modules[key] = mod
     spec.loader.exec_module(mod)
@@ -36,7 +37,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--rows", type=int, default=64, help="max_batch: rows per weight pass")
     args = ap.parse_args()
-    eng, S, lb = _load("engine"), _load("synth"), _load("layer_bench")
+    eng, S = _load("engine"), _load("synth")
+    import layer_bench as lb
     cfg = S.LLAMA3_8B
     prompt = [int(t) for t in S.prompt(cfg, args.prompt, seed=11)]
     out = {"workload": "llama3-8b-shape int8 prompt prefill", "prompt": args.prompt,

@@ -448,11 +448,14 @@ def test_group_attention_sparse(eng, torch, oracle, synth, heads, hd):
 
 
 @pytest.mark.parametrize("max_batch", [8, 3])
-def test_prefill_matches_sequential_decode(eng, torch, synth, max_batch):
-    """ec_prefill runs a 100-token prompt as rows of batched steps (chunks of
+def test_prefill_matches_sequential_decode(eng, torch, oracle, synth, max_batch):
+    """ec_prefill runs a 150-token prompt as rows of batched steps (chunks of
     max_batch rows into one sequence's paged cache; the block selection is
     active past 4 blocks) -- the last token's logits, and every decode step
-    after it, bit-identical to feeding the tokens one at a time."""
+    after it, bit-identical to feeding the tokens one at a time and to the
+    restatement.  The layer-0 LSH index (lsh_update runs on every token in
+    paged mode as well, inference.c:177-191) is built for the prefilled
+    sequence in token order and leaves the other sequences untouched."""
     cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4,
                             vocab_size=2048, seq_len=512, head_dim=64, rope_theta=1e4)
     model = synth.make_model(cfg, seed=41)
@@ -460,17 +463,38 @@ def test_prefill_matches_sequential_decode(eng, torch, synth, max_batch):
     b = eng.Engine(cfg, max_batch=1, sparse_blocks_k=4)
     a.load(model)
     b.load(model)
-    prompt = [int(t) for t in synth.prompt(cfg, 100, seed=9)]
+    pm = oracle.PortModel(model, sparse_blocks_k=4)
+    n = 150
+    prompt = [int(t) for t in synth.prompt(cfg, n, seed=9)]
+    other_before = a.lsh(1)
     lg_a, tok_a = a.prefill(0, prompt)
     for p, t in enumerate(prompt):
         lg_b, am_b = b.step([t], [p])
+        want = pm.forward(t, p)
     assert np.array_equal(bits(lg_a), bits(lg_b[0])), "prompt logits"
+    assert np.array_equal(bits(lg_a), bits(want)), "prompt logits against the restatement"
     assert tok_a == int(am_b[0])
+    la_idx, lb_idx = a.lsh(0), b.lsh(0)
+    assert la_idx["n_units"] == lb_idx["n_units"] == n // 64
+    for key in ("unit_hash", "unit_start", "unit_len", "heads", "next"):
+        assert np.array_equal(la_idx[key], lb_idx[key]), key
+    po = pm.lsh()
+    assert po.n_units == la_idx["n_units"]
+    for u in range(po.n_units):
+        assert po.unit_hash[u] == la_idx["unit_hash"][0, u]
+        assert po.unit_start[u] == la_idx["unit_start"][u]
+    other_after = a.lsh(1)
+    for key in ("unit_hash", "unit_start", "unit_len", "heads", "next"):
+        assert np.array_equal(np.asarray(other_before[key]), np.asarray(other_after[key])), key
+    assert other_after["n_units"] == other_before["n_units"]
+    assert a.counters(0) == b.counters(0)
     tok = tok_a
-    for p in range(100, 106):
+    for p in range(n, n + 6):
         la, ama = a.step([tok], [p])
         lb, amb = b.step([tok], [p])
+        want = pm.forward(tok, p)
         assert np.array_equal(bits(la[0]), bits(lb[0])), f"decode step {p}"
+        assert np.array_equal(bits(la[0]), bits(want)), f"decode step {p} against the restatement"
         tok = int(ama[0])
     a.close()
     b.close()
