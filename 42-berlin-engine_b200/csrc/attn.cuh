@@ -51,6 +51,7 @@ struct StepBuffers {
   float* att;           // [B][H * hd]
   int* sel;             // [B][L?] per-sequence selection scratch: [B][max_sel]
   int* nsel;            // [B]
+  int* selp;            // split attention: the selection's physical blocks [B][max_sel]
   int max_sel;
   const float* rope_cos;  // [seq_len][hd/2]
   const float* rope_sin;
@@ -66,6 +67,7 @@ struct StepBuffers {
   int* lnc;
   int defer_centroid;   // paged prefill: the append leaves block centroids to
                         // launch_paged_centroids (rows of one launch share a block)
+  int fast_tpc;         // split attention: tokens per CTA (set by its launcher)
 };
 
 // Linear-mode candidate capacity per sequence: the window plus max_cand
@@ -110,5 +112,17 @@ cudaError_t launch_paged_select(const KvLayout& kv, const StepBuffers& sb, cudaS
 cudaError_t launch_attention_n(const KvLayout& kv, const StepBuffers& sb, int max_tok,
                                cudaStream_t s);
 size_t attention_smem_bytes(int max_tok, int hd, bool paged);
+
+// Split attention (attn_fast.cu), paged KV: per layer one CTA per sequence
+// appends the token and selects the top-K block set by ranks, then a
+// cluster of `fast_splits` CTAs per (KV head, sequence) attends with the
+// reference's softmax weights and merges over distributed shared memory.
+bool fast_attention_supported(const KvLayout& kv, int sparse_blocks_k);
+int fast_splits(int B);
+cudaError_t fast_attention_prepare(const KvLayout& kv);
+cudaError_t launch_fast_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
+                               int layer, int B, cudaStream_t s, bool pdl);
+cudaError_t launch_fast_attend(const KvLayout& kv, StepBuffers sb, int layer, int B,
+                               cudaStream_t s, bool pdl);
 
 }  // namespace ec

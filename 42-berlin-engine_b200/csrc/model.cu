@@ -59,6 +59,7 @@ struct ec_ctx {
   float *x = nullptr, *qkvb = nullptr, *qrot = nullptr, *att = nullptr, *hbuf = nullptr,
         *logits = nullptr;
   int *argmax = nullptr, *tokens = nullptr, *pos = nullptr, *sel = nullptr, *nsel = nullptr;
+  int* selp = nullptr;  // split attention: physical blocks of the selection
   int *lcand = nullptr, *lnc = nullptr;  // linear mode: selection candidates per sequence
   float* lscore = nullptr;
   int cap_c = 0;
@@ -74,6 +75,7 @@ struct ec_ctx {
   int* tc_ws = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr, *hp = nullptr;
   int max_sel = 0;
+  int fast = 0;  // paged decode steps use the split attention (attention_mode)
   ec::PackedPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_lm{};
   // graph cache
   cudaGraphExec_t gexec = nullptr;
@@ -221,6 +223,8 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     return fail(EC_ERR_UNSUPPORTED, "sparse_blocks_k must be in 1..64 (select_top_k_blocks)");
   if (c.use_paged_kv && c.seq_len > 32768)
     return fail(EC_ERR_UNSUPPORTED, "paged KV supports seq_len <= 32768 (2048 blocks)");
+  if (c.attention_mode != EC_ATTN_REFERENCE && c.attention_mode != EC_ATTN_SPLIT)
+    return fail(EC_ERR_ARG, "attention_mode must be EC_ATTN_REFERENCE or EC_ATTN_SPLIT");
   if (!c.use_paged_kv && (c.sparse_k <= 0 || c.sparse_k > 511))
     return fail(EC_ERR_UNSUPPORTED, "linear KV mode needs sparse_k in 1..511");
   cudaError_t e = cudaSetDevice(device);
@@ -282,6 +286,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   TRY(dalloc(ctx, &ctx->pos, (size_t)S));
   ctx->max_sel = c.sparse_k > c.sparse_blocks_k + 2 ? c.sparse_k : c.sparse_blocks_k + 2;
   TRY(dalloc(ctx, &ctx->sel, (size_t)S * ctx->max_sel));
+  TRY(dalloc(ctx, &ctx->selp, (size_t)S * ctx->max_sel));
   TRY(dalloc(ctx, &ctx->nsel, (size_t)S));
   TRY(dalloc(ctx, &ctx->err, 1));
   TRY(cudaMemset(ctx->err, 0, sizeof(int)));
@@ -424,6 +429,15 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     TRY(ec::packed_prepare());
     TRY(ec::chain_prepare());
     TRY(ec::attn_prepare(ctx->kv, ctx->lsh, sb));
+  }
+  if (c.attention_mode != EC_ATTN_REFERENCE && ctx->kv.paged) {
+    if (!ec::fast_attention_supported(ctx->kv, c.sparse_blocks_k)) {
+      ec_destroy(ctx);
+      return fail(EC_ERR_UNSUPPORTED, "split attention: head_dim <= 128 (multiple of 16), <= 8 "
+                                      "KV heads, 1/2/4/8 query heads per KV head");
+    }
+    ctx->fast = c.attention_mode;
+    TRY(ec::fast_attention_prepare(ctx->kv));
   }
 #undef TRY
   *out = ctx;
@@ -609,6 +623,39 @@ ec::ChainPhase chain_phase(const Mat& m, int pro, int epi, const float* x, const
   return ph;
 }
 
+// One layer's attention block after the QKV projection: the split path
+// (append + rank selection, split attention) or the reference-order path
+// (append + heap selection | linear-mode selection, attention).
+cudaError_t enqueue_attention(ec_ctx* ctx, const ec::KvLayout& kv, const ec::LshLayout& lsh,
+                              ec::StepBuffers& sb, int l, int B, bool split) {
+  cudaError_t e;
+  if (split) {
+    {
+      ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
+      if ((e = ec::launch_fast_select(kv, lsh, sb, l, B, ctx->stream, true))) return e;
+    }
+    ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
+    if ((e = ec::launch_fast_attend(kv, sb, l, B, ctx->stream, true)))
+      return e;
+    ctx->launches += 2;
+    return cudaSuccess;
+  }
+  {
+    ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
+    if ((e = ec::launch_kv_append(kv, lsh, sb, l, B, ctx->stream, true))) return e;
+  }
+  ctx->launches++;
+  if (!kv.paged) {
+    ProfScope ps(ctx, EC_K_SELECT, 0.0);
+    if ((e = ec::launch_linear_select(kv, lsh, sb, l, B, ctx->stream, true))) return e;
+    ctx->launches += ec::kLinearSelectLaunches;
+  }
+  ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
+  if ((e = ec::launch_attention(kv, sb, l, B, ctx->stream, true))) return e;
+  ctx->launches++;
+  return cudaSuccess;
+}
+
 // The batched step (B > 1 with the chain): every sequence-parallel kernel runs
 // once for all B sequences; the weight-streaming GEMVs run as one batched
 // chain per layer per pack of up to kPack sequences.
@@ -632,6 +679,7 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   sb.qrot = ctx->qrot;
   sb.att = ctx->att;
   sb.sel = ctx->sel;
+  sb.selp = ctx->selp;
   sb.nsel = ctx->nsel;
   sb.lcand = ctx->lcand;
   sb.lscore = ctx->lscore;
@@ -695,8 +743,11 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
     }
     if ((e = run(P, L, pk, nb))) return e;
   }
+  const bool split = ctx->fast && prefill_seq < 0;
   for (int l = 0; l < L; l++) {
-    {
+    if (split) {
+      if ((e = enqueue_attention(ctx, kv, ctx->lsh, sb, l, B, true))) return e;
+    } else {
       ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
       if ((e = ec::launch_kv_append(kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
       ctx->launches++;
@@ -714,12 +765,12 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
       if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
       ctx->launches += 2;
     }
-    if (!kv.paged) {
+    if (!kv.paged && !split) {
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
       if ((e = ec::launch_linear_select(kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
       ctx->launches += ec::kLinearSelectLaunches;
     }
-    {
+    if (!split) {
       ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
       if ((e = ec::launch_attention(kv, sb, l, B, ctx->stream, true))) return e;
       ctx->launches++;
@@ -793,6 +844,7 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
   sb.qrot = ctx->qrot;
   sb.att = ctx->att;
   sb.sel = ctx->sel;
+  sb.selp = ctx->selp;
   sb.nsel = ctx->nsel;
   sb.lcand = ctx->lcand;
   sb.lscore = ctx->lscore;
@@ -850,21 +902,7 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
       return e;
   }
   for (int l = 0; l < L; l++) {
-    {
-      ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
-      if ((e = ec::launch_kv_append(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
-      ctx->launches++;
-    }
-    if (!ctx->kv.paged) {
-      ProfScope ps(ctx, EC_K_SELECT, 0.0);
-      if ((e = ec::launch_linear_select(ctx->kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
-      ctx->launches += ec::kLinearSelectLaunches;
-    }
-    {
-      ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
-      if ((e = ec::launch_attention(ctx->kv, sb, l, B, ctx->stream, true))) return e;
-      ctx->launches++;
-    }
+    if ((e = enqueue_attention(ctx, ctx->kv, ctx->lsh, sb, l, B, ctx->fast != 0))) return e;
     const bool last = l + 1 == L;
     for (int b0 = 0; b0 < B; b0 += ec::kTcMaxRows) {
       const int nb = B - b0 < ec::kTcMaxRows ? B - b0 : ec::kTcMaxRows;
@@ -920,6 +958,7 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
     sb.qrot = ctx->qrot + (size_t)b * H * hd;
     sb.att = ctx->att + (size_t)b * H * hd;
     sb.sel = ctx->sel + (size_t)b * ctx->max_sel;
+    sb.selp = ctx->selp + (size_t)b * ctx->max_sel;
     sb.nsel = ctx->nsel + b;
     if (ctx->lcand) {
       sb.lcand = ctx->lcand + (size_t)b * ctx->cap_c;
@@ -966,21 +1005,7 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
                       ctx->attn_norm[l], sb.qkv)))
           return e;
       }
-      {
-        ProfScope ps(ctx, EC_K_KV_APPEND, 4.0 * (H + 2 * KV) * hd * 2 + 2.0 * KV * hd);
-        if ((e = ec::launch_kv_append(kv, lsh, sb, l, 1, ctx->stream, true))) return e;
-      }
-      ctx->launches++;
-      if (!kv.paged) {
-        ProfScope ps(ctx, EC_K_SELECT, 0.0);
-        if ((e = ec::launch_linear_select(kv, lsh, sb, l, 1, ctx->stream, true))) return e;
-        ctx->launches += ec::kLinearSelectLaunches;
-      }
-      {
-        ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
-        if ((e = ec::launch_attention(kv, sb, l, 1, ctx->stream, true))) return e;
-      }
-      ctx->launches++;
+      if ((e = enqueue_attention(ctx, kv, lsh, sb, l, 1, ctx->fast != 0))) return e;
       if (chain) {
         // o (+x), gate/up (RMSNorm, SwiGLU), down (+x), then the next layer's
         // QKV or the LM head: one persistent kernel
@@ -1243,6 +1268,23 @@ extern "C" int ec_read_state(ec_ctx* ctx, int which, int seq, float* out, size_t
       if (n < 1) return fail(EC_ERR_ARG, "buffer too small");
       out[0] = (float)ns;
       for (int i = 0; i < ns && (size_t)(i + 1) < n; i++) out[i + 1] = (float)ids[i];
+      return EC_OK;
+    }
+    case 9: {
+      // paged KV: block centroids of the last layer in logical block order
+      // ([max_blocks][head_dim]), for checking the block selection
+      if (!ctx->kv.paged) return fail(EC_ERR_UNSUPPORTED, "centroids exist in paged mode only");
+      const size_t mb = ctx->kv.max_blocks, hd = c.head_dim;
+      if (n < mb * hd) return fail(EC_ERR_ARG, "buffer too small");
+      const size_t base = ((size_t)seq * c.n_layers + c.n_layers - 1) * mb;
+      std::vector<int> pt(mb);
+      std::vector<float> cen(mb * hd);
+      EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      EC_CUDA_TRY(cudaMemcpy(pt.data(), ctx->kv.page_table + base, mb * 4, cudaMemcpyDeviceToHost));
+      EC_CUDA_TRY(cudaMemcpy(cen.data(), ctx->kv.centroid + base * hd, mb * hd * 4,
+                             cudaMemcpyDeviceToHost));
+      for (size_t lb = 0; lb < mb; lb++)
+        memcpy(out + lb * hd, cen.data() + (size_t)pt[lb] * hd, hd * 4);
       return EC_OK;
     }
     default: return fail(EC_ERR_ARG, "unknown state id");

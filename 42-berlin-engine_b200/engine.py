@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "libengine_cuda.so")
 EC_OK, EC_ERR_ARG, EC_ERR_CUDA, EC_ERR_OOM, EC_ERR_STATE = 0, -1, -2, -3, -4
 EC_ERR_UNSUPPORTED, EC_ERR_TIMEOUT = -5, -6
 EC_W_INT8, EC_W_FP8, EC_W_BF16 = 0, 1, 2
+EC_ATTN_REFERENCE, EC_ATTN_SPLIT = 0, 1
 EC_WQ, EC_WK, EC_WV, EC_WO, EC_W1, EC_W2, EC_W3, EC_ATTN_NORM, EC_FFN_NORM = range(9)
 EC_EMBEDDING, EC_FINAL_NORM, EC_LM_HEAD = 16, 17, 18
 MAT_IDS = {"wq": EC_WQ, "wk": EC_WK, "wv": EC_WV, "wo": EC_WO, "w1": EC_W1, "w2": EC_W2,
@@ -45,7 +46,7 @@ class ModelConfig(C.Structure):
         (n, C.c_int) for n in (
             "weight_kind", "use_paged_kv", "sparse_k", "window", "sparse_blocks_k",
             "lsh_tables", "lsh_bits", "lsh_unit", "lsh_max_units", "lsh_radius",
-            "lsh_max_cand", "max_batch", "tensor_min_batch")]
+            "lsh_max_cand", "max_batch", "tensor_min_batch", "attention_mode")]
 
 
 class Transformer(C.Structure):

@@ -46,6 +46,8 @@ METRIC = "decode tok/s (Llama-3-8B-shaped INT8, b=1 per GPU, 2k context)"
 METRIC_B = "decode tok/s (Llama-3-8B-shaped INT8, b={} per GPU, 2k context)"
 METRIC_70B = "decode tok/s (70B-shaped FP8 per-tensor, b={} per GPU, {} context, LSH top-{})"
 PROMPT = 2048
+# --attention: the paged decode attention (engine_cuda.h attention_mode)
+ATTN_MODES = {"reference": 0, "split": 1}
 SEED = 1234
 
 
@@ -242,7 +244,8 @@ def run_cuda(args):
     else:
         cfg = S.LLAMA3_8B
         tmb = args.tensor_min_batch if B >= args.tensor_min_batch > 0 else 0
-        e = eng.Engine(cfg, device=local, max_batch=B, tensor_min_batch=tmb)
+        e = eng.Engine(cfg, device=local, max_batch=B, tensor_min_batch=tmb,
+                       attention_mode=ATTN_MODES[args.attention])
         src = S.DeviceModel(cfg, seed=SEED, device=local)
 
     def sink(kind, layer, name, t, s):
@@ -357,6 +360,7 @@ def run_cuda(args):
                        "weights": "fp8 e4m3 per-tensor pow2 scale" if big
                        else "int8 per-row pow2 scale",
                        "kv": f"linear bf16, LSH top-{args.sparse_k}" if big else "paged int8",
+                       "attention": "reference order" if big else args.attention,
                        "parallelism": f"dp{ws} (replicas)",
                        "gemm": "tcgen05 int8 (digit planes)" if (not big and tmb)
                        else "cuda-core gemv chain",
@@ -425,6 +429,9 @@ def main():
     ap.add_argument("--sparse-k", type=int, default=511, help="70b: LSH top-K (engine max 511)")
     ap.add_argument("--tensor-min-batch", type=int, default=16,
                     help="batches this large run their GEMMs on the tensor cores (0: never)")
+    ap.add_argument("--attention", default="reference", choices=sorted(ATTN_MODES),
+                    help="paged attention: reference order (bit-exact) or split (within "
+                         "tolerance, same block set)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

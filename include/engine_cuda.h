@@ -84,7 +84,20 @@ typedef struct ec_model_config
 							** their GEMMs on the tensor cores (ec_op_gemm_tc
 							** arithmetic: deterministic, not bit-identical
 							** to the reference); 0 = never (default) */
+	int		attention_mode;	/* paged KV decode attention:
+							** EC_ATTN_REFERENCE (default): the reference's
+							**   heap order and sequential online softmax,
+							**   bit-identical;
+							** EC_ATTN_SPLIT: the same top-K block set
+							**   (chosen by ranks, no heap replay), visited
+							**   in ascending block order, each KV head's
+							**   tokens split over a cluster of CTAs with
+							**   the reference's softmax weights (only the
+							**   additions are reordered) */
 }	ec_model_config;
+
+# define EC_ATTN_REFERENCE 0
+# define EC_ATTN_SPLIT 1
 
 typedef struct ec_ctx	ec_ctx;
 
@@ -154,7 +167,10 @@ int		ec_profile_enable(ec_ctx *ctx, int on);
 int		ec_profile_read(ec_ctx *ctx, int kind, double *ms, int *launches,
 			double *bytes);
 
-/* Introspection for parity checks (device -> host copies). */
+/* Introspection for parity checks (device -> host copies).  ec_read_state
+** `which`: 0 x, 2 rotated q, 3 rotated k, 4 v, 5 attention output, 6 logits,
+** 7 FFN hidden, 8 the last selection ([count, ids...] as floats), 9 paged
+** block centroids of the last layer in logical order ([max_blocks][hd]). */
 int		ec_read_state(ec_ctx *ctx, int which, int seq, float *out, size_t n);
 int		ec_read_lsh(ec_ctx *ctx, int seq, int *n_units, uint32_t *unit_hash,
 			int *unit_start, int *unit_len, int *heads, int *next);

@@ -54,6 +54,7 @@ def main():
     ap.add_argument("--sparse-k", type=int, default=64)
     ap.add_argument("--batch", type=int, default=1, help="sequences per step")
     ap.add_argument("--tensor-min-batch", type=int, default=16)
+    ap.add_argument("--attention", type=int, default=0, help="attention_mode (0 reference, 1 split)")
     args = ap.parse_args()
     B = args.batch
     eng, S = _load("engine"), _load("synth")
@@ -64,7 +65,7 @@ def main():
                         rope_theta=base.rope_theta)
     tmb = args.tensor_min_batch if B >= args.tensor_min_batch > 0 else 0
     e = eng.Engine(cfg, use_paged_kv=bool(args.paged), sparse_k=args.sparse_k, max_batch=B,
-                   tensor_min_batch=tmb)
+                   tensor_min_batch=tmb, attention_mode=args.attention)
     load_device_model(eng, e, S.DeviceModel(cfg, seed=3, device=0))
     torch.cuda.synchronize()
     toks = [S.prompt(cfg, args.prompt, seed=5 + b) for b in range(B)]

@@ -75,11 +75,23 @@ def _slice(synth, base, **over):
     return synth.ModelConfig(**d)
 
 
+def close_enough(got, want):
+    """BASELINE's tolerance: max |difference| <= 2e-2 of the logit range."""
+    return float(np.abs(got - want).max()) <= TOL * float(want.max() - want.min())
+
+
+TOL = 2e-2
+
+
 def _run(eng, torch, ref, synth, cfg, kind, paged, sparse_k, n_prompt, n_greedy, check_every,
-         check_from, sel_check=False):
+         check_from, sel_check=False, mode=0):
+    """mode 0: the reference-order path, bit-exact; otherwise the split
+    attention: logits within TOL of the range, the same selected block SET,
+    equal greedy tokens."""
     src = synth.DeviceModel(cfg, seed=77, device=0, kind=kind)
     e = eng.Engine(cfg, device=0, weight_kind=eng.EC_W_FP8 if kind == "fp8" else eng.EC_W_INT8,
-                   use_paged_kv=paged, sparse_k=sparse_k)
+                   use_paged_kv=paged, sparse_k=sparse_k, attention_mode=mode)
+    same = (lambda a, b: np.array_equal(bits(a), bits(b))) if mode == 0 else close_enough
     _load_device_model(eng, e, src)
     torch.cuda.synchronize()
     rm = ref.RefModel(_HostBF16(cfg, src.bf16_weights()), use_paged_kv=paged, sparse_k=sparse_k)
@@ -96,26 +108,41 @@ def _run(eng, torch, ref, synth, cfg, kind, paged, sparse_k, n_prompt, n_greedy,
         want = rm.forward(int(toks[pos]), pos)
         if not check:
             continue
-        assert np.array_equal(bits(lg[0]), bits(want)), f"prompt step {pos}"
+        assert same(lg[0], want), f"prompt step {pos}"
         if sel_check and pos >= 64 * 16 and pos % 8 == 0:
-            # select_top_k_blocks over the reference's centroids of the last
-            # layer with its query head 0 (score_blocks, paged.c:401-431)
-            q = np.ctypeslib.as_array(R.refd_state(rm.h, 2), (hd,)).copy()
-            kb = np.zeros(cfg.n_kv_heads * 16 * hd, np.int8)
-            vb = np.zeros_like(kb)
-            ks = np.zeros(cfg.n_kv_heads * 16, np.float32)
-            vs = np.zeros_like(ks)
-            cen = np.zeros(hd, np.float32)
-            scores = []
-            while R.refd_paged_block(rm.h, cfg.n_layers - 1, len(scores), kb, vb, ks, vs,
-                                     cen) >= 0:
-                scores.append(P.port_dot_f32(q, cen, hd))
+            if mode == 0:
+                # select_top_k_blocks over the reference's centroids of the
+                # last layer with its query head 0 (score_blocks, paged.c:401-431)
+                q = np.ctypeslib.as_array(R.refd_state(rm.h, 2), (hd,)).copy()
+                kb = np.zeros(cfg.n_kv_heads * 16 * hd, np.int8)
+                vb = np.zeros_like(kb)
+                ks = np.zeros(cfg.n_kv_heads * 16, np.float32)
+                vs = np.zeros_like(ks)
+                cen = np.zeros(hd, np.float32)
+                scores = []
+                while R.refd_paged_block(rm.h, cfg.n_layers - 1, len(scores), kb, vb, ks, vs,
+                                         cen) >= 0:
+                    scores.append(P.port_dot_f32(q, cen, hd))
+            else:
+                # the split path's caches drift from the reference's by
+                # rounding: the same selection rule on the engine's own query
+                # and centroids
+                q = e.state(2)[:hd].copy()
+                nb = (pos + 16) // 16
+                mb = (cfg.seq_len + 15) // 16
+                cens = e.state(9, n=mb * hd)[:nb * hd].reshape(nb, hd)
+                scores = [P.port_dot_f32(q, np.ascontiguousarray(cens[i]), hd) for i in range(nb)]
             sc = np.asarray(scores, np.float32)
             sel = np.zeros(70, np.int32)
             ns = P.port_select_blocks(sc, sc.size, 64, sel)
             got = e.state(8, n=80)
             assert int(got[0]) == ns, f"selected count at {pos}"
-            assert np.array_equal(got[1:1 + ns].astype(np.int32), sel[:ns]), f"selection at {pos}"
+            g = got[1:1 + ns].astype(np.int32)
+            if mode:
+                g, want_sel = np.sort(g), np.sort(sel[:ns])
+            else:
+                want_sel = sel[:ns]
+            assert np.array_equal(g, want_sel), f"selection at {pos}"
             n_sel_checked += 1
     # greedy continuation: the GPU picks the token, the reference must agree
     tok = P.port_argmax(want, want.size)
@@ -123,7 +150,7 @@ def _run(eng, torch, ref, synth, cfg, kind, paged, sparse_k, n_prompt, n_greedy,
         pos = n_prompt + i
         lg, am = e.step([tok], [pos])
         want = rm.forward(tok, pos)
-        assert np.array_equal(bits(lg[0]), bits(want)), f"greedy step {i}"
+        assert same(lg[0], want), f"greedy step {i}"
         ref_tok = P.port_argmax(want, want.size)
         assert int(am[0]) == ref_tok, f"greedy token {i}"
         tok = ref_tok
@@ -131,12 +158,16 @@ def _run(eng, torch, ref, synth, cfg, kind, paged, sparse_k, n_prompt, n_greedy,
     return n_sel_checked
 
 
-def test_llama8b_slice_int8_paged(eng, torch, ref, synth):
+@pytest.mark.parametrize("mode", [0, 1])
+def test_llama8b_slice_int8_paged(eng, torch, ref, synth, mode):
     """Two layers of the Llama-3-8B shape, INT8, paged KV: 1100 prompt tokens
-    (block-sparse past 1024) and 64 greedy steps, bit-exact against the
-    reference; the last layer's block selection checked in heap order."""
+    (block-sparse past 1024) and 64 greedy steps against the reference:
+    bit-exact on the reference-order path with the last layer's block
+    selection in heap order; on the split attention within the tolerance,
+    the same block set, equal tokens."""
     cfg = _slice(synth, synth.LLAMA3_8B)
-    n = _run(eng, torch, ref, synth, cfg, "int8", True, 64, 1100, 64, 50, 1024, sel_check=True)
+    n = _run(eng, torch, ref, synth, cfg, "int8", True, 64, 1100, 64, 50, 1024, sel_check=True,
+             mode=mode)
     assert n >= 9
 
 
