@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_kernel(ChainPa
   // -------------------------------------------------------------- consumers
   const int ct = tid - 32, wc = warp - 1, nc = kWarps * 32;
   const int rq = lane >> 3, sl = lane & 7;
-  bool ok = true;
+  bool ok = true, live = true;
   int t = 0;
   for (int p = 0; p < P.nph; p++) {
     const ChainPhase& ph = P.ph[p];
@@ -152,8 +152,10 @@ __global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_kernel(ChainPa
     } else {
       if (ct == 0) {
         bool got = false;
-        for (uint32_t it = 0; it < kWaitLimit && ok; it++)
-          if (ld_acquire(P.ctr + p - 1) >= G) {
+        const uint32_t lim = P.wait_iters > 0 ? (uint32_t)P.wait_iters : kWaitLimit;
+        const int need = G + (p == 1 ? P.wait_extra : 0);
+        for (uint32_t it = 0; it < lim && ok; it++)
+          if (ld_acquire(P.ctr + p - 1) >= need) {
             got = true;
             break;
           } else {
@@ -181,7 +183,16 @@ __global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_kernel(ChainPa
       uint64_t acc01 = 0, acc23 = 0;
       for (int c0 = 0; c0 < sp.nchunks; c0 += sp.m, t++) {
         const int s = t % S, mc = min(sp.m, sp.nchunks - c0);
-        if (ok) ok = mbar_wait(&full[s], (t / S) & 1, P.err);
+        // every slot is waited for, also after a failed wait: no bulk copy
+        // may still be landing in shared memory when the CTA exits.  A slot
+        // that never fills after a failure means the producer stopped: no
+        // later slot has a copy either.
+        bool landed = false;
+        if (live) landed = mbar_wait(&full[s], (t / S) & 1, ok ? P.err : nullptr);
+        if (!landed) {
+          if (!ok) live = false;
+          ok = false;
+        }
         if (ok && wc < gn) {
           for (int i = 0; i < mc; i++) {
             const uint8_t* base = stages + (size_t)s * stage_bytes + (size_t)(i * gn + wc) * 4 * KCE +
@@ -615,6 +626,28 @@ int chain_smem(const ChainParams& P, int kce, int* stages) {
   if (s < 2) return -1;
   *stages = s;
   return fixed + s * sb;
+}
+
+int chain_blocks_per_sm(int wkind, int kce, int kmax) {
+  ChainParams P{};
+  P.kmax = kmax;
+  int stages = 0;
+  const int smem = chain_smem(P, kce, &stages);
+  if (smem < 0) return 0;
+  int n = 0;
+  cudaError_t e = cudaErrorInvalidValue;
+  const int threads = 32 + 32 * kWarps;
+  if (wkind == EC_W_INT8)
+    e = kce == 512 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                         &n, gemv_chain_kernel<EC_W_INT8, 512>, threads, smem)
+                   : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                         &n, gemv_chain_kernel<EC_W_INT8, 32>, threads, smem);
+  else if (wkind == EC_W_FP8)
+    e = kce == 512 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                         &n, gemv_chain_kernel<EC_W_FP8, 512>, threads, smem)
+                   : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                         &n, gemv_chain_kernel<EC_W_FP8, 32>, threads, smem);
+  return e == cudaSuccess ? n : 0;
 }
 
 cudaError_t chain_launch(int wkind, ChainParams P, int grid, cudaStream_t s, bool pdl) {

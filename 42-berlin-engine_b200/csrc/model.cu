@@ -69,6 +69,7 @@ struct ec_ctx {
   int npacks = 1;            // batched-chain passes per step (max_batch / 8, rounded up)
   void* amax = nullptr;      // split-argmax partials and counters
   bool chain = false;        // one persistent GEMV kernel per layer
+  int chain_kce = 0;         // its packed chunk width
   bool tc = false;           // steps of >= tensor_min_batch sequences: tensor-core GEMMs
   int8_t* tc_digits = nullptr;
   double* tc_sx = nullptr;
@@ -382,6 +383,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     P.nph = 5;
     const char* nc = getenv("EC_NO_CHAIN");
     ctx->chain = ec::chain_kce(P) != 0 && !(nc && atoi(nc));
+    ctx->chain_kce = ctx->chain ? ec::chain_kce(P) : 0;
   }
   // co-resident plans measured slower (the block scheduler may place two CTAs
   // of one GEMV on an SM whose previous CTA has finished): opt-in only
@@ -429,6 +431,16 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     TRY(ec::packed_prepare());
     TRY(ec::chain_prepare());
     TRY(ec::attn_prepare(ctx->kv, ctx->lsh, sb));
+  }
+  if (ctx->chain) {
+    // the chain's grid-wide phase counters need every CTA resident at once
+    int kmax = D > F ? D : F;
+    if (H * hd > kmax) kmax = H * hd;
+    if (ec::chain_blocks_per_sm(c.weight_kind, ctx->chain_kce, kmax) < 1) {
+      ec_destroy(ctx);
+      return fail(EC_ERR_UNSUPPORTED, "the GEMV chain kernel cannot keep one CTA per SM resident "
+                                      "on this device");
+    }
   }
   if (c.attention_mode != EC_ATTN_REFERENCE && ctx->kv.paged) {
     if (!ec::fast_attention_supported(ctx->kv, c.sparse_blocks_k)) {
@@ -713,6 +725,8 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
             ((size_t)layer_slot * ctx->npacks + pack) * (ec::kMaxChainPhases + 1);
     P.err = ctx->err;
     P.eps = c.norm_eps;
+    P.wait_iters = c.wait_limit < 0 ? -c.wait_limit : c.wait_limit;
+    P.wait_extra = c.wait_limit < 0 ? 1 : 0;
     double by = 0;
     for (int i = 0; i < P.nph; i++)
       if (P.ph[i].pro != ec::PRO_NORM_ROWS) by += (double)P.ph[i].N * P.ph[i].K;
@@ -1023,6 +1037,8 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
         P.err = ctx->err;
         P.eps = c.norm_eps;
         P.mark = l == 1;
+        P.wait_iters = c.wait_limit < 0 ? -c.wait_limit : c.wait_limit;
+        P.wait_extra = c.wait_limit < 0 ? 1 : 0;
         const double by = gemv_bytes(ctx->wo[l], ec::PRO_NONE, ec::EPI_RESID) +
                           gemv_bytes(ctx->w13[l], ec::PRO_RMSNORM, ec::EPI_SWIGLU) +
                           gemv_bytes(ctx->w2[l], ec::PRO_NONE, ec::EPI_RESID) +

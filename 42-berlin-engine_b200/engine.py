@@ -46,7 +46,7 @@ class ModelConfig(C.Structure):
         (n, C.c_int) for n in (
             "weight_kind", "use_paged_kv", "sparse_k", "window", "sparse_blocks_k",
             "lsh_tables", "lsh_bits", "lsh_unit", "lsh_max_units", "lsh_radius",
-            "lsh_max_cand", "max_batch", "tensor_min_batch", "attention_mode")]
+            "lsh_max_cand", "max_batch", "tensor_min_batch", "attention_mode", "wait_limit")]
 
 
 class Transformer(C.Structure):

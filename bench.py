@@ -1,18 +1,24 @@
 """Decode throughput of the B200 hot path (BASELINE.json metric: decode tok/s).
 
-Workload (BASELINE config 3): Llama-3-8B-shaped random-init decoder, INT8
+Workload (BASELINE config 4): Llama-3-8B-shaped random-init decoder, INT8
 per-channel weights (power-of-two scales), paged INT8 KV cache (the
 reference's default mode), a 2048-token random prompt already in the cache,
-then greedy decode at batch 1 per GPU.  One step = one decode token of every
-sequence.  Multi-GPU: one process per GPU, independent sequences (weak
-scaling, no collective on the data path); value = tokens of all ranks /
-max-over-ranks time.
+then greedy decode.  One step = one decode token of every sequence.
+
+The JSON line's headline is batch 1 per GPU; `dp_b64` in the same line times
+64 sequences per GPU (config 4's batch split data-parallel: global batch
+64 x N) on the tensor-core path of the same engine.  `--attention` picks the
+paged attention: `split` (default; the reference's block set and softmax
+weights, additions regrouped over a cluster of CTAs) or `reference` (the
+reference's sequential order, bit-identical logits).  Multi-GPU: one process
+per GPU, independent sequences (weak scaling, no collective on the data
+path); value = tokens of all ranks / max-over-ranks time.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
 
 `--impl reference` times the reference engine's own CPU decode
 (oracle/_ref, transformer_forward over BF16 weights equal to the INT8
-weights) on the host cores, rank 0 only.
+weights) on the host cores at the same context, rank 0 only.
 """
 import argparse
 import ctypes as C
@@ -155,19 +161,22 @@ def cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads):
         return _cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads)
 
 
-def _cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads):
+def _cpu_baseline(cfg, model_src, context, steps, warmup, threads):
     os.environ["OMP_NUM_THREADS"] = str(threads)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle  # CPU baseline leg only
     if oracle.ref_available():
         m, kind = oracle.RefModel(model_src, use_paged_kv=True, sparse_k=64), "reference"
+        # positions 0..context-1 through the reference's own paged_kv_append
+        # and lsh_update (synthetic K/V: no CPU prompt)
+        m.fill_context(context, seed=7)
+        tok, pos = 1, context
     else:
         m, kind = oracle.PortModel(model_src), "port"
-    toks = _load("synth").prompt(cfg, n_prompt, seed=7)
-    for p in range(n_prompt):
-        lg = m.forward(int(toks[p]), p)
-    tok = int(np.argmax(lg))
-    pos = n_prompt
+        toks = _load("synth").prompt(cfg, 16, seed=7)
+        for p in range(16):
+            lg = m.forward(int(toks[p]), p)
+        tok, pos = int(np.argmax(lg)), 16
     for _ in range(warmup):
         lg = m.forward(tok, pos)
         tok, pos = int(np.argmax(lg)), pos + 1
@@ -179,13 +188,24 @@ def _cpu_baseline(cfg, model_src, n_prompt, steps, warmup, threads):
     return steps / dt, kind
 
 
+def host_cores():
+    """(threads used, physical cores) of this host."""
+    logical = os.cpu_count() or 1
+    try:
+        import psutil
+        physical = psutil.cpu_count(logical=False) or logical
+    except Exception:
+        physical = logical
+    return logical, physical
+
+
 def run_reference(args):
     ws, rank, local = dist_setup()
     if rank != 0:
         return
     S = _load("synth")
     cfg = S.LLAMA3_8B
-    threads = os.cpu_count() or 1
+    threads, physical = host_cores()
     try:
         import torch
         if not torch.cuda.is_available():
@@ -196,22 +216,34 @@ def run_reference(args):
     except Exception as exc:  # generate on the host instead
         print(f"[bench] device generation unavailable ({exc}); host generation", file=sys.stderr)
         src_model = S.make_model(cfg, seed=SEED)
-    n_prompt = 16
-    val, kind = cpu_baseline(cfg, src_model, n_prompt, args.steps, args.warmup, threads)
-    sample = (f"{args.steps} decode steps after a {n_prompt}-token prompt (context "
-              f"{n_prompt}..{n_prompt + args.steps + args.warmup} instead of 2k: the step is "
-              f"dominated by the 16 GB of BF16 weight reads either way)")
+    val, kind = cpu_baseline(cfg, src_model, args.prompt, args.steps, args.warmup, threads)
+    sample = (f"{args.steps} decode steps at context {args.prompt}.."
+              f"{args.prompt + args.warmup + args.steps} (positions 0..{args.prompt - 1} of every "
+              f"layer's paged cache filled with synthetic K/V through the reference's own "
+              f"paged_kv_append and lsh_update, no CPU prompt)")
     line = {"metric": METRIC, "value": round(val, 4), "unit": "tok/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000.0 / val, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "llama3-8b-shape decode b=1", "global_batch": 1,
-                       "weights": "bf16 (= int8 * pow2 scale)", "kv": "paged int8"},
+            "config": config_block(args, ws, big=False, B=1),
             "cpu_baseline": {"value": round(val, 4), "unit": "tok/s", "cores": threads,
-                             "kind": kind, "sample": sample},
+                             "physical_cores": physical, "kind": kind, "sample": sample},
             "e2e": {"value": round(val, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    line["config"]["weights"] = "bf16 (= int8 * pow2 scale)"
     emit(line)
+
+
+def config_block(args, ws, big, B, tmb=0):
+    """The `config` object both arms print for the same workload."""
+    return {"workload": f"{'70b' if big else 'llama3-8b'}-shape decode b={B} per GPU",
+            "global_batch": ws * B, "context": args.prompt,
+            "weights": "fp8 e4m3 per-tensor pow2 scale" if big else "int8 per-row pow2 scale",
+            "kv": f"linear bf16, LSH top-{args.sparse_k}" if big else "paged int8",
+            "attention": "reference order" if big else args.attention,
+            "parallelism": f"dp{ws} (replicas)",
+            "gemm": "tcgen05 int8 (digit planes)" if (not big and tmb) else "cuda-core gemv chain",
+            "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"}
 
 
 class _HostWeights:
@@ -224,6 +256,47 @@ class _HostWeights:
         return self._bf
 
 
+def timed_steps(e, torch, stream, tok, pos, B, steps, warmup, local):
+    """W untimed steps, then K steps bracketed by CUDA events on the engine's
+    stream (inputs resident on the device, greedy tokens fed back on the
+    device); returns ms per step, max over ranks."""
+    dp = _load("dp")
+    for _ in range(warmup):
+        e.step_device(tok.data_ptr(), pos.data_ptr(), B, True)
+    e.sync()
+    dp.barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    torch.cuda.nvtx.range_push("timed")  # lets a profiler select these launches
+    for _ in range(steps):
+        e.step_device(tok.data_ptr(), pos.data_ptr(), B, True)
+    torch.cuda.nvtx.range_pop()
+    ev1.record(stream)
+    e.sync()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / steps
+    ms = dp.max_over_ranks(ms, f"cuda:{local}")
+    dp.barrier()
+    return ms
+
+
+def e2e_steps(e, cur_tok, cur_pos, steps, local):
+    """The same step through the C ABI with host buffers: tokens and positions
+    copied in, logits and greedy tokens copied out, every step."""
+    dp = _load("dp")
+    for _ in range(2):
+        lg, am = e.step(cur_tok, cur_pos)
+        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        lg, am = e.step(cur_tok, cur_pos)
+        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
+    ms = (time.perf_counter() - t0) * 1000.0 / steps
+    return dp.max_over_ranks(ms, f"cuda:{local}"), cur_tok, cur_pos
+
+
 def run_cuda(args):
     import torch
     ws, rank, local = dist_setup()
@@ -234,6 +307,8 @@ def run_cuda(args):
     S = _load("synth")
     B = args.batch
     big = args.model == "70b"
+    dpb = 0 if (big or args.dp_batch <= B) else args.dp_batch  # the b=64-per-GPU record
+    tmb = 0
     if big:
         # BASELINE config 5 on one GPU: FP8 E4M3 per-tensor weights (~70 GB),
         # linear BF16 KV with the reference's LSH-routed top-K attention
@@ -243,8 +318,9 @@ def run_cuda(args):
         src = S.DeviceModel(cfg, seed=SEED, device=local, kind="fp8")
     else:
         cfg = S.LLAMA3_8B
-        tmb = args.tensor_min_batch if B >= args.tensor_min_batch > 0 else 0
-        e = eng.Engine(cfg, device=local, max_batch=B, tensor_min_batch=tmb,
+        nb = max(B, dpb)
+        tmb = args.tensor_min_batch if nb >= args.tensor_min_batch > 0 else 0
+        e = eng.Engine(cfg, device=local, max_batch=nb, tensor_min_batch=tmb,
                        attention_mode=ATTN_MODES[args.attention])
         src = S.DeviceModel(cfg, seed=SEED, device=local)
 
@@ -262,51 +338,22 @@ def run_cuda(args):
     src.generate(sink)
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
-    # prompt: 2048 random tokens through the decode path (KV cache filled)
-    # B independent sequences, each its own random prompt, decoded together
-    prompts = [S.prompt(cfg, args.prompt, seed=7 + rank * 1000 + b) for b in range(B)]
+    # prompt: random tokens through the decode path (KV cache filled), every
+    # sequence its own prompt, all sequences of the engine decoded together
+    nseq = max(B, dpb)
+    prompts = [S.prompt(cfg, args.prompt, seed=7 + rank * 1000 + b) for b in range(nseq)]
     for p in range(args.prompt):
-        _, am = e.step([int(pr[p]) for pr in prompts], [p] * B, want_logits=False)
-    tok = torch.tensor([int(a) for a in am], dtype=torch.int32, device=f"cuda:{local}")
-    pos = torch.tensor([args.prompt] * B, dtype=torch.int32, device=f"cuda:{local}")
+        _, am = e.step([int(pr[p]) for pr in prompts], [p] * nseq, want_logits=False)
+    dev = f"cuda:{local}"
+    tok_all = torch.tensor([int(a) for a in am], dtype=torch.int32, device=dev)
+    pos_all = torch.tensor([args.prompt] * nseq, dtype=torch.int32, device=dev)
     stream = torch.cuda.ExternalStream(e.stream())
-
-    def steps(n):
-        for _ in range(n):
-            e.step_device(tok.data_ptr(), pos.data_ptr(), B, True)
-
-    steps(args.warmup)
-    e.sync()
-    dp.barrier()
+    tok, pos = tok_all[:B].clone(), pos_all[:B].clone()
     with Clocks(local) as clk:
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        torch.cuda.nvtx.range_push("timed")  # lets a profiler select these launches
-        steps(args.steps)
-        torch.cuda.nvtx.range_pop()
-        ev1.record(stream)
-        e.sync()
-        torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1) / args.steps
-    ms = dp.max_over_ranks(ms, f"cuda:{local}")
-    dp.barrier()
+        ms = timed_steps(e, torch, stream, tok, pos, B, args.steps, args.warmup, local)
     value = dp.job_throughput(B, ws, ms)
-
-    # end to end through the C ABI with host buffers (token/pos in, logits out)
-    cur_tok, cur_pos = [int(v) for v in tok.cpu()], [int(v) for v in pos.cpu()]
-    host_logits = np.empty((B, cfg.vocab_size), np.float32)
-    for _ in range(2):
-        lg, am = e.step(cur_tok, cur_pos)
-        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        lg, am = e.step(cur_tok, cur_pos)
-        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
-    e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
-    e2e_ms = dp.max_over_ranks(e2e_ms, f"cuda:{local}")
-    del host_logits
+    e2e_ms, cur_tok, cur_pos = e2e_steps(e, [int(v) for v in tok.cpu()],
+                                         [int(v) for v in pos.cpu()], args.steps, local)
 
     # live per-kernel timing (profiling mode: events around each launch)
     e.profile(True)
@@ -315,6 +362,33 @@ def run_cuda(args):
         cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
     prof = e.profile_read()
     e.profile(False)
+    launches_b = e.launches_per_step(B)
+
+    dp_rec = None
+    if dpb:
+        # BASELINE config 4's batch split data-parallel: dpb sequences per GPU
+        # (global batch dpb x N) on the tensor-core path, the same engine and
+        # context; the first B sequences were advanced by the steps above, so
+        # every sequence restarts from its own position
+        tok_d, pos_d = tok_all.clone(), pos_all.clone()
+        pos_d[:B] = torch.tensor(cur_pos, dtype=torch.int32, device=dev)
+        tok_d[:B] = torch.tensor(cur_tok, dtype=torch.int32, device=dev)
+        dsteps = max(3, min(args.steps, 20))
+        with Clocks(local) as clk_d:
+            ms_d = timed_steps(e, torch, stream, tok_d, pos_d, dpb, dsteps, args.warmup, local)
+        e2e_d, _, _ = e2e_steps(e, [int(v) for v in tok_d.cpu()], [int(v) for v in pos_d.cpu()],
+                                dsteps, local)
+        dp_rec = {
+            "metric": METRIC_B.format(dpb), "value": round(dp.job_throughput(dpb, ws, ms_d), 3),
+            "unit": "tok/s", "n_gpus": ws, "steps": dsteps, "warmup": args.warmup,
+            "ms_per_step": round(ms_d, 4), "higher_is_better": True, "scaling": "weak",
+            "config": config_block(args, ws, big, dpb, tmb),
+            "e2e": {"value": round(ws * dpb * 1000.0 / e2e_d, 3), "unit": "tok/s",
+                    "h2d_bytes_per_step": 8 * dpb,
+                    "d2h_bytes_per_step": 4 * dpb * (cfg.vocab_size + 1)},
+            "gpu_launches": e.launches_per_step(dpb) * dsteps,
+            "clocks": clk_d.summary()}
+
     # roofline of the dominant kernel: its algorithmic bytes per launch over its
     # event-timed average launch duration
     tot_ms = sum(v["ms"] for v in prof.values())
@@ -355,19 +429,10 @@ def run_cuda(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp8" if big else "int8",
             "data": "synthetic",
-            "config": {"workload": f"{'70b' if big else 'llama3-8b'}-shape decode b={B} per GPU",
-                       "global_batch": ws * B, "context": args.prompt,
-                       "weights": "fp8 e4m3 per-tensor pow2 scale" if big
-                       else "int8 per-row pow2 scale",
-                       "kv": f"linear bf16, LSH top-{args.sparse_k}" if big else "paged int8",
-                       "attention": "reference order" if big else args.attention,
-                       "parallelism": f"dp{ws} (replicas)",
-                       "gemm": "tcgen05 int8 (digit planes)" if (not big and tmb)
-                       else "cuda-core gemv chain",
-                       "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"},
+            "config": config_block(args, ws, big, B, tmb if (tmb and B >= tmb) else 0),
             "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B * (cfg.vocab_size + 1)},
-            "gpu_launches": e.launches_per_step(B) * args.steps,
+            "gpu_launches": launches_b * args.steps,
             "roofline": {"bound": "hbm", "kernel": dom,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
@@ -381,24 +446,29 @@ def run_cuda(args):
             "kernel_share": {k: round(v["ms"] / tot_ms, 4) for k, v in prof.items() if tot_ms},
             "clocks": clk.summary(),
         }
+        if dp_rec:
+            line["dp_b%d" % dpb] = dp_rec
+        threads, physical = host_cores()
         if big:
-            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": os.cpu_count() or 1,
+            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": threads,
                                     "kind": "reference",
                                     "sample": "unavailable: the reference's BF16 copy of the "
                                               "70B shape (~140 GB) exceeds host memory"}
         elif not args.no_cpu_baseline and ws == 1:  # rank 0, one GPU only
             del src
             torch.cuda.empty_cache()
-            threads = os.cpu_count() or 1
             try:
                 src2 = S.DeviceModel(cfg, seed=SEED, device=local)
                 hw = _HostWeights(cfg, src2.bf16_weights())
                 del src2
                 torch.cuda.empty_cache()
-                cps, kind = cpu_baseline(cfg, hw, 16, max(2, min(args.steps, 8)), 1, threads)
+                cps, kind = cpu_baseline(cfg, hw, args.prompt, 6, 1, threads)
                 line["cpu_baseline"] = {
-                    "value": round(cps, 4), "unit": "tok/s", "cores": threads, "kind": kind,
-                    "sample": "8B-shape decode steps after a 16-token prompt (weights-bound)"}
+                    "value": round(cps, 4), "unit": "tok/s", "cores": threads,
+                    "physical_cores": physical, "kind": kind,
+                    "sample": f"6 decode steps of the 8B shape at context {args.prompt} (K/V of "
+                              f"positions 0..{args.prompt - 1} synthetic through the "
+                              f"reference's paged_kv_append)"}
             except Exception as exc:
                 line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": threads,
                                         "kind": "reference", "sample": f"failed: {exc}"}
@@ -429,7 +499,10 @@ def main():
     ap.add_argument("--sparse-k", type=int, default=511, help="70b: LSH top-K (engine max 511)")
     ap.add_argument("--tensor-min-batch", type=int, default=16,
                     help="batches this large run their GEMMs on the tensor cores (0: never)")
-    ap.add_argument("--attention", default="reference", choices=sorted(ATTN_MODES),
+    ap.add_argument("--dp-batch", type=int, default=64,
+                    help="also time this many sequences per GPU (config 4's batch split "
+                         "data-parallel; 0: skip)")
+    ap.add_argument("--attention", default="split", choices=sorted(ATTN_MODES),
                     help="paged attention: reference order (bit-exact) or split (within "
                          "tolerance, same block set)")
     args = ap.parse_args()

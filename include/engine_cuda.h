@@ -94,6 +94,11 @@ typedef struct ec_model_config
 							**   tokens split over a cluster of CTAs with
 							**   the reference's softmax weights (only the
 							**   additions are reordered) */
+	int		wait_limit;		/* bounded device waits between the GEMV chain's
+							** phases: 0 = the default (about a second);
+							** n > 0: n polls; n < 0: -n polls for a count
+							** that is never reached (tests the timeout
+							** path: the step returns EC_ERR_TIMEOUT) */
 }	ec_model_config;
 
 # define EC_ATTN_REFERENCE 0

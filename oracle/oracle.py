@@ -150,6 +150,7 @@ def ref():
         vp = C.c_void_p
         _sig(lib, "refd_create", vp, C.POINTER(RefdConfig), vp, vp, vp, C.POINTER(vp))
         _sig(lib, "refd_forward", C.POINTER(C.c_float), vp, C.c_int, C.c_int)
+        _sig(lib, "refd_fill_context", C.c_int, vp, C.c_int, C.c_uint)
         _sig(lib, "refd_state", C.POINTER(C.c_float), vp, C.c_int)
         _sig(lib, "refd_lsh_index", C.POINTER(LshIndex), vp)
         _sig(lib, "refd_paged_block", C.c_int, vp, C.c_int, C.c_int, i8p, i8p, f32p, f32p,
@@ -289,6 +290,12 @@ class RefModel:
         out = (C.c_ulonglong * 2)()
         self.lib.refd_lsh_counters(self.h, out)
         return int(out[0]), int(out[1])
+
+    def fill_context(self, n, seed=1):
+        """Positions 0..n-1 of the paged cache from synthetic K/V through the
+        reference's paged_kv_append and lsh_update (no projections)."""
+        if self.lib.refd_fill_context(self.h, int(n), int(seed)) != 0:
+            raise RuntimeError("refd_fill_context failed")
 
     def lsh_index(self):
         return self.lib.refd_lsh_index(self.h).contents

@@ -189,6 +189,54 @@ float	*refd_forward(void *h, int token, int pos)
 	return (transformer_forward(&((t_refd *)h)->t, token, pos));
 }
 
+/*
+** Fill positions 0..n-1 of every layer's paged KV cache with seeded
+** synthetic keys and values through the reference's own paged_kv_append
+** (paged.c:195) and layer 0's lsh_update (ops_lsh.c:296), the two calls
+** transformer_forward makes per token (inference.c:169-192), without the
+** projections.  Used by the timed CPU baseline to decode at a long context
+** without paying for a CPU prompt.  Values: uniform in [-2, 2) from a 32-bit
+** LCG (roughly the spread of the projections of the synthetic models).
+*/
+int	refd_fill_context(void *h, int n, unsigned seed)
+{
+	t_transformer	*t = &((t_refd *)h)->t;
+	int				kvd;
+	float			*k;
+	float			*v;
+	int				pos;
+	int				i;
+	int				d;
+
+	if (!t->use_paged_kv || n > t->config.seq_len)
+		return (-1);
+	kvd = t->config.n_kv_heads * t->config.head_dim;
+	k = malloc(kvd * sizeof(float));
+	v = malloc(kvd * sizeof(float));
+	if (!k || !v)
+		return (free(k), free(v), -1);
+	for (pos = 0; pos < n; pos++)
+	{
+		for (i = 0; i < t->config.n_layers; i++)
+		{
+			for (d = 0; d < kvd; d++)
+			{
+				seed = seed * 1664525u + 1013904223u;
+				k[d] = ((float)(seed >> 8) / 16777216.0f) * 4.0f - 2.0f;
+				seed = seed * 1664525u + 1013904223u;
+				v[d] = ((float)(seed >> 8) / 16777216.0f) * 4.0f - 2.0f;
+			}
+			paged_kv_append(&t->paged_kv[i], k, v, pos);
+			if (i == 0 && t->lsh_ctx && t->lsh_index)
+				lsh_update((t_lsh_index *)t->lsh_index, (t_lsh_ctx *)t->lsh_ctx,
+					k, t->config.head_dim, pos);
+		}
+	}
+	free(k);
+	free(v);
+	return (0);
+}
+
 /* copies of intermediate state for layer-level parity checks */
 const float	*refd_state(void *h, int which)
 {

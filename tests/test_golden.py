@@ -127,3 +127,26 @@ def test_tiny_decode_trace(oracle, tiny_model, mode):
         if pos >= 63:
             assert P.port_argmax(lg, lg.size) == toks[pos + 1]
     assert np.array_equal(np.array(pm.counters()), G[f"tiny_{mode}_counters"])
+
+
+def test_reference_context_fill(ref, synth):
+    """The CPU baseline's context fill: positions 0..n-1 of the reference's
+    paged cache through its own paged_kv_append / lsh_update, then decode
+    steps at position n (finite logits, the block-sparse path active past
+    1024 tokens)."""
+    cfg = synth.ModelConfig(dim=256, hidden_dim=512, n_layers=2, n_heads=4, n_kv_heads=2,
+                            vocab_size=512, seq_len=2048, head_dim=64, rope_theta=1e4)
+    model = synth.make_model(cfg, seed=2)
+    m = ref.RefModel(model, use_paged_kv=True, sparse_k=64)
+    m.fill_context(1100, seed=3)
+    for p in range(1100, 1103):
+        lg = m.forward(5, p)
+        assert np.all(np.isfinite(lg))
+    kb = np.zeros(cfg.n_kv_heads * 16 * cfg.head_dim, np.int8)
+    vb = np.zeros_like(kb)
+    ks = np.zeros(cfg.n_kv_heads * 16, np.float32)
+    vs = np.zeros_like(ks)
+    cen = np.zeros(cfg.head_dim, np.float32)
+    assert ref.ref().refd_paged_block(m.h, 1, 68, kb, vb, ks, vs, cen) == 15
+    assert ref.ref().refd_paged_block(m.h, 1, 67, kb, vb, ks, vs, cen) == 16
+    assert np.abs(cen).max() > 0
