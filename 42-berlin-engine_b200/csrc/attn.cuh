@@ -103,6 +103,10 @@ cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const
                                  int layer, int B, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
                              cudaStream_t s, bool pdl);
+// Batched paged steps whose attention runs as attention_group_kernel (one CTA
+// per KV head and sequence, the reference's order): faster than the split
+// attention from 4 sequences on, so split mode keeps it there.
+bool use_group_attention(const KvLayout& kv, const StepBuffers& sb, int B);
 
 // Per-op entry points on one layer (a KvLayout with n_layers = 1):
 // append one token, select blocks (sb.q_rotated), attention with max_tok.

@@ -757,7 +757,7 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
     }
     if ((e = run(P, L, pk, nb))) return e;
   }
-  const bool split = ctx->fast && prefill_seq < 0;
+  const bool split = ctx->fast && prefill_seq < 0 && !ec::use_group_attention(kv, sb, B);
   for (int l = 0; l < L; l++) {
     if (split) {
       if ((e = enqueue_attention(ctx, kv, ctx->lsh, sb, l, B, true))) return e;
@@ -916,7 +916,9 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
       return e;
   }
   for (int l = 0; l < L; l++) {
-    if ((e = enqueue_attention(ctx, ctx->kv, ctx->lsh, sb, l, B, ctx->fast != 0))) return e;
+    if ((e = enqueue_attention(ctx, ctx->kv, ctx->lsh, sb, l, B,
+                               ctx->fast && !ec::use_group_attention(ctx->kv, sb, B))))
+      return e;
     const bool last = l + 1 == L;
     for (int b0 = 0; b0 < B; b0 += ec::kTcMaxRows) {
       const int nb = B - b0 < ec::kTcMaxRows ? B - b0 : ec::kTcMaxRows;

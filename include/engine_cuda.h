@@ -88,12 +88,15 @@ typedef struct ec_model_config
 							** EC_ATTN_REFERENCE (default): the reference's
 							**   heap order and sequential online softmax,
 							**   bit-identical;
-							** EC_ATTN_SPLIT: the same top-K block set
-							**   (chosen by ranks, no heap replay), visited
-							**   in ascending block order, each KV head's
-							**   tokens split over a cluster of CTAs with
-							**   the reference's softmax weights (only the
-							**   additions are reordered) */
+							** EC_ATTN_SPLIT: steps of 1-3 sequences run
+							**   the reference's selection (block heap
+							**   replayed exactly) in one kernel and split
+							**   each KV head's visiting order over a
+							**   cluster of CTAs with the reference's
+							**   softmax weights (only the additions are
+							**   regrouped: within the tests' tolerance);
+							**   larger batches keep the grouped
+							**   reference-order attention */
 	int		wait_limit;		/* bounded device waits between the GEMV chain's
 							** phases: 0 = the default (about a second);
 							** n > 0: n polls; n < 0: -n polls for a count

@@ -89,7 +89,8 @@ def test_split_decode_b1(eng, torch, oracle, synth, heads, kvh, hd):
 
 @pytest.mark.parametrize("B", [3, 9])
 def test_split_decode_batched(eng, torch, oracle, synth, B):
-    """B sequences per step (B = 3: 16 splits per KV head; B = 9: 4 splits,
+    """B sequences per step (B = 3: the split attention, 8 CTAs per KV head;
+    B = 9: split mode keeps the grouped reference-order attention; both on
     the exact batched chain): every sequence within tolerance of its own
     restatement model past the block-sparse threshold."""
     cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=2,
