@@ -1,5 +1,7 @@
 // misc.cu -- embedding lookup, argmax, and the stand-alone per-op kernels
 // (RMSNorm, RoPE, SwiGLU, INT8 quantisation) behind the ec_op_* entry points.
+#include <cuda_fp8.h>
+
 #include "ec_internal.cuh"
 #include "misc.cuh"
 
@@ -110,11 +112,15 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   }
 }
 
-// op_rmsnorm (ops_norm.c:105-124) of one vector; one CTA.
+// op_rmsnorm (ops_norm.c:105-124) of one vector per CTA (row blockIdx.x,
+// `stride` floats apart).
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float* out, const float* x,
-                                                      const uint16_t* w, int n, float eps) {
+                                                      const uint16_t* w, int n, float eps,
+                                                      long stride) {
   __shared__ float red[9];
   const int tid = threadIdx.x;
+  x += blockIdx.x * stride;
+  out += blockIdx.x * stride;
   if (tid < 8) {
     float acc = 0.0f;
     for (int j = tid; j < (n & ~7); j += 8) acc = __fmaf_rn(x[j], x[j], acc);
@@ -342,7 +348,135 @@ cudaError_t launch_argmax(const float* logits, int n, int B, int* out, int* toke
 
 cudaError_t launch_rmsnorm(float* out, const float* x, const uint16_t* w, int n, float eps,
                            cudaStream_t s) {
-  rmsnorm_kernel<<<1, 256, 0, s>>>(out, x, w, n, eps);
+  rmsnorm_kernel<<<1, 256, 0, s>>>(out, x, w, n, eps, 0L);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_rows(float* out, const float* x, const uint16_t* w, int n, float eps,
+                                int rows, long stride, cudaStream_t s) {
+  rmsnorm_kernel<<<rows, 256, 0, s>>>(out, x, w, n, eps, stride);
+  return cudaGetLastError();
+}
+
+// The final hidden adapter (inference.c:583-638): out[r] = simd_dot_bf16_f32
+// (A[r], x) in its 8-lane order (lane l takes columns l, l + 8, ...; then
+// ((l0+l4)+(l1+l5))+((l2+l6)+(l3+l7))), and xa[r] = x[r] + 16 * out[r]
+// (ADAPTER_SCALE, config.h:54; a power of two, so the product is exact).
+// 8 threads per row, 32 rows per CTA, grid (rows / 32, sequences).
+__global__ void __launch_bounds__(256) adapter_kernel(const uint16_t* __restrict__ A,
+                                                      const float* __restrict__ x,
+                                                      float* __restrict__ xa, int D) {
+  const int b = blockIdx.y, l = threadIdx.x & 7;
+  const int r = blockIdx.x * 32 + (threadIdx.x >> 3);
+  const float* xb = x + (long)b * D;
+  const uint16_t* a = A + (long)min(r, D - 1) * D;
+  float acc = 0.0f;
+  for (int j = l; j < (D & ~7); j += 8) acc = __fmaf_rn(bf16_to_f32(a[j]), xb[j], acc);
+  const float h4 = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+  const float t2 = __fadd_rn(h4, __shfl_xor_sync(0xffffffffu, h4, 1));
+  float sum = __fadd_rn(t2, __shfl_xor_sync(0xffffffffu, t2, 2));
+  if (l == 0 && r < D) {
+    for (int j = D & ~7; j < D; j++) sum = __fmaf_rn(bf16_to_f32(a[j]), xb[j], sum);
+    xa[(long)b * D + r] = __fadd_rn(xb[r], __fmul_rn(16.0f, sum));
+  }
+}
+
+cudaError_t launch_adapter(const uint16_t* A, const float* x, float* xa, int D, int B,
+                           cudaStream_t s) {
+  adapter_kernel<<<dim3((D + 31) / 32, B), 256, 0, s>>>(A, x, xa, D);
+  return cudaGetLastError();
+}
+
+// logits[b][i] += bias[i] (inference.c:645-651)
+__global__ void logit_bias_kernel(float* logits, const float* __restrict__ bias, int V) {
+  float* row = logits + (long)blockIdx.y * V;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x)
+    row[i] = __fadd_rn(row[i], bias[i]);
+}
+
+cudaError_t launch_logit_bias(float* logits, const float* bias, int V, int B, cudaStream_t s) {
+  logit_bias_kernel<<<dim3(64, B), 256, 0, s>>>(logits, bias, V);
+  return cudaGetLastError();
+}
+
+// Quantise-at-load (the reference ships BF16 weights only,
+// loader_parse.c:35-49): INT8 per output row, scale = max|w| / 127 (1 / 127
+// for an all-zero row), q = clamp(rint(w / scale), -127, 127) with IEEE
+// division and round-half-even.  One CTA per row.
+__global__ void __launch_bounds__(256) quant_rows_int8_kernel(const uint16_t* __restrict__ w,
+                                                              int8_t* __restrict__ q,
+                                                              float* __restrict__ scale, int cols) {
+  __shared__ float s_red[8];
+  const long r = blockIdx.x;
+  const uint16_t* row = w + r * cols;
+  float m = 0.0f;
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) m = fmaxf(m, fabsf(bf16_to_f32(row[j])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float amax = 0.0f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); i++) amax = fmaxf(amax, s_red[i]);
+  const float sc = __fdiv_rn(amax > 0.0f ? amax : 1.0f, 127.0f);
+  for (int j = threadIdx.x; j < cols; j += blockDim.x) {
+    float v = rintf(__fdiv_rn(bf16_to_f32(row[j]), sc));
+    v = fminf(fmaxf(v, -127.0f), 127.0f);
+    q[r * cols + j] = (int8_t)(int)v;
+  }
+  if (threadIdx.x == 0) scale[r] = sc;
+}
+
+cudaError_t launch_quant_rows_int8(const uint16_t* w, int8_t* q, float* scale, int rows, int cols,
+                                   cudaStream_t s) {
+  quant_rows_int8_kernel<<<rows, 256, 0, s>>>(w, q, scale, cols);
+  return cudaGetLastError();
+}
+
+// max |w| over a BF16 tensor into *out (float bits; out zeroed by the caller)
+__global__ void absmax_bf16_kernel(const uint16_t* __restrict__ w, long n, unsigned* out) {
+  float m = 0.0f;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(bf16_to_f32(w[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+cudaError_t launch_absmax_bf16(const uint16_t* w, long n, unsigned* out, cudaStream_t s) {
+  absmax_bf16_kernel<<<296, 256, 0, s>>>(w, n, out);
+  return cudaGetLastError();
+}
+
+// FP8 E4M3 per tensor: code = nearest E4M3 value of w / scale (ties to even,
+// saturating at 448; negative zero stored as +0)
+__global__ void quant_fp8_kernel(const uint16_t* __restrict__ w, uint8_t* __restrict__ q, long n,
+                                 float scale) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float x = __fdiv_rn(bf16_to_f32(w[i]), scale);
+    uint8_t c = (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+    q[i] = c == 0x80 ? 0 : c;
+  }
+}
+
+cudaError_t launch_quant_fp8(const uint16_t* w, uint8_t* q, long n, float scale, cudaStream_t s) {
+  quant_fp8_kernel<<<592, 256, 0, s>>>(w, q, n, scale);
+  return cudaGetLastError();
+}
+
+// out[0] |= 1 when any of n elements of `bits`-bit width is not +0 / -0.
+__global__ void nonzero_kernel(const void* p, long n, int bits, int* out) {
+  int any = 0;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    if (bits == 16)
+      any |= (static_cast<const uint16_t*>(p)[i] & 0x7FFFu) != 0;
+    else
+      any |= (static_cast<const uint32_t*>(p)[i] & 0x7FFFFFFFu) != 0;
+  }
+  if (__syncthreads_or(any) && threadIdx.x == 0) atomicOr(out, 1);
+}
+
+cudaError_t launch_nonzero(const void* p, long n, int bits, int* out, cudaStream_t s) {
+  nonzero_kernel<<<148, 256, 0, s>>>(p, n, bits, out);
   return cudaGetLastError();
 }
 

@@ -15,6 +15,19 @@ cudaError_t launch_argmax(const float* logits, int n, int B, int* out, int* toke
                           cudaStream_t s, bool pdl);
 cudaError_t launch_rmsnorm(float* out, const float* x, const uint16_t* w, int n, float eps,
                            cudaStream_t s);
+cudaError_t launch_rmsnorm_rows(float* out, const float* x, const uint16_t* w, int n, float eps,
+                                int rows, long stride, cudaStream_t s);
+// final hidden adapter: xa = x + 16 * (A . x) per row (B rows of D)
+cudaError_t launch_adapter(const uint16_t* A, const float* x, float* xa, int D, int B,
+                           cudaStream_t s);
+cudaError_t launch_logit_bias(float* logits, const float* bias, int V, int B, cudaStream_t s);
+// *out |= 1 when any element (16- or 32-bit) is not a signed zero
+cudaError_t launch_nonzero(const void* p, long n, int bits, int* out, cudaStream_t s);
+// quantise-at-load of BF16 weights: INT8 per row / FP8 E4M3 per tensor
+cudaError_t launch_quant_rows_int8(const uint16_t* w, int8_t* q, float* scale, int rows, int cols,
+                                   cudaStream_t s);
+cudaError_t launch_absmax_bf16(const uint16_t* w, long n, unsigned* out, cudaStream_t s);
+cudaError_t launch_quant_fp8(const uint16_t* w, uint8_t* q, long n, float scale, cudaStream_t s);
 cudaError_t launch_rope(float* data, int n_heads, int hd, int pos, const float* c, const float* sn,
                         int max_seq, cudaStream_t s);
 cudaError_t launch_silu(float* out, const float* g, const float* u, int n, cudaStream_t s);

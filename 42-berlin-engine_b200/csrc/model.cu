@@ -51,6 +51,12 @@ struct ec_ctx {
   std::vector<uint16_t*> attn_norm, ffn_norm;
   uint16_t* emb = nullptr;
   uint16_t* final_norm = nullptr;
+  // optional (inference.c:583-651): final hidden adapter [D][D] BF16 and
+  // logit bias [V]; applied only when registered and not all zero
+  uint16_t* adapter = nullptr;
+  float* logit_bias = nullptr;
+  bool adapter_on = false, bias_on = false;
+  float* xa = nullptr;  // [max_batch][D] adapted final hidden state
   std::vector<unsigned> have;  // bit per tensor per layer
   unsigned have_global = 0;
   // state
@@ -519,12 +525,39 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
         e = put_rows(ctx->lm, data, c.vocab_size, 0, 1);
         if (e == cudaSuccess) e = put_scales(ctx->lm.scale, c.vocab_size, 1);
         break;
+      case EC_FINAL_ADAPTER:
+      case EC_LOGIT_BIAS: {
+        // optional tensors: kept only when not all zero (the reference's
+        // zero-initialised adapter and bias change nothing)
+        const bool ad = which == EC_FINAL_ADAPTER;
+        const size_t n = ad ? (size_t)D * D : (size_t)c.vocab_size;
+        void** dst = ad ? reinterpret_cast<void**>(&ctx->adapter)
+                        : reinterpret_cast<void**>(&ctx->logit_bias);
+        if (!*dst) {
+          e = ad ? dalloc(ctx, &ctx->adapter, n) : dalloc(ctx, &ctx->logit_bias, n);
+          if (e == cudaSuccess && ad && !ctx->xa) e = dalloc(ctx, &ctx->xa, (size_t)c.max_batch * D);
+        }
+        if (e == cudaSuccess) e = cudaMemcpy(*dst, data, n * (ad ? 2 : 4), kind);
+        int* flag = nullptr;
+        if (e == cudaSuccess) e = dalloc(ctx, &flag, 1);
+        if (e == cudaSuccess) e = cudaMemset(flag, 0, 4);
+        if (e == cudaSuccess) e = ec::launch_nonzero(*dst, (long)n, ad ? 16 : 32, flag, nullptr);
+        int any = 0;
+        if (e == cudaSuccess) e = cudaMemcpy(&any, flag, 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) (ad ? ctx->adapter_on : ctx->bias_on) = any != 0;
+        // the captured step changes shape: capture again on the next step
+        if (ctx->gexec) {
+          cudaGraphExecDestroy(ctx->gexec);
+          ctx->gexec = nullptr;
+        }
+        break;
+      }
       default:
         return fail(EC_ERR_ARG, "unknown global tensor id");
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
-    ctx->have_global |= 1u << (which - EC_EMBEDDING);
+    if (which <= EC_LM_HEAD) ctx->have_global |= 1u << (which - EC_EMBEDDING);
     return EC_OK;
   }
   if (layer >= c.n_layers) return fail(EC_ERR_ARG, "layer out of range");
@@ -567,6 +600,81 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
   if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
   ctx->have[layer] |= 1u << which;
   return EC_OK;
+}
+
+extern "C" int ec_set_weight_bf16(ec_ctx* ctx, int layer, int which, const uint16_t* data,
+                                  int on_device) {
+  if (!ctx || !data) return fail(EC_ERR_ARG, "null argument");
+  const ec_model_config& c = ctx->c;
+  const int D = c.dim, F = c.hidden_dim, QD = c.n_heads * c.head_dim, KVD = c.n_kv_heads * c.head_dim;
+  int rows = 0, cols = 0;
+  if (layer < 0 && which == EC_LM_HEAD) {
+    rows = c.vocab_size;
+    cols = D;
+  } else if (layer >= 0) {
+    switch (which) {
+      case EC_WQ: rows = QD; cols = D; break;
+      case EC_WK: case EC_WV: rows = KVD; cols = D; break;
+      case EC_WO: rows = D; cols = QD; break;
+      case EC_W1: case EC_W3: rows = F; cols = D; break;
+      case EC_W2: rows = D; cols = F; break;
+      default: break;
+    }
+  }
+  if (!rows) return ec_set_weight(ctx, layer, which, data, nullptr, on_device);
+  cudaSetDevice(ctx->device);
+  if (on_device) EC_CUDA_TRY(cudaDeviceSynchronize());
+  const size_t n = (size_t)rows * cols;
+  uint16_t* bf = nullptr;
+  uint8_t* q = nullptr;
+  float* sc = nullptr;
+  unsigned* amax = nullptr;
+  auto release = [&]() {
+    if (!on_device) cudaFree(bf);
+    cudaFree(q);
+    cudaFree(sc);
+    cudaFree(amax);
+  };
+  cudaError_t e = cudaSuccess;
+  if (!on_device) {
+    e = cudaMalloc(&bf, n * 2);
+    // on the stream the quantisation runs on: a pageable cudaMemcpy may
+    // return before its DMA has landed, and ctx->stream does not wait for it
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(bf, data, n * 2, cudaMemcpyHostToDevice, ctx->stream);
+  } else {
+    bf = const_cast<uint16_t*>(data);
+  }
+  if (e == cudaSuccess) e = cudaMalloc(&q, n);
+  if (e == cudaSuccess) e = cudaMalloc(&sc, (size_t)rows * 4);
+  if (e == cudaSuccess) {
+    if (c.weight_kind == EC_W_INT8) {
+      e = ec::launch_quant_rows_int8(bf, reinterpret_cast<int8_t*>(q), sc, rows, cols, ctx->stream);
+    } else {
+      e = cudaMalloc(&amax, 4);
+      if (e == cudaSuccess) e = cudaMemsetAsync(amax, 0, 4, ctx->stream);
+      if (e == cudaSuccess) e = ec::launch_absmax_bf16(bf, (long)n, amax, ctx->stream);
+      unsigned bits = 0;
+      if (e == cudaSuccess) e = cudaMemcpyAsync(&bits, amax, 4, cudaMemcpyDeviceToHost, ctx->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+      if (e == cudaSuccess) {
+        float m = 0.0f;
+        memcpy(&m, &bits, 4);
+        const float s = m > 0.0f ? (float)exp2(ceil(log2((double)m / 448.0))) : 1.0f;
+        e = ec::launch_quant_fp8(bf, q, (long)n, s, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e == cudaSuccess) e = cudaMemcpy(sc, &s, 4, cudaMemcpyHostToDevice);
+      }
+    }
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) {
+    release();
+    return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+  }
+  const int rc = ec_set_weight(ctx, layer, which, q, sc, 1);
+  release();
+  return rc;
 }
 
 extern "C" int ec_reset(ec_ctx* ctx, int seq) {
@@ -635,6 +743,34 @@ ec::ChainPhase chain_phase(const Mat& m, int pro, int epi, const float* x, const
   return ph;
 }
 
+// The end of the step after the last layer's down projection when a final
+// adapter or logit bias is registered (inference.c:580-651): RMSNorm of x
+// (rows of D floats) into xn, the adapter xn -> xa, the LM head on it
+// (lm(in, out, rows) issues the caller's GEMV), the logit bias.
+template <typename LM>
+cudaError_t enqueue_final_extras(ec_ctx* ctx, const float* x, float* xn, float* xa, int B,
+                                 float* logits, LM lm) {
+  const ec_model_config& c = ctx->c;
+  cudaError_t e;
+  if ((e = ec::launch_rmsnorm_rows(xn, x, ctx->final_norm, c.dim, c.norm_eps, B, c.dim,
+                                   ctx->stream)))
+    return e;
+  ctx->launches++;
+  const float* in = xn;
+  if (ctx->adapter_on) {
+    if ((e = ec::launch_adapter(ctx->adapter, xn, xa, c.dim, B, ctx->stream))) return e;
+    ctx->launches++;
+    in = xa;
+  }
+  if ((e = lm(in, logits, B))) return e;
+  if (ctx->bias_on) {
+    if ((e = ec::launch_logit_bias(logits, ctx->logit_bias, c.vocab_size, B, ctx->stream)))
+      return e;
+    ctx->launches++;
+  }
+  return cudaSuccess;
+}
+
 // One layer's attention block after the QKV projection: the split path
 // (append + rank selection, split attention) or the reference-order path
 // (append + heap selection | linear-mode selection, attention).
@@ -676,6 +812,7 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   const ec_model_config& c = ctx->c;
   const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
   const int V = c.vocab_size, L = c.n_layers, QW = (H + 2 * KV) * hd;
+  const bool extras = ctx->adapter_on || ctx->bias_on;
   cudaError_t e;
   ctx->launches = 0;
   ec::StepBuffers sb{};
@@ -805,7 +942,7 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
                                      ctx->logits + (size_t)b0 * V)
                        : chain_phase(ctx->qkv[l + 1], ec::PRO_RMSNORM, ec::EPI_STORE, x,
                                      ctx->attn_norm[l + 1], ctx->qkvb + (size_t)b0 * QW);
-        P.nph = 4;
+        P.nph = (last && extras) ? 3 : 4;
       } else {
         P.ph[0] = phase(ctx->wo[l], ec::PRO_NONE, ec::EPI_RESID, att, H * hd, nullptr, x, D);
         P.ph[1] = norm(x, ctx->ffn_norm[l], xn);
@@ -816,10 +953,26 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
                                ctx->logits + (size_t)b0 * V, V)
                        : phase(ctx->qkv[l + 1], ec::PRO_NONE, ec::EPI_STORE, xn, D, nullptr,
                                ctx->qkvb + (size_t)b0 * QW, QW);
-        P.nph = 6;
+        P.nph = (last && extras) ? 4 : 6;
       }
       if ((e = run(P, l, pk, nb))) return e;
     }
+  }
+  if (extras) {
+    // final RMSNorm, adapter, then the LM head as one-phase chains per pack
+    auto lm = [&](const float* in, float* out, int rows) -> cudaError_t {
+      for (int b0 = 0, pk = 0; b0 < rows; b0 += kPack, pk++) {
+        const int nb = rows - b0 < kPack ? rows - b0 : kPack;
+        ec::ChainParams P{};
+        P.ph[0] = phase(ctx->lm, ec::PRO_NONE, ec::EPI_STORE, in + (size_t)b0 * D, D, nullptr,
+                        out + (size_t)b0 * V, V);
+        P.nph = 1;
+        cudaError_t e2 = run(P, L, pk, nb);
+        if (e2) return e2;
+      }
+      return cudaSuccess;
+    };
+    if ((e = enqueue_final_extras(ctx, ctx->x, ctx->xn, ctx->xa, B, ctx->logits, lm))) return e;
   }
   {
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
@@ -843,6 +996,7 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
   const ec_model_config& c = ctx->c;
   const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
   const int V = c.vocab_size, L = c.n_layers, QW = (H + 2 * KV) * hd;
+  const bool extras = ctx->adapter_on || ctx->bias_on;
   cudaError_t e;
   ctx->launches = 0;
   ec::StepBuffers sb{};
@@ -928,13 +1082,27 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
       if ((e = proj(ctx->wo[l], att, H * hd, nullptr, x, D, ec::EPI_RESID, nb))) return e;
       if ((e = proj(ctx->w13[l], x, D, ctx->ffn_norm[l], hb, F, ec::EPI_SWIGLU, nb))) return e;
       if ((e = proj(ctx->w2[l], hb, F, nullptr, x, D, ec::EPI_RESID, nb))) return e;
-      if (last)
+      if (last && extras)
+        e = cudaSuccess;  // the LM head runs after the adapter and bias below
+      else if (last)
         e = proj(ctx->lm, x, D, ctx->final_norm, ctx->logits + (size_t)b0 * V, V, ec::EPI_STORE, nb);
       else
         e = proj(ctx->qkv[l + 1], x, D, ctx->attn_norm[l + 1], ctx->qkvb + (size_t)b0 * QW, QW,
                  ec::EPI_STORE, nb);
       if (e) return e;
     }
+  }
+  if (extras) {
+    auto lm = [&](const float* in, float* out, int rows) -> cudaError_t {
+      for (int b0 = 0; b0 < rows; b0 += ec::kTcMaxRows) {
+        const int nb = rows - b0 < ec::kTcMaxRows ? rows - b0 : ec::kTcMaxRows;
+        cudaError_t e2 = proj(ctx->lm, in + (size_t)b0 * D, D, nullptr, out + (size_t)b0 * V, V,
+                              ec::EPI_STORE, nb);
+        if (e2) return e2;
+      }
+      return cudaSuccess;
+    };
+    if ((e = enqueue_final_extras(ctx, ctx->x, ctx->xn, ctx->xa, B, ctx->logits, lm))) return e;
   }
   {
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
@@ -966,6 +1134,7 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
   sb.sparse_blocks_k = c.sparse_blocks_k;
   sb.err = ctx->err;
   sb.max_sel = ctx->max_sel;
+  const bool extras = ctx->adapter_on || ctx->bias_on;
   for (int b = 0; b < B; b++) {
     // Batch-1 kernels: sequence b's state lives at offset b of every buffer.
     float* x = ctx->x + (size_t)b * D;
@@ -1034,7 +1203,8 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
                                 ctx->attn_norm[l + 1], sb.qkv);
         else
           P.ph[3] = chain_phase(ctx->lm, ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->final_norm, lg);
-        P.nph = 4;
+        // with a final adapter or logit bias the LM head runs after them
+        P.nph = (l + 1 == c.n_layers && extras) ? 3 : 4;
         P.ctr = ctx->chain_ctr + (size_t)l * ctx->npacks * (ec::kMaxChainPhases + 1);
         P.err = ctx->err;
         P.eps = c.norm_eps;
@@ -1044,8 +1214,9 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
         const double by = gemv_bytes(ctx->wo[l], ec::PRO_NONE, ec::EPI_RESID) +
                           gemv_bytes(ctx->w13[l], ec::PRO_RMSNORM, ec::EPI_SWIGLU) +
                           gemv_bytes(ctx->w2[l], ec::PRO_NONE, ec::EPI_RESID) +
-                          gemv_bytes(l + 1 < c.n_layers ? ctx->qkv[l + 1] : ctx->lm, ec::PRO_RMSNORM,
-                                     ec::EPI_STORE);
+                          (P.nph == 4 ? gemv_bytes(l + 1 < c.n_layers ? ctx->qkv[l + 1] : ctx->lm,
+                                                   ec::PRO_RMSNORM, ec::EPI_STORE)
+                                      : 0.0);
         ProfScope ps(ctx, EC_K_GEMV_CHAIN, by);
         if ((e = ec::chain_launch(c.weight_kind, P, ctx->n_sm, ctx->stream, true))) return e;
         ctx->launches++;
@@ -1060,7 +1231,15 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
                     nullptr, x)))
         return e;
     }
-    if (!chain) {
+    if (extras) {
+      auto lm = [&](const float* in, float* out, int) -> cudaError_t {
+        return gemv(ctx, EC_K_GEMV_LM, ctx->lm, ctx->p_lm, ec::PRO_NONE, ec::EPI_STORE, in, nullptr,
+                    out);
+      };
+      if ((e = enqueue_final_extras(ctx, x, ctx->xn + (size_t)b * D,
+                                    ctx->xa ? ctx->xa + (size_t)b * D : nullptr, 1, lg, lm)))
+        return e;
+    } else if (!chain) {
       if ((e = gemv(ctx, EC_K_GEMV_LM, ctx->lm, ctx->p_lm, ec::PRO_RMSNORM, ec::EPI_STORE, x,
                     ctx->final_norm, lg)))
         return e;
@@ -1243,23 +1422,29 @@ extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
   // down -- or with the chain: append, [select], attention, chain -- then
   // [LM head] and argmax
   const int sel = ctx->kv.paged ? 0 : ec::kLinearSelectLaunches;
+  // a registered final adapter / logit bias: final RMSNorm, [adapter], the
+  // LM head on its own, [bias]
+  const bool extras = ctx->adapter_on || ctx->bias_on;
+  const int ex = extras ? 1 + ctx->adapter_on + ctx->bias_on : 0;
   if (ctx->tc && B >= ctx->c.tensor_min_batch) {
     // embed, per pass QKV(0) (quant, GEMM, combine), per layer append,
     // [select], attention and 4 projections per pass, argmax per sequence
     const int passes = (B + ec::kTcMaxRows - 1) / ec::kTcMaxRows;
-    return 1 + 3 * passes + ctx->c.n_layers * (2 + sel + 12 * passes) + 1;
+    return 1 + 3 * passes + ctx->c.n_layers * (2 + sel + 12 * passes) + 1 + ex;
   }
   if (ctx->chain && B > 1) {
     const int packs = (B + kPack - 1) / kPack;
-    return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + 1;
+    return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + 1 + (extras ? ex + packs : 0);
   }
-  if (ctx->chain) return B * (2 + ctx->c.n_layers * (3 + sel) + 1);
-  return B * (1 + ctx->c.n_layers * (6 + sel) + 2);
+  if (ctx->chain) return B * (2 + ctx->c.n_layers * (3 + sel) + 1 + (extras ? ex + 1 : 0));
+  return B * (1 + ctx->c.n_layers * (6 + sel) + 2 + ex);
 }
 
 extern "C" int ec_read_state(ec_ctx* ctx, int which, int seq, float* out, size_t n) {
   if (!ctx || !out || seq < 0 || seq >= ctx->c.max_batch) return fail(EC_ERR_ARG, "bad argument");
   cudaSetDevice(ctx->device);
+  // the copies below run on the legacy stream, which does not wait for ctx->stream
+  EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   const ec_model_config& c = ctx->c;
   const int qkvw = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
   const float* src = nullptr;

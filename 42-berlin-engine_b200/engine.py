@@ -18,6 +18,7 @@ EC_W_INT8, EC_W_FP8, EC_W_BF16 = 0, 1, 2
 EC_ATTN_REFERENCE, EC_ATTN_SPLIT = 0, 1
 EC_WQ, EC_WK, EC_WV, EC_WO, EC_W1, EC_W2, EC_W3, EC_ATTN_NORM, EC_FFN_NORM = range(9)
 EC_EMBEDDING, EC_FINAL_NORM, EC_LM_HEAD = 16, 17, 18
+EC_FINAL_ADAPTER, EC_LOGIT_BIAS = 19, 20
 MAT_IDS = {"wq": EC_WQ, "wk": EC_WK, "wv": EC_WV, "wo": EC_WO, "w1": EC_W1, "w2": EC_W2,
            "w3": EC_W3}
 
@@ -33,7 +34,7 @@ EXPORTS = [
     "ec_transformer_forward", "ec_transformer_argmax", "ec_transformer_reset",
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read", "ec_lsh_attn_create",
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
-    "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill",
+    "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill", "ec_set_weight_bf16",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
@@ -82,6 +83,7 @@ def lib():
             "ec_create": (i, [C.POINTER(ModelConfig), i, C.POINTER(vp)]),
             "ec_destroy": (None, [vp]),
             "ec_set_weight": (i, [vp, i, i, vp, vp, i]),
+            "ec_set_weight_bf16": (i, [vp, i, i, vp, i]),
             "ec_reset": (i, [vp, i]),
             "ec_decode_step": (i, [vp, vp, vp, i, vp, vp]),
             "ec_decode_step_device": (i, [vp, vp, vp, i, i]),
@@ -188,6 +190,30 @@ class Engine:
         check(L.ec_set_weight(self.h, -1, EC_EMBEDDING, _ptr(model.emb), None, 0))
         check(L.ec_set_weight(self.h, -1, EC_FINAL_NORM, _ptr(model.final_norm), None, 0))
         check(L.ec_set_weight(self.h, -1, EC_LM_HEAD, _ptr(model.lm[0]), _ptr(model.lm[1]), 0))
+
+    def load_bf16(self, bf):
+        """Register BF16 host weights (synth.Model.bf16_weights() form); the
+        matrices are quantised on the device (ec_set_weight_bf16)."""
+        L = lib()
+        for i, lw in enumerate(bf["layers"]):
+            for n, mid in MAT_IDS.items():
+                check(L.ec_set_weight_bf16(self.h, i, mid, _ptr(np.ascontiguousarray(lw[n])), 0))
+            check(L.ec_set_weight(self.h, i, EC_ATTN_NORM, _ptr(lw["attention_norm"]), None, 0))
+            check(L.ec_set_weight(self.h, i, EC_FFN_NORM, _ptr(lw["ffn_norm"]), None, 0))
+        check(L.ec_set_weight(self.h, -1, EC_EMBEDDING, _ptr(bf["emb"]), None, 0))
+        check(L.ec_set_weight(self.h, -1, EC_FINAL_NORM, _ptr(bf["final_norm"]), None, 0))
+        check(L.ec_set_weight_bf16(self.h, -1, EC_LM_HEAD, _ptr(bf["lm"]), 0))
+
+    def set_final(self, adapter=None, logit_bias=None):
+        """Register the optional final hidden adapter (bf16 [dim][dim] host
+        array) and logit bias (float [vocab]); an all-zero tensor stays off."""
+        L = lib()
+        if adapter is not None:
+            check(L.ec_set_weight(self.h, -1, EC_FINAL_ADAPTER,
+                                  _ptr(np.ascontiguousarray(adapter, np.uint16)), None, 0))
+        if logit_bias is not None:
+            check(L.ec_set_weight(self.h, -1, EC_LOGIT_BIAS,
+                                  _ptr(np.ascontiguousarray(logit_bias, np.float32)), None, 0))
 
     def set_weight_device(self, layer, which, ptr, scale_ptr):
         check(lib().ec_set_weight(self.h, layer, which, C.c_void_p(ptr),

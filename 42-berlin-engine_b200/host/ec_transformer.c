@@ -45,6 +45,19 @@ static const struct
 	{"ffn_norm", EC_FFN_NORM}, {"post_attention_layernorm", EC_FFN_NORM},
 };
 
+/* A matrix with scales is already quantised (the context's INT8 / FP8
+** format); without scales it is the reference's BF16 tensor, quantised on
+** the device (ec_set_weight_bf16).  Vectors are BF16 either way. */
+static int	set_one(t_ec_transformer *t, int layer, int which, const void *data,
+		const float *scales)
+{
+	const int	matrix = (layer >= 0 && which <= EC_W3) || which == EC_LM_HEAD;
+
+	if (matrix && !scales)
+		return (ec_set_weight_bf16(t->ctx, layer, which, data, 0));
+	return (ec_set_weight(t->ctx, layer, which, data, matrix ? scales : NULL, 0));
+}
+
 int	ec_transformer_set_tensor(t_ec_transformer *t, const char *name,
 		const void *data, const float *scales)
 {
@@ -62,8 +75,7 @@ int	ec_transformer_set_tensor(t_ec_transformer *t, const char *name,
 			return (EC_ERR_ARG);
 		for (i = 0; i < sizeof(g_layer_names) / sizeof(g_layer_names[0]); i++)
 			if (strstr(name, g_layer_names[i].pat))
-				return (ec_set_weight(t->ctx, layer, g_layer_names[i].which,
-						data, scales, 0));
+				return (set_one(t, layer, g_layer_names[i].which, data, scales));
 		return (EC_ERR_ARG);
 	}
 	if (!strcmp(name, "tok_embeddings.weight")
@@ -72,7 +84,7 @@ int	ec_transformer_set_tensor(t_ec_transformer *t, const char *name,
 	if (!strcmp(name, "norm.weight") || !strcmp(name, "model.norm.weight"))
 		return (ec_set_weight(t->ctx, -1, EC_FINAL_NORM, data, NULL, 0));
 	if (!strcmp(name, "output.weight") || !strcmp(name, "lm_head.weight"))
-		return (ec_set_weight(t->ctx, -1, EC_LM_HEAD, data, scales, 0));
+		return (set_one(t, -1, EC_LM_HEAD, data, scales));
 	return (EC_ERR_ARG);
 }
 

@@ -34,7 +34,10 @@ int		ec_transformer_init(t_ec_transformer *t, const ec_model_config *c,
 ** the LLaMA (attention.wq, feed_forward.w1, attention_norm, ...) or
 ** HuggingFace (self_attn.q_proj, mlp.gate_proj, input_layernorm, ...)
 ** spellings, plus tok_embeddings / norm / output (or model.embed_tokens,
-** model.norm, lm_head).  `scales` as for ec_set_weight. */
+** model.norm, lm_head).  A matrix passed with `scales` is already in the
+** context's weight format (as ec_set_weight); with scales == NULL it is the
+** reference's BF16 tensor and is quantised on the device
+** (ec_set_weight_bf16). */
 int		ec_transformer_set_tensor(t_ec_transformer *t, const char *name,
 			const void *data, const float *scales);
 

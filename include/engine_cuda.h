@@ -54,6 +54,11 @@ extern "C" {
 # define EC_EMBEDDING 16
 # define EC_FINAL_NORM 17
 # define EC_LM_HEAD 18
+/* optional global tensors (inference.c:583-651); a tensor that is all zero
+** (the reference's zero-initialised state) is kept switched off */
+# define EC_FINAL_ADAPTER 19	/* bf16 [dim][dim]: x += 16 * (A . x) after the
+								** final RMSNorm, before the LM head */
+# define EC_LOGIT_BIAS 20		/* float [vocab_size]: logits += bias */
 
 typedef struct ec_model_config
 {
@@ -125,9 +130,27 @@ void	ec_destroy(ec_ctx *ctx);
 ** pointer unless `on_device` is nonzero.  Matrices are row-major
 ** [out_features][in_features] in the context's weight_kind; `scales` holds
 ** one float per row (INT8) or one float (FP8).  Norm weights and the
-** embedding are BF16 and take scales = NULL.  Data is copied. */
+** embedding are BF16 and take scales = NULL.  Data is copied.  With
+** on_device = 1 the call first waits for the whole device
+** (cudaDeviceSynchronize: data a caller's stream still writes is complete),
+** so it must not run while another stream on the device is capturing a
+** graph. */
 int		ec_set_weight(ec_ctx *ctx, int layer, int which, const void *data,
 			const float *scales, int on_device);
+
+/* Quantise-at-load: the reference loads BF16 tensors only
+** (loader_parse.c:35-49, t_dtype tensor.h:20-24).  `data` is a BF16 matrix
+** [out_features][in_features] (host, or device when on_device); it is
+** quantised on the device to the context's weight_kind and registered as
+** ec_set_weight would: INT8 per row with scale = max|w| / 127 (1 / 127 for
+** a zero row), q = clamp(rint(w / scale), +-127); FP8 E4M3 per tensor with
+** scale = 2^ceil(log2(max|w| / 448)) (1 for an all-zero tensor) and the
+** nearest E4M3 value of w / scale, ties to even, saturating.  Ids other
+** than the seven matrices and EC_LM_HEAD are passed to ec_set_weight
+** (they are BF16 already).  Like ec_set_weight(on_device = 1), device data
+** makes the call synchronise the device first. */
+int		ec_set_weight_bf16(ec_ctx *ctx, int layer, int which, const uint16_t *data,
+			int on_device);
 
 /* Start sequence `seq` fresh (paged_kv_reset, paged.c:297; lsh_index_reset,
 ** ops_lsh.c:111). */

@@ -17,6 +17,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_SO = os.path.join(HERE, "libec_port.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_driver.so")
+DROPIN_SO = os.path.join(HERE, "_ref", "libref_dropin.so")
 
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
@@ -142,48 +143,73 @@ def ref_available():
     return os.path.exists(REF_SO)
 
 
+def dropin_available():
+    return os.path.exists(DROPIN_SO)
+
+
+_dropin = None
+
+
+def dropin():
+    """The reference engine built with the drop-in hook (oracle/dropin.py):
+    its transformer_forward calls libengine_cuda.so once a context is
+    attached with refd_attach_gpu.  Load libengine_cuda.so first (the engine
+    binding) so that both share one copy of it."""
+    global _dropin
+    if _dropin is None:
+        _dropin = _bind(C.CDLL(DROPIN_SO))
+        _sig(_dropin, "refd_attach_gpu", None, C.c_void_p, C.c_void_p)
+    return _dropin
+
+
 def ref():
     """The reference engine's own code, compiled from its sources by oracle/Makefile."""
     global _ref
     if _ref is None:
-        lib = C.CDLL(REF_SO)
-        vp = C.c_void_p
-        _sig(lib, "refd_create", vp, C.POINTER(RefdConfig), vp, vp, vp, C.POINTER(vp))
-        _sig(lib, "refd_forward", C.POINTER(C.c_float), vp, C.c_int, C.c_int)
-        _sig(lib, "refd_fill_context", C.c_int, vp, C.c_int, C.c_uint)
-        _sig(lib, "refd_state", C.POINTER(C.c_float), vp, C.c_int)
-        _sig(lib, "refd_lsh_index", C.POINTER(LshIndex), vp)
-        _sig(lib, "refd_paged_block", C.c_int, vp, C.c_int, C.c_int, i8p, i8p, f32p, f32p,
-             f32p)
-        _sig(lib, "refd_linear_k", C.POINTER(C.c_uint16), vp, C.c_int)
-        _sig(lib, "refd_lsh_counters", None, vp, C.POINTER(C.c_ulonglong))
-        _sig(lib, "refd_matmul", C.c_int, f32p, u16p, f32p, C.c_int, C.c_int)
-        _sig(lib, "refd_rmsnorm", None, f32p, f32p, u16p, C.c_int, C.c_float)
-        _sig(lib, "refd_rope_create", vp, C.c_int, C.c_int, C.c_float)
-        _sig(lib, "refd_rope_table", C.POINTER(C.c_float), vp, C.c_int)
-        _sig(lib, "refd_rope_apply", None, vp, f32p, C.c_int, C.c_int)
-        _sig(lib, "refd_silu_mul", None, f32p, f32p, f32p, C.c_int)
-        _sig(lib, "refd_quant_int8", C.c_float, i8p, f32p, C.c_int)
-        _sig(lib, "refd_argmax", C.c_int, f32p, C.c_int)
-        _sig(lib, "refd_heap_topk", C.c_int, f32p, i32p, C.c_int, C.c_int, i32p)
-        _sig(lib, "refd_lsh_ctx_create", vp, C.c_int, C.c_uint)
-        _sig(lib, "refd_lsh_hyperplanes", C.POINTER(C.c_float), vp)
-        _sig(lib, "refd_lsh_hash", C.c_int, vp, f32p)
-        _sig(lib, "refd_lsh_index_create", vp)
-        _sig(lib, "refd_lsh_update", None, vp, vp, f32p, C.c_int, C.c_int)
-        _sig(lib, "refd_lsh_find", C.c_int, vp, C.c_int, i32p, C.c_int)
-        _sig(lib, "refd_paged_create", vp, C.c_int, C.c_int, C.c_int)
-        _sig(lib, "refd_paged_append", None, vp, f32p, f32p, C.c_int)
-        _sig(lib, "refd_paged_phys", C.c_int, vp, C.c_int)
-        _sig(lib, "refd_paged_nblocks", C.c_int, vp)
-        _sig(lib, "refd_paged_attention", None, vp, f32p, f32p, C.c_int, C.c_int, C.c_int)
-        _sig(lib, "refd_paged_sparse", C.c_int, vp, f32p, f32p, C.c_int, C.c_int, C.c_int,
-             C.c_int, i32p)
-        _sig(lib, "refd_paged_scores", None, vp, f32p, f32p)
-        _sig(lib, "refd_linear_sparse_attention", None, f32p, f32p, u16p, u16p, C.c_int,
-             i32p, C.c_int, C.c_int, C.c_int, C.c_int)
-        _ref = lib
+        _ref = _bind(C.CDLL(REF_SO))
     return _ref
+
+
+def _bind(lib):
+    """Signatures of the refd_* driver calls (ref_driver.c)."""
+    vp = C.c_void_p
+    _sig(lib, "refd_create", vp, C.POINTER(RefdConfig), vp, vp, vp, C.POINTER(vp))
+    _sig(lib, "refd_forward", C.POINTER(C.c_float), vp, C.c_int, C.c_int)
+    _sig(lib, "refd_fill_context", C.c_int, vp, C.c_int, C.c_uint)
+    _sig(lib, "refd_set_adapter", None, vp, vp)
+    _sig(lib, "refd_set_logit_bias", None, vp, vp)
+    _sig(lib, "refd_state", C.POINTER(C.c_float), vp, C.c_int)
+    _sig(lib, "refd_lsh_index", C.POINTER(LshIndex), vp)
+    _sig(lib, "refd_paged_block", C.c_int, vp, C.c_int, C.c_int, i8p, i8p, f32p, f32p,
+         f32p)
+    _sig(lib, "refd_linear_k", C.POINTER(C.c_uint16), vp, C.c_int)
+    _sig(lib, "refd_lsh_counters", None, vp, C.POINTER(C.c_ulonglong))
+    _sig(lib, "refd_matmul", C.c_int, f32p, u16p, f32p, C.c_int, C.c_int)
+    _sig(lib, "refd_rmsnorm", None, f32p, f32p, u16p, C.c_int, C.c_float)
+    _sig(lib, "refd_rope_create", vp, C.c_int, C.c_int, C.c_float)
+    _sig(lib, "refd_rope_table", C.POINTER(C.c_float), vp, C.c_int)
+    _sig(lib, "refd_rope_apply", None, vp, f32p, C.c_int, C.c_int)
+    _sig(lib, "refd_silu_mul", None, f32p, f32p, f32p, C.c_int)
+    _sig(lib, "refd_quant_int8", C.c_float, i8p, f32p, C.c_int)
+    _sig(lib, "refd_argmax", C.c_int, f32p, C.c_int)
+    _sig(lib, "refd_heap_topk", C.c_int, f32p, i32p, C.c_int, C.c_int, i32p)
+    _sig(lib, "refd_lsh_ctx_create", vp, C.c_int, C.c_uint)
+    _sig(lib, "refd_lsh_hyperplanes", C.POINTER(C.c_float), vp)
+    _sig(lib, "refd_lsh_hash", C.c_int, vp, f32p)
+    _sig(lib, "refd_lsh_index_create", vp)
+    _sig(lib, "refd_lsh_update", None, vp, vp, f32p, C.c_int, C.c_int)
+    _sig(lib, "refd_lsh_find", C.c_int, vp, C.c_int, i32p, C.c_int)
+    _sig(lib, "refd_paged_create", vp, C.c_int, C.c_int, C.c_int)
+    _sig(lib, "refd_paged_append", None, vp, f32p, f32p, C.c_int)
+    _sig(lib, "refd_paged_phys", C.c_int, vp, C.c_int)
+    _sig(lib, "refd_paged_nblocks", C.c_int, vp)
+    _sig(lib, "refd_paged_attention", None, vp, f32p, f32p, C.c_int, C.c_int, C.c_int)
+    _sig(lib, "refd_paged_sparse", C.c_int, vp, f32p, f32p, C.c_int, C.c_int, C.c_int,
+         C.c_int, i32p)
+    _sig(lib, "refd_paged_scores", None, vp, f32p, f32p)
+    _sig(lib, "refd_linear_sparse_attention", None, f32p, f32p, u16p, u16p, C.c_int,
+         i32p, C.c_int, C.c_int, C.c_int, C.c_int)
+    return lib
 
 
 # ---------------------------------------------------------------------------
@@ -260,7 +286,7 @@ class RefModel:
     path's bit for bit.
     """
 
-    def __init__(self, model, use_paged_kv=True, sparse_k=64):
+    def __init__(self, model, use_paged_kv=True, sparse_k=64, lib=None):
         cfg = model.cfg
         self.cfg = cfg
         bf = model.bf16_weights()
@@ -278,7 +304,7 @@ class RefModel:
                        norm_eps=cfg.norm_eps, use_paged_kv=int(use_paged_kv),
                        sparse_k=sparse_k)
         self._keep += [ptrs, c]
-        self.lib = ref()
+        self.lib = lib or ref()
         self.h = self.lib.refd_create(C.byref(c), bf["emb"].ctypes.data,
                                       bf["final_norm"].ctypes.data, bf["lm"].ctypes.data, ptrs)
 
@@ -290,6 +316,14 @@ class RefModel:
         out = (C.c_ulonglong * 2)()
         self.lib.refd_lsh_counters(self.h, out)
         return int(out[0]), int(out[1])
+
+    def set_final(self, adapter=None, logit_bias=None):
+        """Attach the final hidden adapter (bf16 [dim][dim]) and the logit bias
+        (float [vocab]); None detaches."""
+        self._keep += [adapter, logit_bias]
+        self.lib.refd_set_adapter(self.h, adapter.ctypes.data if adapter is not None else None)
+        self.lib.refd_set_logit_bias(self.h,
+                                     logit_bias.ctypes.data if logit_bias is not None else None)
 
     def fill_context(self, n, seed=1):
         """Positions 0..n-1 of the paged cache from synthetic K/V through the

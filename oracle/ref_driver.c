@@ -189,6 +189,31 @@ float	*refd_forward(void *h, int token, int pos)
 	return (transformer_forward(&((t_refd *)h)->t, token, pos));
 }
 
+#ifdef ENGINE_CUDA
+/* drop-in build only: attach a libengine_cuda context (NULL: CPU path) */
+void	refd_attach_gpu(void *h, void *ctx)
+{
+	((t_refd *)h)->t.gpu = (struct ec_ctx *)ctx;
+}
+#endif
+
+/*
+** The optional final hidden adapter (bf16 [dim][dim]) and logit bias (float
+** [vocab]) that transformer_forward applies after the final norm
+** (inference.c:583-651); NULL detaches.  The caller keeps the memory.
+*/
+void	refd_set_adapter(void *h, const uint16_t *adapter)
+{
+	t_refd	*r = (t_refd *)h;
+
+	r->t.final_adapter = adapter ? mk2d(r, adapter, r->t.config.dim, r->t.config.dim) : NULL;
+}
+
+void	refd_set_logit_bias(void *h, const float *bias)
+{
+	((t_refd *)h)->t.logit_bias = (float *)bias;
+}
+
 /*
 ** Fill positions 0..n-1 of every layer's paged KV cache with seeded
 ** synthetic keys and values through the reference's own paged_kv_append

@@ -50,6 +50,20 @@ def test_default_config_is_reference_defaults(eng):
     assert c.use_paged_kv == 1
 
 
+def test_config_struct_layout_matches_header(eng):
+    """ec_config_default writes exactly sizeof(ec_model_config) bytes: the
+    ctypes mirror has the header's size (no byte past it is touched) and
+    the fields the header appended last (attention_mode, wait_limit) default
+    to 0."""
+    n = C.sizeof(eng.ModelConfig)
+    buf = (C.c_uint8 * (n + 64))(*([0xAB] * (n + 64)))
+    assert eng.lib().ec_config_default(C.cast(buf, C.POINTER(eng.ModelConfig))) == 0
+    assert bytes(buf[n:]) == b"\xab" * 64
+    c = eng.ModelConfig.from_buffer(buf)
+    assert c.attention_mode == 0 and c.wait_limit == 0 and c.max_batch == 1
+    assert bytes(buf[n - 4:n]) == b"\x00" * 4
+
+
 def test_argument_errors_without_device(eng):
     L = eng.lib()
     assert L.ec_create(None, 0, None) == eng.EC_ERR_ARG

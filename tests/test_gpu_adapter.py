@@ -1,0 +1,84 @@
+"""The final hidden adapter and logit bias (inference.c:583-651) against the
+reference itself: transformer_forward of oracle/_ref with the same adapter
+(bf16 [dim][dim], x += 16 * (A . x) after the final RMSNorm) and bias
+(logits += bias) attached.
+
+Bit-exact on the exact paths (batch 1 and the batched chain); within
+BASELINE's 2e-2 of the logit range with equal greedy tokens on the
+tensor-core batched step; an all-zero adapter and bias stay switched off
+(the reference's zero-initialised tensors change nothing)."""
+import numpy as np
+import pytest
+
+from conftest import load_pkg_module
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def eng():
+    return load_pkg_module("engine")
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def _setup(synth, seed=5):
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4,
+                            vocab_size=2048, seq_len=512, head_dim=64, rope_theta=1e4)
+    model = synth.make_model(cfg, seed=seed)
+    rng = np.random.default_rng(seed)
+    adapter = synth.f32_to_bf16(rng.standard_normal((cfg.dim, cfg.dim), dtype=np.float32)
+                                * np.float32(0.002))
+    bias = (rng.standard_normal(cfg.vocab_size, dtype=np.float32) * np.float32(0.5))
+    return cfg, model, adapter, bias
+
+
+@pytest.mark.parametrize("B,tmb", [(1, 0), (3, 0), (16, 16)])
+def test_adapter_and_bias_match_reference(eng, torch, ref, synth, B, tmb):
+    cfg, model, adapter, bias = _setup(synth)
+    e = eng.Engine(cfg, max_batch=B, tensor_min_batch=tmb)
+    e.load(model)
+    e.set_final(adapter, bias)
+    rms = []
+    for _ in range(B):
+        m = ref.RefModel(model, use_paged_kv=True, sparse_k=64)
+        m.set_final(adapter, bias)
+        rms.append(m)
+    prompts = [synth.prompt(cfg, 40, seed=30 + b) for b in range(B)]
+    toks = [int(p[0]) for p in prompts]
+    P = ref.port()
+    for t in range(48):
+        lg, am = e.step(toks, [t] * B)
+        for b in range(B):
+            want = rms[b].forward(toks[b], t)
+            if tmb:
+                d = float(np.abs(lg[b] - want).max())
+                assert d <= 2e-2 * float(want.max() - want.min()), f"step {t} sequence {b}"
+            else:
+                assert np.array_equal(lg[b].view(np.uint32), want.view(np.uint32)), \
+                    f"step {t} sequence {b}"
+            assert int(am[b]) == P.port_argmax(want, want.size), f"token {t} sequence {b}"
+        toks = [int(prompts[b][t + 1]) if t + 1 < 40 else int(am[b]) for b in range(B)]
+    e.close()
+
+
+def test_zero_adapter_and_bias_stay_off(eng, torch, ref, synth):
+    cfg, model, adapter, bias = _setup(synth, seed=6)
+    e = eng.Engine(cfg)
+    e.load(model)
+    n0 = e.launches_per_step(1)
+    e.set_final(np.zeros_like(adapter), np.zeros_like(bias))
+    assert e.launches_per_step(1) == n0
+    m = ref.RefModel(model, use_paged_kv=True, sparse_k=64)
+    for p, t in enumerate(synth.prompt(cfg, 8, seed=2)):
+        lg, _ = e.step([int(t)], [p])
+        assert np.array_equal(lg[0].view(np.uint32), m.forward(int(t), p).view(np.uint32))
+    e.set_final(adapter, bias)
+    assert e.launches_per_step(1) == n0 + 4  # final norm, adapter, LM head, bias
+    e.close()
