@@ -137,7 +137,9 @@ __global__ void __launch_bounds__(256) linear_cand_kernel(KvLayout kv, LshLayout
   pdl_wait();
   const int pos = step_pos(sb, b);
   const int kv_len = min(pos + 1, kv.seq_len);
-  const float* q = sb.qrot + (long)b * H * hd;
+  // every query head (tensor parallelism: all ranks' heads, gathered)
+  const int Hq = sb.q_all ? sb.h_all : H;
+  const float* q = sb.q_all ? sb.q_all + (long)b * Hq * hd : sb.qrot + (long)b * H * hd;
   if (!(sb.sparse_k > 0 && kv_len > sb.sparse_k)) {
     if (tid == 0) {
       sb.nsel[b] = -1;  // dense attention over [0, kv_len)
@@ -154,8 +156,8 @@ __global__ void __launch_bounds__(256) linear_cand_kernel(KvLayout kv, LshLayout
     // q_mean over all heads (inference.c:290-295)
     for (int d = tid; d < hd; d += blockDim.x) {
       float a = 0.0f;
-      for (int h = 0; h < H; h++) a = __fadd_rn(a, q[h * hd + d]);
-      qm[d] = __fdiv_rn(a, (float)H);
+      for (int h = 0; h < Hq; h++) a = __fadd_rn(a, q[h * hd + d]);
+      qm[d] = __fdiv_rn(a, (float)Hq);
     }
     if (tid < 16) s_code[tid] = 0;
     for (int i = tid; i < lsh.max_units / 32 + 1 && i < 4096 / 32; i += blockDim.x) s_seen[i] = 0;
@@ -259,11 +261,36 @@ __global__ void __launch_bounds__(256) linear_score_kernel(KvLayout kv, StepBuff
     part[tid] = dot_bf16_ref(kv.lk + ((lrow + pos) * KV + kh) * hd, q + kh * grp * hd, hd);
   }
   __syncthreads();
+  if (sb.score_parts) {
+    // tensor parallelism: this rank's heads' dots, summed after the gather
+    if (live) sb.score_parts[((long)b * cap_c + c) * KV + kh] = part[tid];
+    return;
+  }
   if (live && kh == 0) {
     float sc = 0.0f;
     for (int h = 0; h < KV; h++) sc = __fadd_rn(sc, part[tid + h]);
     sb.lscore[(long)b * cap_c + c] = sc;
   }
+}
+
+// Tensor parallelism: the candidate scores from every rank's per-head dots
+// (parts_all [world][B][cap][kv_local], ranks holding consecutive KV heads),
+// added in global head order from 0 as linear_score_kernel does.
+__global__ void tp_sum_scores_kernel(StepBuffers sb, const float* __restrict__ parts_all,
+                                     int world, int kv_local, int cap_c, int B) {
+  const int b = blockIdx.y;
+  const int nc = sb.lnc[b];
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < nc; c += gridDim.x * blockDim.x) {
+    float sc = 0.0f;
+    for (int r = 0; r < world; r++)
+      for (int h = 0; h < kv_local; h++)
+        sc = __fadd_rn(sc, parts_all[(((long)r * B + b) * cap_c + c) * kv_local + h]);
+    sb.lscore[(long)b * cap_c + c] = sc;
+  }
+}
+
+__global__ void lsh_update_key_kernel(LshLayout lsh, StepBuffers sb, const float* k, int hd) {
+  lsh_update_token(lsh, 0, k, step_pos(sb, 0), hd);
 }
 
 // The top-K of the scored candidates (heap_push, inference.c:356-423): one
@@ -1405,6 +1432,37 @@ cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const
                   sb, layer, cap_c);
   if (!e) e = launch_ex(linear_heap_kernel, dim3(B), dim3(32), 0, s, pdl, lsh, sb, cap_c);
   return e;
+}
+
+cudaError_t launch_linear_candidates(const KvLayout& kv, const LshLayout& lsh,
+                                     const StepBuffers& sb, int layer, int B, cudaStream_t s) {
+  return launch_ex(linear_cand_kernel, dim3(B), dim3(256), (size_t)kv.head_dim * 4, s, false, kv,
+                   lsh, sb, layer);
+}
+
+cudaError_t launch_linear_score_parts(const KvLayout& kv, const LshLayout& lsh,
+                                      const StepBuffers& sb, int layer, int B, cudaStream_t s) {
+  const int cap_c = linear_cand_cap(sb, lsh);
+  const int cpb = 256 / kv.n_kv_heads;
+  return launch_ex(linear_score_kernel, dim3((cap_c + cpb - 1) / cpb, B), dim3(256), 0, s, false,
+                   kv, sb, layer, cap_c);
+}
+
+cudaError_t launch_linear_sum_heap(const LshLayout& lsh, const StepBuffers& sb,
+                                   const float* parts_all, int world, int kv_local, int B,
+                                   cudaStream_t s) {
+  const int cap_c = linear_cand_cap(sb, lsh);
+  tp_sum_scores_kernel<<<dim3(32, B), 256, 0, s>>>(sb, parts_all, world, kv_local, cap_c, B);
+  cudaError_t e = cudaGetLastError();
+  if (!e) e = launch_ex(linear_heap_kernel, dim3(B), dim3(32), 0, s, false, lsh, sb, cap_c);
+  return e;
+}
+
+cudaError_t launch_lsh_update_key(const LshLayout& lsh, const StepBuffers& sb, const float* k,
+                                  int hd, cudaStream_t s) {
+  if (lsh.tables <= 0) return cudaSuccess;
+  lsh_update_key_kernel<<<1, 256, 0, s>>>(lsh, sb, k, hd);
+  return cudaGetLastError();
 }
 
 bool use_group_attention(const KvLayout& kv, const StepBuffers& sb, int B) {

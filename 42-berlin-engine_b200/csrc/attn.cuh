@@ -68,6 +68,13 @@ struct StepBuffers {
   int defer_centroid;   // paged prefill: the append leaves block centroids to
                         // launch_paged_centroids (rows of one launch share a block)
   int fast_tpc;         // split attention: tokens per CTA (set by its launcher)
+  // tensor parallelism (linear mode): the LSH query mean reads every rank's
+  // rotated queries (q_all [B][h_all][hd], all-gathered), and the candidate
+  // scores leave their per-KV-head dots in score_parts [B][cap][KV] for the
+  // cross-rank sum in head order (tp_sum_scores)
+  const float* q_all;
+  int h_all;
+  float* score_parts;
 };
 
 // Linear-mode candidate capacity per sequence: the window plus max_cand
@@ -101,6 +108,21 @@ cudaError_t launch_paged_select_rows(const KvLayout& kv, const StepBuffers& sb, 
                                      cudaStream_t s);
 cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const StepBuffers& sb,
                                  int layer, int B, cudaStream_t s, bool pdl);
+// The same in three pieces for tensor parallelism: candidates (every rank,
+// identical), per-KV-head dots into sb.score_parts (this rank's heads), and,
+// once the dots of all ranks are gathered ([world][cap][KV per rank] from
+// `parts_all`), their sum in global head order followed by the heap.
+cudaError_t launch_linear_candidates(const KvLayout& kv, const LshLayout& lsh,
+                                     const StepBuffers& sb, int layer, int B, cudaStream_t s);
+cudaError_t launch_linear_score_parts(const KvLayout& kv, const LshLayout& lsh,
+                                      const StepBuffers& sb, int layer, int B, cudaStream_t s);
+cudaError_t launch_linear_sum_heap(const LshLayout& lsh, const StepBuffers& sb,
+                                   const float* parts_all, int world, int kv_local, int B,
+                                   cudaStream_t s);
+// lsh_update (layer 0, KV head 0) from a key vector that is not in sb.qkv
+// (tensor parallelism: the gathered keys of every rank)
+cudaError_t launch_lsh_update_key(const LshLayout& lsh, const StepBuffers& sb, const float* k,
+                                  int hd, cudaStream_t s);
 cudaError_t launch_attention(const KvLayout& kv, const StepBuffers& sb, int layer, int B,
                              cudaStream_t s, bool pdl);
 // Batched paged steps whose attention runs as attention_group_kernel (one CTA

@@ -463,6 +463,23 @@ cudaError_t launch_quant_fp8(const uint16_t* w, uint8_t* q, long n, float scale,
   return cudaGetLastError();
 }
 
+// Tensor parallelism: x[i] += sum of the ranks' partials of a row-split
+// projection, added in rank order (parts [world][n]); every rank computes the
+// same sum, so x stays identical on all ranks.
+__global__ void tp_resid_kernel(float* __restrict__ x, const float* __restrict__ parts, int world,
+                                int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    float sum = parts[i];
+    for (int r = 1; r < world; r++) sum = __fadd_rn(sum, parts[(long)r * n + i]);
+    x[i] = __fadd_rn(x[i], sum);
+  }
+}
+
+cudaError_t launch_tp_resid(float* x, const float* parts, int world, int n, cudaStream_t s) {
+  tp_resid_kernel<<<(n + 255) / 256 < 64 ? (n + 255) / 256 : 64, 256, 0, s>>>(x, parts, world, n);
+  return cudaGetLastError();
+}
+
 // out[0] |= 1 when any of n elements of `bits`-bit width is not +0 / -0.
 __global__ void nonzero_kernel(const void* p, long n, int bits, int* out) {
   int any = 0;

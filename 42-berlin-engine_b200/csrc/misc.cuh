@@ -28,6 +28,8 @@ cudaError_t launch_quant_rows_int8(const uint16_t* w, int8_t* q, float* scale, i
                                    cudaStream_t s);
 cudaError_t launch_absmax_bf16(const uint16_t* w, long n, unsigned* out, cudaStream_t s);
 cudaError_t launch_quant_fp8(const uint16_t* w, uint8_t* q, long n, float scale, cudaStream_t s);
+// tensor parallelism: x += sum over ranks (in rank order) of parts [world][n]
+cudaError_t launch_tp_resid(float* x, const float* parts, int world, int n, cudaStream_t s);
 cudaError_t launch_rope(float* data, int n_heads, int hd, int pos, const float* c, const float* sn,
                         int max_seq, cudaStream_t s);
 cudaError_t launch_silu(float* out, const float* g, const float* u, int n, cudaStream_t s);

@@ -16,6 +16,7 @@
 #include "gemv.cuh"
 #include "misc.cuh"
 #include "tc_gemm.cuh"
+#include "tp.cuh"
 
 static thread_local char g_err[512];
 
@@ -40,7 +41,19 @@ struct Mat {
 }  // namespace
 
 struct ec_ctx {
-  ec_model_config c;
+  ec_model_config c;   // shapes of this context (of one shard under tensor parallelism)
+  ec_model_config cg;  // shapes of the whole model (== c without tensor parallelism)
+  // tensor parallelism (ec_create_tp): rank, ranks, the NCCL communicator and
+  // the exchange buffers of one sequence step
+  int tp_rank = 0, tp_world = 1;
+  void* nccl = nullptr;
+  float* tp_q = nullptr;      // [H_all * hd] rotated queries of every rank
+  float* tp_k = nullptr;      // [KV_all * hd] rotated keys of every rank
+  float* tp_part = nullptr;   // [dim] partial of a row-split projection on this rank
+  float* tp_parts = nullptr;  // [world][dim] the partials of every rank
+  float* tp_sp = nullptr;     // [cap][KV] per-head candidate dots of this rank
+  float* tp_sps = nullptr;    // [world][cap][KV]
+  float* tp_lg = nullptr;     // [vocab / world] logits of this rank
   int device = 0;
   int n_sm = 148;
   cudaStream_t stream = nullptr;
@@ -202,6 +215,12 @@ extern "C" int ec_config_default(ec_model_config* c) {
 extern "C" void ec_destroy(ec_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
+  if (ctx->nccl) {
+    cudaStreamSynchronize(ctx->stream);
+    if (const ec::NcclApi* api = ec::nccl_api(nullptr))
+      api->comm_destroy(static_cast<ncclComm_t>(ctx->nccl));
+    ctx->nccl = nullptr;
+  }
   if (ctx->gexec) cudaGraphExecDestroy(ctx->gexec);
   cudaStreamSynchronize(ctx->stream);
   for (auto& r : ctx->recs) {
@@ -214,9 +233,12 @@ extern "C" void ec_destroy(ec_ctx* ctx) {
   delete ctx;
 }
 
-extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
-  if (!cfg || !out) return fail(EC_ERR_ARG, "null argument");
-  const ec_model_config& c = *cfg;
+namespace {
+
+// Context for shapes c on `device`; `global` (tensor parallelism) holds the
+// shapes of the whole model, of which c is the shard of rank `rank`.
+int create_ctx(const ec_model_config& c, int device, const ec_model_config* global, int rank,
+               int world, ec_ctx** out) {
   if (c.dim <= 0 || c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
       c.n_heads % c.n_kv_heads || (c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128) || c.dim % 32 ||
       c.hidden_dim % 32 || c.vocab_size <= 0 || c.seq_len <= 0 || c.max_batch <= 0)
@@ -238,6 +260,9 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
   ec_ctx* ctx = new ec_ctx();
   ctx->c = c;
+  ctx->cg = global ? *global : c;
+  ctx->tp_rank = rank;
+  ctx->tp_world = world;
   ctx->device = device;
   cudaDeviceGetAttribute(&ctx->n_sm, cudaDevAttrMultiProcessorCount, device);
   ctx->esize = 1;
@@ -253,6 +278,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   TRY(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
   const int L = c.n_layers, H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim;
   const int F = c.hidden_dim, V = c.vocab_size, S = c.max_batch;
+  const int Vg = ctx->cg.vocab_size;  // embedding rows, logits per sequence
   ctx->qkv.resize(L);
   ctx->wo.resize(L);
   ctx->w13.resize(L);
@@ -279,7 +305,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   TRY(dalloc(ctx, &ctx->lm.w, ec::packed_bytes(V, D)));
   TRY(cudaMemset(ctx->lm.w, 0, ec::packed_bytes(V, D)));
   TRY(dalloc(ctx, &ctx->lm.scale, (size_t)V));
-  TRY(dalloc(ctx, &ctx->emb, (size_t)V * D));
+  TRY(dalloc(ctx, &ctx->emb, (size_t)Vg * D));
   TRY(dalloc(ctx, &ctx->final_norm, (size_t)D));
   // activations
   TRY(dalloc(ctx, &ctx->x, (size_t)S * D));
@@ -287,7 +313,7 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
   TRY(dalloc(ctx, &ctx->att, (size_t)S * H * hd));
   TRY(dalloc(ctx, &ctx->qrot, (size_t)S * H * hd));
   TRY(dalloc(ctx, &ctx->hbuf, (size_t)S * F));
-  TRY(dalloc(ctx, &ctx->logits, (size_t)S * V));
+  TRY(dalloc(ctx, &ctx->logits, (size_t)S * Vg));
   TRY(dalloc(ctx, &ctx->argmax, (size_t)S));
   TRY(dalloc(ctx, &ctx->tokens, (size_t)S));
   TRY(dalloc(ctx, &ctx->pos, (size_t)S));
@@ -457,10 +483,89 @@ extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
     ctx->fast = c.attention_mode;
     TRY(ec::fast_attention_prepare(ctx->kv));
   }
+  if (world > 1) {
+    const ec_model_config& g = ctx->cg;
+    const int cap = ctx->kv.paged ? 0 : ctx->cap_c;
+    TRY(dalloc(ctx, &ctx->tp_q, (size_t)g.n_heads * hd));
+    TRY(dalloc(ctx, &ctx->tp_k, (size_t)g.n_kv_heads * hd));
+    TRY(dalloc(ctx, &ctx->tp_part, (size_t)D));
+    TRY(dalloc(ctx, &ctx->tp_parts, (size_t)world * D));
+    TRY(dalloc(ctx, &ctx->tp_lg, (size_t)V));
+    if (cap) {
+      TRY(dalloc(ctx, &ctx->tp_sp, (size_t)cap * KV));
+      TRY(dalloc(ctx, &ctx->tp_sps, (size_t)world * cap * KV));
+    }
+  }
 #undef TRY
   *out = ctx;
   for (int s = 0; s < S; s++) ec_reset(ctx, s);
   return cudaDeviceSynchronize() == cudaSuccess ? EC_OK : EC_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" int ec_create(const ec_model_config* cfg, int device, ec_ctx** out) {
+  if (!cfg || !out) return fail(EC_ERR_ARG, "null argument");
+  return create_ctx(*cfg, device, nullptr, 0, 1, out);
+}
+
+extern "C" int ec_tp_unique_id(void* out, size_t n) {
+  const char* why = nullptr;
+  const ec::NcclApi* api = ec::nccl_api(&why);
+  if (!api) return fail(EC_ERR_UNSUPPORTED, why);
+  if (!out || n < sizeof(ncclUniqueId)) return fail(EC_ERR_ARG, "id buffer smaller than 128 bytes");
+  ncclUniqueId id;
+  const ncclResult_t r = api->get_unique_id(&id);
+  if (r != ncclSuccess) return fail(EC_ERR_CUDA, api->error_string(r));
+  memcpy(out, &id, sizeof(id));
+  return EC_OK;
+}
+
+extern "C" int ec_create_tp(const ec_model_config* cfg, int device, int rank, int world,
+                            const void* id, ec_ctx** out) {
+  if (!cfg || !out || !id) return fail(EC_ERR_ARG, "null argument");
+  if (world < 1 || rank < 0 || rank >= world) return fail(EC_ERR_ARG, "bad rank or world size");
+  const ec_model_config& g = *cfg;
+  if (g.n_heads % world || g.n_kv_heads % world || g.hidden_dim % world || g.vocab_size % world ||
+      (g.hidden_dim / world) % 32)
+    return fail(EC_ERR_UNSUPPORTED, "heads, KV heads, hidden_dim and vocab_size must divide by the "
+                                    "number of ranks");
+  if (g.attention_mode != EC_ATTN_REFERENCE || g.tensor_min_batch > 0)
+    return fail(EC_ERR_UNSUPPORTED, "tensor parallelism runs the reference-order attention and "
+                                    "the exact GEMV chain");
+  const char* why = nullptr;
+  const ec::NcclApi* api = ec::nccl_api(&why);
+  if (!api) return fail(EC_ERR_UNSUPPORTED, why);
+  ec_model_config c = g;  // this rank's shard
+  c.n_heads = g.n_heads / world;
+  c.n_kv_heads = g.n_kv_heads / world;
+  c.hidden_dim = g.hidden_dim / world;
+  c.vocab_size = g.vocab_size / world;
+  ec_ctx* ctx = nullptr;
+  int rc = create_ctx(c, device, &g, rank, world, &ctx);
+  if (rc) return rc;
+  ncclUniqueId uid;
+  memcpy(&uid, id, sizeof(uid));
+  ncclComm_t comm = nullptr;
+  cudaSetDevice(device);
+  const ncclResult_t r = api->comm_init_rank(&comm, world, uid, rank);
+  if (r != ncclSuccess) {
+    ec_destroy(ctx);
+    return fail(EC_ERR_CUDA, api->error_string(r));
+  }
+  ctx->nccl = comm;
+  // one collective of each kind outside any stream capture: NCCL sets up its
+  // connections on first use, which a captured step must not do
+  ec::NcclApi const* a = api;
+  ncclResult_t w = a->all_gather(ctx->tp_part, ctx->tp_parts, (size_t)c.dim, ncclFloat32, comm,
+                                 ctx->stream);
+  if (w == ncclSuccess) w = a->broadcast(ctx->nsel, ctx->nsel, 1, ncclInt32, 0, comm, ctx->stream);
+  if (w != ncclSuccess || cudaStreamSynchronize(ctx->stream) != cudaSuccess) {
+    ec_destroy(ctx);
+    return fail(EC_ERR_CUDA, w != ncclSuccess ? a->error_string(w) : "NCCL warm-up failed");
+  }
+  *out = ctx;
+  return EC_OK;
 }
 
 extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data,
@@ -478,28 +583,44 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
   const cudaMemcpyKind skind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   const int D = c.dim, F = c.hidden_dim, hd = c.head_dim, H = c.n_heads, KV = c.n_kv_heads;
   const bool fp8 = c.weight_kind == EC_W_FP8;
+  // tensor parallelism: this rank takes rows [r0, r0 + n) of a column-split
+  // matrix (QKV, gate/up, LM head) or columns [c0, c0 + n) of a row-split one
+  // (o, down); per-row scales follow the rows
+  const int R = ctx->tp_rank;
+  const ec_model_config& g = ctx->cg;
   // FP8 per-tensor scale -> per-row scale vector (same value on every row)
-  auto put_scales = [&](float* dst, int rows, int stride) -> cudaError_t {
-    if (!scales) return cudaErrorInvalidValue;
-    if (!fp8) return cudaMemcpy2D(dst, stride * 4, scales, 4, 4, rows, skind);
+  auto put_scales_from = [&](float* dst, const float* src, int rows, int stride) -> cudaError_t {
+    if (!src) return cudaErrorInvalidValue;
+    if (!fp8) return cudaMemcpy2D(dst, stride * 4, src, 4, 4, rows, skind);
     float s = 0.0f;
-    cudaError_t e = cudaMemcpy(&s, scales, 4, on_device ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost);
+    cudaError_t e = cudaMemcpy(&s, src, 4, on_device ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost);
     if (e != cudaSuccess) return e;
     std::vector<float> v(rows, s);
     return cudaMemcpy2D(dst, stride * 4, v.data(), 4, 4, rows, cudaMemcpyHostToDevice);
   };
-  // nr row-major rows of m.cols bytes -> packed rows row_base + row_stride*i
-  auto put_rows = [&](Mat& m, const void* src, int nr, int row_base, int row_stride) -> cudaError_t {
+  // scales of local rows [0, rows) = global rows [row0, row0 + rows)
+  auto put_scales = [&](float* dst, int rows, int stride, long row0 = 0) -> cudaError_t {
+    if (!scales) return cudaErrorInvalidValue;
+    return put_scales_from(dst, fp8 ? scales : scales + row0, rows, stride);
+  };
+  // nr row-major rows of m.cols bytes -> packed rows row_base + row_stride*i;
+  // src_cols > m.cols: the rows of src are src_cols bytes long and this
+  // rank takes bytes [col0, col0 + m.cols) of each (a row-split shard)
+  auto put_rows = [&](Mat& m, const void* src, int nr, int row_base, int row_stride,
+                      int src_cols = 0, int col0 = 0) -> cudaError_t {
     const size_t bytes = (size_t)nr * m.cols;
     const uint8_t* d = static_cast<const uint8_t*>(src);
     void* tmp = nullptr;
     cudaError_t e2;
-    if (!on_device) {
+    if (!on_device || (src_cols && src_cols != m.cols)) {
       if ((e2 = cudaMalloc(&tmp, bytes)) != cudaSuccess) return e2;
       // same stream as the pack: a pageable cudaMemcpy may return before its
       // DMA has landed, and ctx->stream does not wait for the legacy stream
-      if ((e2 = cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, ctx->stream)) !=
-          cudaSuccess) {
+      if (src_cols && src_cols != m.cols)
+        e2 = cudaMemcpy2DAsync(tmp, m.cols, d + col0, src_cols, m.cols, nr, kind, ctx->stream);
+      else
+        e2 = cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, ctx->stream);
+      if (e2 != cudaSuccess) {
         cudaFree(tmp);
         return e2;
       }
@@ -516,17 +637,21 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
   if (layer < 0) {
     switch (which) {
       case EC_EMBEDDING:
-        e = cudaMemcpy(ctx->emb, data, (size_t)c.vocab_size * D * 2, kind);
+        e = cudaMemcpy(ctx->emb, data, (size_t)ctx->cg.vocab_size * D * 2, kind);
         break;
       case EC_FINAL_NORM:
         e = cudaMemcpy(ctx->final_norm, data, (size_t)D * 2, kind);
         break;
-      case EC_LM_HEAD:
-        e = put_rows(ctx->lm, data, c.vocab_size, 0, 1);
-        if (e == cudaSuccess) e = put_scales(ctx->lm.scale, c.vocab_size, 1);
+      case EC_LM_HEAD: {
+        const long r0 = (long)R * c.vocab_size;
+        e = put_rows(ctx->lm, static_cast<const uint8_t*>(data) + r0 * D, c.vocab_size, 0, 1);
+        if (e == cudaSuccess) e = put_scales(ctx->lm.scale, c.vocab_size, 1, r0);
         break;
+      }
       case EC_FINAL_ADAPTER:
       case EC_LOGIT_BIAS: {
+        if (ctx->tp_world > 1)
+          return fail(EC_ERR_UNSUPPORTED, "final adapter / logit bias with tensor parallelism");
         // optional tensors: kept only when not all zero (the reference's
         // zero-initialised adapter and bias change nothing)
         const bool ad = which == EC_FINAL_ADAPTER;
@@ -561,29 +686,32 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
     return EC_OK;
   }
   if (layer >= c.n_layers) return fail(EC_ERR_ARG, "layer out of range");
+  const uint8_t* src8 = static_cast<const uint8_t*>(data);
   switch (which) {
     case EC_WQ: case EC_WK: case EC_WV: {
       const int r0 = which == EC_WQ ? 0 : (which == EC_WK ? H * hd : (H + KV) * hd);
       const int nr = which == EC_WQ ? H * hd : KV * hd;
+      const long g0 = (long)R * nr;  // this rank's heads within the whole matrix
       Mat& m = ctx->qkv[layer];
-      e = put_rows(m, data, nr, r0, 1);
-      if (e == cudaSuccess) e = put_scales(m.scale + r0, nr, 1);
+      e = put_rows(m, src8 + g0 * D, nr, r0, 1);
+      if (e == cudaSuccess) e = put_scales(m.scale + r0, nr, 1, g0);
       break;
     }
     case EC_WO:
-      e = put_rows(ctx->wo[layer], data, D, 0, 1);
+      e = put_rows(ctx->wo[layer], data, D, 0, 1, g.n_heads * hd, R * H * hd);
       if (e == cudaSuccess) e = put_scales(ctx->wo[layer].scale, D, 1);
       break;
     case EC_W1: case EC_W3: {
       // interleave: row 2i = gate i, row 2i+1 = up i
       Mat& m = ctx->w13[layer];
       const int off = which == EC_W1 ? 0 : 1;
-      e = put_rows(m, data, F, off, 2);
-      if (e == cudaSuccess) e = put_scales(m.scale + off, F, 2);
+      const long g0 = (long)R * F;
+      e = put_rows(m, src8 + g0 * D, F, off, 2);
+      if (e == cudaSuccess) e = put_scales(m.scale + off, F, 2, g0);
       break;
     }
     case EC_W2:
-      e = put_rows(ctx->w2[layer], data, D, 0, 1);
+      e = put_rows(ctx->w2[layer], data, D, 0, 1, g.hidden_dim, R * F);
       if (e == cudaSuccess) e = put_scales(ctx->w2[layer].scale, D, 1);
       break;
     case EC_ATTN_NORM:
@@ -605,7 +733,7 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
 extern "C" int ec_set_weight_bf16(ec_ctx* ctx, int layer, int which, const uint16_t* data,
                                   int on_device) {
   if (!ctx || !data) return fail(EC_ERR_ARG, "null argument");
-  const ec_model_config& c = ctx->c;
+  const ec_model_config& c = ctx->cg;  // the whole matrix comes in (a shard is taken later)
   const int D = c.dim, F = c.hidden_dim, QD = c.n_heads * c.head_dim, KVD = c.n_kv_heads * c.head_dim;
   int rows = 0, cols = 0;
   if (layer < 0 && which == EC_LM_HEAD) {
@@ -1117,8 +1245,227 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
   return cudaSuccess;
 }
 
+// Tensor-parallel decode step (ec_create_tp): this rank holds heads, KV
+// heads, hidden rows and vocabulary rows [rank * n, (rank + 1) * n).  Per
+// sequence and layer:
+//   QKV (this rank's heads) -> RoPE + append (its KV heads) -> [layer 0:
+//   keys gathered, LSH update of KV head 0 on every rank] -> paged: the block
+//   selection of rank 0 (query head 0, KV head 0's centroids) broadcast |
+//   linear: queries gathered for the LSH query mean, per-head candidate dots
+//   gathered and added in head order, heap on every rank -> attention (its
+//   heads) -> o partial -> gather, x += partials in rank order -> gate/up
+//   (RMSNorm of the replicated x) + down partial -> gather, x += -> next QKV;
+//   after the last layer the LM head rows, gathered into the whole logits.
+// Every rank keeps identical x, selections and logits.  Collectives are
+// NCCL all-gathers / broadcasts on the context stream (captured in the
+// step graph); the sums over ranks run in rank order in the engine's own
+// kernels, so the result does not depend on NCCL's reduction order.
+cudaError_t enqueue_step_tp(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback) {
+  const ec_model_config& c = ctx->c;
+  const ec_model_config& g = ctx->cg;
+  const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
+  const int W = ctx->tp_world, Vg = g.vocab_size, L = c.n_layers;
+  const ec::NcclApi* api = ec::nccl_api(nullptr);
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->nccl);
+  cudaError_t e;
+  ctx->launches = 0;
+  auto gather = [&](const void* send, void* recv, size_t count) -> cudaError_t {
+    const ncclResult_t r = api->all_gather(send, recv, count, ncclFloat32, comm, ctx->stream);
+    if (r != ncclSuccess) {
+      ec_set_last_error(api->error_string(r));
+      return cudaErrorUnknown;
+    }
+    return cudaSuccess;
+  };
+  auto bcast = [&](void* buf, size_t count) -> cudaError_t {
+    const ncclResult_t r = api->broadcast(buf, buf, count, ncclInt32, 0, comm, ctx->stream);
+    if (r != ncclSuccess) {
+      ec_set_last_error(api->error_string(r));
+      return cudaErrorUnknown;
+    }
+    return cudaSuccess;
+  };
+  // one or more GEMV phases: the chain kernel, or one launch per matrix
+  auto phases = [&](ec::ChainParams& P, int slot, const ec::PackedPlan* plans[],
+                    int kinds[]) -> cudaError_t {
+    if (ctx->chain) {
+      P.ctr = ctx->chain_ctr + (size_t)slot * ctx->npacks * (ec::kMaxChainPhases + 1);
+      P.err = ctx->err;
+      P.eps = c.norm_eps;
+      ProfScope ps(ctx, EC_K_GEMV_CHAIN, 0.0);
+      ctx->launches++;
+      return ec::chain_launch(c.weight_kind, P, ctx->n_sm, ctx->stream, true);
+    }
+    for (int i = 0; i < P.nph; i++) {
+      const ec::ChainPhase& ph = P.ph[i];
+      Mat m;
+      m.w = const_cast<uint8_t*>(ph.w);
+      m.scale = const_cast<float*>(ph.scale);
+      m.rows = ph.N;
+      m.cols = ph.K;
+      cudaError_t e2 = gemv(ctx, kinds[i], m, *plans[i], ph.pro, ph.epi, ph.x, ph.norm_w, ph.y);
+      if (e2) return e2;
+    }
+    return cudaSuccess;
+  };
+  ec::StepBuffers sb{};
+  sb.rope_cos = ctx->rope_cos;
+  sb.rope_sin = ctx->rope_sin;
+  sb.sparse_k = c.sparse_k;
+  sb.window = c.window;
+  sb.sparse_blocks_k = c.sparse_blocks_k;
+  sb.err = ctx->err;
+  sb.max_sel = ctx->max_sel;
+  for (int b = 0; b < B; b++) {
+    float* x = ctx->x + (size_t)b * D;
+    sb.pos = pos + b;
+    sb.qkv = ctx->qkvb + (size_t)b * (H + 2 * KV) * hd;
+    sb.qrot = ctx->qrot + (size_t)b * H * hd;
+    sb.att = ctx->att + (size_t)b * H * hd;
+    sb.sel = ctx->sel + (size_t)b * ctx->max_sel;
+    sb.selp = ctx->selp + (size_t)b * ctx->max_sel;
+    sb.nsel = ctx->nsel + b;
+    if (ctx->lcand) {
+      sb.lcand = ctx->lcand + (size_t)b * ctx->cap_c;
+      sb.lscore = ctx->lscore + (size_t)b * ctx->cap_c;
+      sb.lnc = ctx->lnc + b;
+    }
+    ec::KvLayout kv = ctx->kv;
+    ec::LshLayout lsh = ctx->lsh;
+    const size_t per = (size_t)kv.n_layers * kv.max_blocks;
+    if (kv.paged) {
+      kv.kq += b * per * KV * 16 * hd;
+      kv.vq += b * per * KV * 16 * hd;
+      kv.ks += b * per * KV * 16;
+      kv.vs += b * per * KV * 16;
+      kv.centroid += b * per * hd;
+      kv.page_table += b * per;
+    } else {
+      kv.lk += (size_t)b * kv.n_layers * kv.seq_len * KV * hd;
+      kv.lv += (size_t)b * kv.n_layers * kv.seq_len * KV * hd;
+    }
+    if (lsh.tables > 0) {
+      lsh.acc += (size_t)b * hd;
+      lsh.meta += b * 4;
+      lsh.unit_hash += (size_t)b * lsh.tables * lsh.max_units;
+      lsh.unit_start += (size_t)b * lsh.max_units;
+      lsh.unit_len += (size_t)b * lsh.max_units;
+      lsh.heads += ((size_t)b * lsh.tables) << lsh.bits;
+      lsh.next += (size_t)b * lsh.tables * lsh.max_units;
+      lsh.counters += b * 2;
+    }
+    ec::LshLayout no_lsh = lsh;  // the append leaves the LSH update to the gathered keys
+    no_lsh.tables = 0;
+    if ((e = ec::launch_embed(ctx->emb, tokens + b, x, D, Vg, 1, ctx->stream, true))) return e;
+    ctx->launches++;
+    float* hb = ctx->hbuf + (size_t)b * F;
+    int kinds[2];
+    const ec::PackedPlan* plans[2];
+    for (int l = 0; l < L; l++) {
+      if (l == 0) {
+        ec::ChainParams P{};
+        P.ph[0] = chain_phase(ctx->qkv[0], ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->attn_norm[0],
+                              sb.qkv);
+        P.nph = 1;
+        kinds[0] = EC_K_GEMV_QKV;
+        plans[0] = &ctx->p_qkv;
+        if ((e = phases(P, L, plans, kinds))) return e;
+      }
+      {
+        ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
+        if ((e = ec::launch_kv_append(kv, no_lsh, sb, l, 1, ctx->stream, true))) return e;
+        ctx->launches++;
+      }
+      if (l == 0 && lsh.tables > 0) {
+        // lsh_update of KV head 0 (rank 0's first head) on every rank
+        if ((e = gather(sb.qkv + H * hd, ctx->tp_k, (size_t)KV * hd))) return e;
+        if ((e = ec::launch_lsh_update_key(lsh, sb, ctx->tp_k, hd, ctx->stream))) return e;
+        ctx->launches++;
+      }
+      if (kv.paged) {
+        // rank 0 scored the blocks with query head 0 and KV head 0's centroids
+        if ((e = bcast(sb.sel, (size_t)ctx->max_sel))) return e;
+        if ((e = bcast(sb.nsel, 1))) return e;
+      } else {
+        ProfScope ps(ctx, EC_K_SELECT, 0.0);
+        if ((e = gather(sb.qrot, ctx->tp_q, (size_t)H * hd))) return e;
+        ec::StepBuffers s2 = sb;
+        s2.q_all = ctx->tp_q;
+        s2.h_all = g.n_heads;
+        s2.score_parts = ctx->tp_sp;
+        if ((e = ec::launch_linear_candidates(kv, lsh, s2, l, 1, ctx->stream))) return e;
+        if ((e = ec::launch_linear_score_parts(kv, lsh, s2, l, 1, ctx->stream))) return e;
+        if ((e = gather(ctx->tp_sp, ctx->tp_sps, (size_t)ctx->cap_c * KV))) return e;
+        if ((e = ec::launch_linear_sum_heap(lsh, sb, ctx->tp_sps, W, KV, 1, ctx->stream))) return e;
+        ctx->launches += 4;
+      }
+      {
+        ProfScope ps(ctx, EC_K_ATTENTION, 0.0);
+        if ((e = ec::launch_attention(kv, sb, l, 1, ctx->stream, false))) return e;
+        ctx->launches++;
+      }
+      {
+        // o: this rank's head columns, then the sum over ranks
+        ec::ChainParams P{};
+        P.ph[0] = chain_phase(ctx->wo[l], ec::PRO_NONE, ec::EPI_STORE, sb.att, nullptr, ctx->tp_part);
+        P.nph = 1;
+        kinds[0] = EC_K_GEMV_O;
+        plans[0] = &ctx->p_o;
+        if ((e = phases(P, l, plans, kinds))) return e;
+        if ((e = gather(ctx->tp_part, ctx->tp_parts, (size_t)D))) return e;
+        if ((e = ec::launch_tp_resid(x, ctx->tp_parts, W, D, ctx->stream))) return e;
+        ctx->launches++;
+      }
+      {
+        // gate/up (its hidden rows) + down (its hidden columns), then the sum
+        ec::ChainParams P{};
+        P.ph[0] = chain_phase(ctx->w13[l], ec::PRO_RMSNORM, ec::EPI_SWIGLU, x, ctx->ffn_norm[l], hb);
+        P.ph[1] = chain_phase(ctx->w2[l], ec::PRO_NONE, ec::EPI_STORE, hb, nullptr, ctx->tp_part);
+        P.nph = 2;
+        kinds[0] = EC_K_GEMV_GATEUP;
+        kinds[1] = EC_K_GEMV_DOWN;
+        plans[0] = &ctx->p_w13;
+        plans[1] = &ctx->p_w2;
+        if ((e = phases(P, l, plans, kinds))) return e;
+        if ((e = gather(ctx->tp_part, ctx->tp_parts, (size_t)D))) return e;
+        if ((e = ec::launch_tp_resid(x, ctx->tp_parts, W, D, ctx->stream))) return e;
+        ctx->launches++;
+      }
+      {
+        ec::ChainParams P{};
+        if (l + 1 < L) {
+          P.ph[0] = chain_phase(ctx->qkv[l + 1], ec::PRO_RMSNORM, ec::EPI_STORE, x,
+                                ctx->attn_norm[l + 1], sb.qkv);
+          kinds[0] = EC_K_GEMV_QKV;
+          plans[0] = &ctx->p_qkv;
+        } else {
+          P.ph[0] = chain_phase(ctx->lm, ec::PRO_RMSNORM, ec::EPI_STORE, x, ctx->final_norm,
+                                ctx->tp_lg);
+          kinds[0] = EC_K_GEMV_LM;
+          plans[0] = &ctx->p_lm;
+        }
+        P.nph = 1;
+        if ((e = phases(P, l, plans, kinds))) return e;
+      }
+    }
+    float* lg = ctx->logits + (size_t)b * Vg;
+    if ((e = gather(ctx->tp_lg, lg, (size_t)c.vocab_size))) return e;
+    ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * Vg);
+    if ((e = ec::launch_argmax_split(lg, Vg, 1, ctx->argmax + b,
+                                     feedback ? const_cast<int*>(tokens) + b : nullptr,
+                                     feedback ? const_cast<int*>(pos) + b : nullptr,
+                                     static_cast<uint8_t*>(ctx->amax) +
+                                         (size_t)b * (ec::argmax_scratch_bytes(1)),
+                                     ctx->stream, false)))
+      return e;
+    ctx->launches++;
+  }
+  return cudaSuccess;
+}
+
 // Enqueue one decode step for B sequences (tokens/pos in device memory).
 cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback) {
+  if (ctx->tp_world > 1) return enqueue_step_tp(ctx, tokens, pos, B, feedback);
   if (ctx->tc && B >= ctx->c.tensor_min_batch)
     return enqueue_step_tc(ctx, tokens, pos, B, feedback);
   if (ctx->chain && B > 1) return enqueue_step_batched(ctx, tokens, pos, B, feedback);
@@ -1176,7 +1523,8 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
     }
     {
       ProfScope ps(ctx, EC_K_EMBED, 2.0 * D + 4.0 * D);
-      if ((e = ec::launch_embed(ctx->emb, tokens + b, x, D, c.vocab_size, 1, ctx->stream, true)))
+      if ((e = ec::launch_embed(ctx->emb, tokens + b, x, D, ctx->cg.vocab_size, 1, ctx->stream,
+                                true)))
         return e;
     }
     ctx->launches++;
@@ -1327,14 +1675,14 @@ extern "C" int ec_decode_step(ec_ctx* ctx, const int* tokens, const int* pos, in
   if (B <= 0 || B > ctx->c.max_batch) return fail(EC_ERR_ARG, "B out of range");
   cudaSetDevice(ctx->device);
   for (int b = 0; b < B; b++)
-    if (tokens[b] < 0 || tokens[b] >= ctx->c.vocab_size || pos[b] < 0)
+    if (tokens[b] < 0 || tokens[b] >= ctx->cg.vocab_size || pos[b] < 0)
       return fail(EC_ERR_ARG, "token or position out of range");
   EC_CUDA_TRY(cudaMemcpyAsync(ctx->tokens, tokens, B * 4, cudaMemcpyHostToDevice, ctx->stream));
   EC_CUDA_TRY(cudaMemcpyAsync(ctx->pos, pos, B * 4, cudaMemcpyHostToDevice, ctx->stream));
   int rc = run_step(ctx, ctx->tokens, ctx->pos, B, 0);
   if (rc) return rc;
   if (logits_host)
-    EC_CUDA_TRY(cudaMemcpyAsync(logits_host, ctx->logits, (size_t)B * ctx->c.vocab_size * 4,
+    EC_CUDA_TRY(cudaMemcpyAsync(logits_host, ctx->logits, (size_t)B * ctx->cg.vocab_size * 4,
                                 cudaMemcpyDeviceToHost, ctx->stream));
   if (argmax_host)
     EC_CUDA_TRY(cudaMemcpyAsync(argmax_host, ctx->argmax, B * 4, cudaMemcpyDeviceToHost, ctx->stream));
@@ -1349,8 +1697,8 @@ extern "C" int ec_prefill(ec_ctx* ctx, int seq, const int* tokens, int n, int po
   const ec_model_config& c = ctx->c;
   if (seq < 0 || seq >= c.max_batch) return fail(EC_ERR_ARG, "bad sequence");
   if (pos0 < 0 || (long)pos0 + n > c.seq_len) return fail(EC_ERR_ARG, "positions past seq_len");
-  if (!ctx->kv.paged || !ctx->chain)
-    return fail(EC_ERR_UNSUPPORTED, "prefill needs paged KV and the chain GEMV layout");
+  if (!ctx->kv.paged || !ctx->chain || ctx->tp_world > 1)
+    return fail(EC_ERR_UNSUPPORTED, "prefill needs paged KV and the chain GEMV layout (one rank)");
   for (int i = 0; i < n; i++)
     if (tokens[i] < 0 || tokens[i] >= c.vocab_size) return fail(EC_ERR_ARG, "token out of range");
   cudaSetDevice(ctx->device);
@@ -1422,6 +1770,15 @@ extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
   // down -- or with the chain: append, [select], attention, chain -- then
   // [LM head] and argmax
   const int sel = ctx->kv.paged ? 0 : ec::kLinearSelectLaunches;
+  if (ctx->tp_world > 1) {
+    // per sequence: embed, QKV(0), per layer append, [LSH update on layer 0],
+    // [linear: candidates, dots, sum, heap], attention, o, sum, gate/up+down
+    // (one chain, else two), sum, next QKV or LM head; argmax.  NCCL's own
+    // kernels are not counted.
+    const int ffn = ctx->chain ? 1 : 2;
+    const int lsh0 = ctx->lsh.tables > 0 ? 1 : 0;
+    return B * (3 + lsh0 + ctx->c.n_layers * ((ctx->kv.paged ? 0 : 4) + 6 + ffn));
+  }
   // a registered final adapter / logit bias: final RMSNorm, [adapter], the
   // LM head on its own, [bias]
   const bool extras = ctx->adapter_on || ctx->bias_on;
@@ -1459,7 +1816,7 @@ extern "C" int ec_read_state(ec_ctx* ctx, int which, int seq, float* out, size_t
             cnt = (size_t)c.n_kv_heads * c.head_dim; break;
     case 5: src = ctx->att + (size_t)seq * c.n_heads * c.head_dim;
             cnt = (size_t)c.n_heads * c.head_dim; break;
-    case 6: src = ctx->logits + (size_t)seq * c.vocab_size; cnt = c.vocab_size; break;
+    case 6: src = ctx->logits + (size_t)seq * ctx->cg.vocab_size; cnt = ctx->cg.vocab_size; break;
     case 7: src = ctx->hbuf + (size_t)seq * c.hidden_dim; cnt = c.hidden_dim; break;
     case 8: {
       // attended selection of the last attention launch: [n, ids...] as floats

@@ -35,6 +35,7 @@ EXPORTS = [
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read", "ec_lsh_attn_create",
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
     "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill", "ec_set_weight_bf16",
+    "ec_tp_unique_id", "ec_create_tp",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
@@ -81,6 +82,8 @@ def lib():
             "ec_last_error": (C.c_char_p, []),
             "ec_config_default": (i, [C.POINTER(ModelConfig)]),
             "ec_create": (i, [C.POINTER(ModelConfig), i, C.POINTER(vp)]),
+            "ec_tp_unique_id": (i, [vp, C.c_size_t]),
+            "ec_create_tp": (i, [C.POINTER(ModelConfig), i, i, i, vp, C.POINTER(vp)]),
             "ec_destroy": (None, [vp]),
             "ec_set_weight": (i, [vp, i, i, vp, vp, i]),
             "ec_set_weight_bf16": (i, [vp, i, i, vp, i]),
@@ -168,14 +171,29 @@ def _ptr(a):
     return C.c_void_p(a.ctypes.data) if a is not None else None
 
 
-class Engine:
-    """One decode context (ec_ctx) on one device."""
+def tp_unique_id():
+    """128 bytes naming a new tensor-parallel group (ec_tp_unique_id); one
+    rank creates it, every rank passes the same bytes to Engine(tp=...)."""
+    buf = C.create_string_buffer(128)
+    check(lib().ec_tp_unique_id(buf, 128))
+    return buf.raw
 
-    def __init__(self, cfg, device=0, **kw):
+
+class Engine:
+    """One decode context (ec_ctx) on one device.  tp=(rank, world, id):
+    this rank of a tensor-parallel group (ec_create_tp)."""
+
+    def __init__(self, cfg, device=0, tp=None, **kw):
         self.model_cfg = cfg
         self.c = config_from(cfg, **kw)
         self.h = C.c_void_p()
-        check(lib().ec_create(C.byref(self.c), device, C.byref(self.h)))
+        if tp is None:
+            check(lib().ec_create(C.byref(self.c), device, C.byref(self.h)))
+        else:
+            rank, world, uid = tp
+            self._uid = C.create_string_buffer(bytes(uid), 128)
+            check(lib().ec_create_tp(C.byref(self.c), device, rank, world, self._uid,
+                                     C.byref(self.h)))
 
     def load(self, model):
         """Register a synth.Model (host numpy arrays)."""

@@ -51,6 +51,8 @@ def _load(name):
 METRIC = "decode tok/s (Llama-3-8B-shaped INT8, b=1 per GPU, 2k context)"
 METRIC_B = "decode tok/s (Llama-3-8B-shaped INT8, b={} per GPU, 2k context)"
 METRIC_70B = "decode tok/s (70B-shaped FP8 per-tensor, b={} per GPU, {} context, LSH top-{})"
+METRIC_70B_TP = ("decode tok/s (70B-shaped FP8 per-tensor, b={}, tensor-parallel over {} GPUs, {} "
+                 "context, LSH top-{})")
 PROMPT = 2048
 # --attention: the paged decode attention (engine_cuda.h attention_mode)
 ATTN_MODES = {"reference": 0, "split": 1}
@@ -234,14 +236,16 @@ def run_reference(args):
     emit(line)
 
 
-def config_block(args, ws, big, B, tmb=0):
+def config_block(args, ws, big, B, tmb=0, tp=False):
     """The `config` object both arms print for the same workload."""
-    return {"workload": f"{'70b' if big else 'llama3-8b'}-shape decode b={B} per GPU",
-            "global_batch": ws * B, "context": args.prompt,
+    return {"workload": f"{'70b' if big else 'llama3-8b'}-shape decode b={B}"
+                        + (f" tensor-parallel over {ws} GPUs" if tp else " per GPU"),
+            "global_batch": B if tp else ws * B, "context": args.prompt,
             "weights": "fp8 e4m3 per-tensor pow2 scale" if big else "int8 per-row pow2 scale",
             "kv": f"linear bf16, LSH top-{args.sparse_k}" if big else "paged int8",
             "attention": "reference order" if big else args.attention,
-            "parallelism": f"dp{ws} (replicas)",
+            "parallelism": f"tp{ws} (NCCL all-gathers, rank-order sums)" if tp
+                           else f"dp{ws} (replicas)",
             "gemm": "tcgen05 int8 (digit planes)" if (not big and tmb) else "cuda-core gemv chain",
             "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"}
 
@@ -309,11 +313,20 @@ def run_cuda(args):
     big = args.model == "70b"
     dpb = 0 if (big or args.dp_batch <= B) else args.dp_batch  # the b=64-per-GPU record
     tmb = 0
+    tp = None
+    if big and args.tp and ws > 1:
+        # config 5 tensor-parallel: every rank holds 1/N of the heads, FFN and
+        # vocabulary rows and decodes the same sequences (ec_create_tp)
+        import torch.distributed as dist
+        box = [eng.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        tp = (rank, ws, box[0])
     if big:
-        # BASELINE config 5 on one GPU: FP8 E4M3 per-tensor weights (~70 GB),
-        # linear BF16 KV with the reference's LSH-routed top-K attention
+        # FP8 E4M3 per-tensor weights (~70 GB), linear BF16
+        # KV with the reference's LSH-routed top-K attention; one GPU, or split
+        # tensor-parallel over the ranks with --tp
         cfg = S.LLAMA_70B
-        e = eng.Engine(cfg, device=local, max_batch=B, weight_kind=eng.EC_W_FP8,
+        e = eng.Engine(cfg, device=local, tp=tp, max_batch=B, weight_kind=eng.EC_W_FP8,
                        use_paged_kv=False, sparse_k=args.sparse_k)
         src = S.DeviceModel(cfg, seed=SEED, device=local, kind="fp8")
     else:
@@ -341,7 +354,9 @@ def run_cuda(args):
     # prompt: random tokens through the decode path (KV cache filled), every
     # sequence its own prompt, all sequences of the engine decoded together
     nseq = max(B, dpb)
-    prompts = [S.prompt(cfg, args.prompt, seed=7 + rank * 1000 + b) for b in range(nseq)]
+    # tensor parallelism: every rank decodes the same sequences
+    prank = 0 if tp else rank
+    prompts = [S.prompt(cfg, args.prompt, seed=7 + prank * 1000 + b) for b in range(nseq)]
     for p in range(args.prompt):
         _, am = e.step([int(pr[p]) for pr in prompts], [p] * nseq, want_logits=False)
     dev = f"cuda:{local}"
@@ -351,7 +366,9 @@ def run_cuda(args):
     tok, pos = tok_all[:B].clone(), pos_all[:B].clone()
     with Clocks(local) as clk:
         ms = timed_steps(e, torch, stream, tok, pos, B, args.steps, args.warmup, local)
-    value = dp.job_throughput(B, ws, ms)
+    # data parallel: every rank its own sequences; tensor parallel: the same B
+    seq_ranks = 1 if tp else ws
+    value = dp.job_throughput(B, seq_ranks, ms)
     e2e_ms, cur_tok, cur_pos = e2e_steps(e, [int(v) for v in tok.cpu()],
                                          [int(v) for v in pos.cpu()], args.steps, local)
 
@@ -394,6 +411,8 @@ def run_cuda(args):
     tot_ms = sum(v["ms"] for v in prof.values())
     weight_bytes = (sum(int(np.prod(s)) for s in S.mat_shapes(cfg).values()) * cfg.n_layers
                     + cfg.vocab_size * cfg.dim)
+    if tp:
+        weight_bytes //= ws  # this rank's shard
     if big:
         # linear BF16 K and V of the attended top-K tokens (candidate scoring
         # reads more K rows; not counted)
@@ -422,15 +441,16 @@ def run_cuda(args):
 
     if rank == 0:
         line = {
-            "metric": (METRIC_70B.format(B, args.prompt, args.sparse_k) if big else
+            "metric": (METRIC_70B_TP.format(B, ws, args.prompt, args.sparse_k) if tp else
+                       METRIC_70B.format(B, args.prompt, args.sparse_k) if big else
                        METRIC if B == 1 else METRIC_B.format(B)), "value": round(value, 3),
             "unit": "tok/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "fp8" if big else "int8",
             "data": "synthetic",
-            "config": config_block(args, ws, big, B, tmb if (tmb and B >= tmb) else 0),
-            "e2e": {"value": round(ws * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
+            "config": config_block(args, ws, big, B, tmb if (tmb and B >= tmb) else 0, tp=bool(tp)),
+            "e2e": {"value": round(seq_ranks * B * 1000.0 / e2e_ms, 3), "unit": "tok/s",
                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B * (cfg.vocab_size + 1)},
             "gpu_launches": launches_b * args.steps,
             "roofline": {"bound": "hbm", "kernel": dom,
@@ -497,6 +517,8 @@ def main():
     ap.add_argument("--model", default="8b", choices=["8b", "70b"],
                     help="8b: the headline INT8 config; 70b: FP8 config 5 on one GPU")
     ap.add_argument("--sparse-k", type=int, default=511, help="70b: LSH top-K (engine max 511)")
+    ap.add_argument("--tp", action="store_true",
+                    help="70b under torchrun: tensor-parallel over the ranks (else replicas)")
     ap.add_argument("--tensor-min-batch", type=int, default=16,
                     help="batches this large run their GEMMs on the tensor cores (0: never)")
     ap.add_argument("--dp-batch", type=int, default=64,

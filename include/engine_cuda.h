@@ -126,6 +126,29 @@ int		ec_config_default(ec_model_config *c);
 int		ec_create(const ec_model_config *c, int device, ec_ctx **out);
 void	ec_destroy(ec_ctx *ctx);
 
+/* Tensor parallelism over `world` GPUs (one process or thread per GPU, one
+** context each): rank r holds query heads, KV heads, hidden (FFN) rows and
+** vocabulary rows [r * n, (r + 1) * n) of the model `c` describes (each
+** count must divide by world).  QKV, gate/up and the LM head are split by
+** rows, o and down by columns; ec_set_weight still takes the WHOLE tensor
+** and keeps this rank's shard.  Row-split projections are all-gathered and
+** added in rank order, the reference's cross-head quantities (the LSH
+** query mean over all heads, candidate scores summed over KV heads,
+** inference.c:290-353; the paged block selection from query head 0 and KV
+** head 0, paged.c:401-495; the layer-0 LSH key) are exchanged so that every
+** rank holds the same activations, selections and whole logits.  Not
+** bit-identical to one GPU (the row-split sums are regrouped by rank):
+** within 2e-2 of the logit range, equal greedy tokens in the tests.
+** Collectives are NCCL (libnccl.so.2, loaded on first use) on the context
+** stream.  `id` holds 128 bytes from ec_tp_unique_id on one rank, shared
+** with the others by the caller; every rank calls ec_create_tp with the
+** same id (it blocks until all have).  Reference-order attention and the
+** exact GEMV chain only (attention_mode EC_ATTN_REFERENCE,
+** tensor_min_batch 0); no prefill, adapter or logit bias. */
+int		ec_tp_unique_id(void *out, size_t n);
+int		ec_create_tp(const ec_model_config *c, int device, int rank, int world,
+			const void *id, ec_ctx **out);
+
 /* Register one tensor (model.c:167-265 weight mapping).  `data` is a host
 ** pointer unless `on_device` is nonzero.  Matrices are row-major
 ** [out_features][in_features] in the context's weight_kind; `scales` holds
