@@ -1691,8 +1691,13 @@ extern "C" int ec_decode_step(ec_ctx* ctx, const int* tokens, const int* pos, in
   return check_err(ctx);
 }
 
-extern "C" int ec_prefill(ec_ctx* ctx, int seq, const int* tokens, int n, int pos0,
-                          float* logits_host, int* argmax_host) {
+namespace {
+
+// The rows of ec_prefill / ec_verify: n tokens of sequence seq from pos0, in
+// chunks of max_batch rows; the greedy token of every row to argmax_all when
+// given, the last row's logits / greedy token to the two others.
+int prefill_rows(ec_ctx* ctx, int seq, const int* tokens, int n, int pos0, float* logits_host,
+                 int* argmax_host, int* argmax_all) {
   if (!ctx || !tokens || n <= 0) return fail(EC_ERR_ARG, "null argument or n <= 0");
   const ec_model_config& c = ctx->c;
   if (seq < 0 || seq >= c.max_batch) return fail(EC_ERR_ARG, "bad sequence");
@@ -1712,6 +1717,9 @@ extern "C" int ec_prefill(ec_ctx* ctx, int seq, const int* tokens, int n, int po
     EC_CUDA_TRY(cudaMemcpyAsync(ctx->pos, pos.data(), C * 4, cudaMemcpyHostToDevice, ctx->stream));
     cudaError_t e = enqueue_step_batched(ctx, ctx->tokens, ctx->pos, C, false, seq, pos0 + c0);
     if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+    if (argmax_all)
+      EC_CUDA_TRY(cudaMemcpyAsync(argmax_all + c0, ctx->argmax, C * 4, cudaMemcpyDeviceToHost,
+                                  ctx->stream));
     // the host vectors above are read before the next chunk overwrites them
     EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     last_rows = C;
@@ -1725,6 +1733,19 @@ extern "C" int ec_prefill(ec_ctx* ctx, int seq, const int* tokens, int n, int po
   EC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   if (ctx->prof) prof_collect(ctx);
   return check_err(ctx);
+}
+
+}  // namespace
+
+extern "C" int ec_prefill(ec_ctx* ctx, int seq, const int* tokens, int n, int pos0,
+                          float* logits_host, int* argmax_host) {
+  return prefill_rows(ctx, seq, tokens, n, pos0, logits_host, argmax_host, nullptr);
+}
+
+extern "C" int ec_verify(ec_ctx* ctx, int seq, const int* tokens, int n, int pos0,
+                         int* greedy_out) {
+  if (!greedy_out) return fail(EC_ERR_ARG, "null argument");
+  return prefill_rows(ctx, seq, tokens, n, pos0, nullptr, nullptr, greedy_out);
 }
 
 extern "C" float* ec_logits_device(ec_ctx* ctx) { return ctx ? ctx->logits : nullptr; }

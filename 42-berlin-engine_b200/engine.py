@@ -35,7 +35,7 @@ EXPORTS = [
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read", "ec_lsh_attn_create",
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
     "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill", "ec_set_weight_bf16",
-    "ec_tp_unique_id", "ec_create_tp",
+    "ec_tp_unique_id", "ec_create_tp", "ec_verify",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
@@ -105,6 +105,7 @@ def lib():
             "ec_gemm_tc_pack": (i, [vp, vp, i, i, vp]),
             "ec_op_gemm_tc": (i, [vp, vp, vp, vp, i, i, i, vp]),
             "ec_prefill": (i, [vp, i, vp, i, i, vp, vp]),
+            "ec_verify": (i, [vp, i, vp, i, i, vp]),
             "ec_op_gemv_packed": (i, [i, vp, vp, vp, vp, i, i, vp]),
             "ec_op_gemv_packed_batch": (i, [i, vp, vp, vp, vp, i, i, i, vp]),
             "ec_op_rmsnorm": (i, [vp, vp, vp, i, f, vp]),
@@ -296,6 +297,13 @@ class Engine:
                                _ptr(am)))
         return lg, int(am[0])
 
+    def verify(self, seq, tokens, pos0):
+        """Greedy token after each of `tokens` (ec_verify)."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(tokens.size, np.int32)
+        check(lib().ec_verify(self.h, int(seq), _ptr(tokens), tokens.size, int(pos0), _ptr(out)))
+        return out
+
     def step_device(self, tokens_ptr, pos_ptr, B, feedback=True):
         check(lib().ec_decode_step_device(self.h, C.c_void_p(tokens_ptr), C.c_void_p(pos_ptr),
                                           B, int(feedback)))
@@ -319,6 +327,29 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+def speculate(target, draft, token, pos, n_draft, seq=0):
+    """One burst of mtp_generate (speculate.c:93-258) with two engines of one
+    vocabulary: the draft decodes n_draft greedy tokens from `token` at
+    `pos`, the target verifies them in one ec_verify pass; returns the
+    target's tokens for the accepted prefix plus its correction (at most
+    n_draft tokens), exactly the greedy tokens the target alone would give.
+    Both engines' caches stay valid for the returned tokens (positions past
+    them are overwritten by the next steps)."""
+    drafts, cur = [], int(token)
+    for i in range(n_draft):
+        _, am = draft.step([cur], [pos + i], want_logits=False)
+        cur = int(am[0])
+        drafts.append(cur)
+    checks = [int(token)] + drafts[:-1]
+    pred = target.verify(seq, checks, pos)
+    out = []
+    for i in range(n_draft):
+        out.append(int(pred[i]))
+        if int(pred[i]) != drafts[i]:
+            break
+    return out
 
 
 class HostTransformer:

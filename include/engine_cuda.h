@@ -273,6 +273,18 @@ int		ec_op_gemv_packed(int wkind, const void *w_packed, const float *scale,
 int		ec_prefill(ec_ctx *ctx, int seq, const int *tokens, int n, int pos0,
 			float *logits_host, int *argmax_host);
 
+/* Speculative decoding's verification (mtp_generate, speculate.c:187-258):
+** the target model runs draft tokens tokens[0..n) of sequence `seq` at
+** positions pos0.. as the rows of batched steps (the ec_prefill path) and
+** writes the greedy token after every row to greedy_out[0..n) -- the
+** prediction the reference's token-by-token verification loop compares
+** with draft token i + 1, bit-identical to n decode steps.  The caller keeps
+** the accepted prefix and continues from the first mismatch; positions past
+** it need no rewind (kv_cache_rewind, speculate.c:66, is a no-op: the next
+** steps overwrite them).  Paged KV, one rank. */
+int		ec_verify(ec_ctx *ctx, int seq, const int *tokens, int n, int pos0,
+			int *greedy_out);
+
 /* op_matmul (src/compute/ops.h:33) for nb activation rows at once on the
 ** tensor cores, INT8 weights only (the large-batch decode and prefill path;
 ** the reference runs op_matmul once per row).  ec_gemm_tc_bytes gives the
