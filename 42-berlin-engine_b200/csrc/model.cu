@@ -215,13 +215,16 @@ extern "C" int ec_config_default(ec_model_config* c) {
 extern "C" void ec_destroy(ec_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  // the captured step holds NCCL work: release it before the communicator
+  if (ctx->gexec) cudaGraphExecDestroy(ctx->gexec);
+  ctx->gexec = nullptr;
   if (ctx->nccl) {
-    cudaStreamSynchronize(ctx->stream);
+    cudaDeviceSynchronize();
     if (const ec::NcclApi* api = ec::nccl_api(nullptr))
       api->comm_destroy(static_cast<ncclComm_t>(ctx->nccl));
     ctx->nccl = nullptr;
   }
-  if (ctx->gexec) cudaGraphExecDestroy(ctx->gexec);
   cudaStreamSynchronize(ctx->stream);
   for (auto& r : ctx->recs) {
     cudaEventDestroy(r.a);

@@ -44,8 +44,8 @@ def _worker(rank, world, uid, kind, paged, n_prompt, n_greedy, out_q):
         fed.append(tok)
         logits.append(lg[0].copy())
         tok = toks[p + 1] if p + 1 < n_prompt else int(am[0])
-    e.close()
     out_q.put((rank, fed, np.stack(logits)))
+    e.close()
 
 
 @pytest.mark.parametrize("kind,paged", [("int8", True), ("fp8", False)])
@@ -65,11 +65,16 @@ def test_tp2_matches_restatement(oracle, synth, kind, paged):
     for p in procs:
         p.start()
     res = {}
-    for _ in range(2):
-        r, fed, lgs = q.get(timeout=600)
-        res[r] = (fed, lgs)
+    try:
+        for _ in range(2):
+            r, fed, lgs = q.get(timeout=300)
+            res[r] = (fed, lgs)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.exitcode is None:
+                p.kill()
     for p in procs:
-        p.join(timeout=60)
         assert p.exitcode == 0
     fed0, lg0 = res[0]
     fed1, lg1 = res[1]
