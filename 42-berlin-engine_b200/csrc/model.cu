@@ -1295,7 +1295,10 @@ cudaError_t enqueue_step_tp(ec_ctx* ctx, const int* tokens, const int* pos, int 
       P.ctr = ctx->chain_ctr + (size_t)slot * ctx->npacks * (ec::kMaxChainPhases + 1);
       P.err = ctx->err;
       P.eps = c.norm_eps;
-      ProfScope ps(ctx, EC_K_GEMV_CHAIN, 0.0);
+      double by = 0.0;  // weights, row scales and vectors of the phases
+      for (int i = 0; i < P.nph; i++)
+        by += (double)P.ph[i].N * P.ph[i].K + 8.0 * P.ph[i].N + 4.0 * P.ph[i].K;
+      ProfScope ps(ctx, EC_K_GEMV_CHAIN, by);
       ctx->launches++;
       return ec::chain_launch(c.weight_kind, P, ctx->n_sm, ctx->stream, true);
     }

@@ -247,7 +247,8 @@ def config_block(args, ws, big, B, tmb=0, tp=False):
             "parallelism": f"tp{ws} (NCCL all-gathers, rank-order sums)" if tp
                            else f"dp{ws} (replicas)",
             "gemm": "tcgen05 int8 (digit planes)" if (not big and tmb) else "cuda-core gemv chain",
-            "l2": "inputs larger than L2 (7.5 GB weights streamed per step)"}
+            "l2": "inputs larger than L2 ({} GB of weights streamed per step{})".format(
+                "69.5" if big else "7.5", f" over {ws} GPUs" if tp else "")}
 
 
 class _HostWeights:
