@@ -1123,7 +1123,8 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
 // tc_quant (RMSNorm when the reference has one, digit planes) -> tc_gemm
 // (tcgen05, whole tiles finished in its epilogue) -> tc_combine (tiles split
 // between CTAs), per pass of up to kTcMaxRows sequences.
-cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback) {
+cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int B, bool feedback,
+                            int prefill_seq = -1, int prefill_pos0 = 0) {
   const ec_model_config& c = ctx->c;
   const int H = c.n_heads, KV = c.n_kv_heads, hd = c.head_dim, D = c.dim, F = c.hidden_dim;
   const int V = c.vocab_size, L = c.n_layers, QW = (H + 2 * KV) * hd;
@@ -1200,10 +1201,33 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
                   ctx->qkvb + (size_t)b0 * QW, QW, ec::EPI_STORE, nb)))
       return e;
   }
+  // prefill (ec_prefill): the B rows are consecutive tokens of one sequence,
+  // as in enqueue_step_batched
+  ec::KvLayout kv = ctx->kv;
+  if (prefill_seq >= 0) {
+    kv.seq_plus1 = prefill_seq + 1;
+    sb.defer_centroid = 1;
+  }
   for (int l = 0; l < L; l++) {
-    if ((e = enqueue_attention(ctx, ctx->kv, ctx->lsh, sb, l, B,
-                               ctx->fast && !ec::use_group_attention(ctx->kv, sb, B))))
-      return e;
+    if (prefill_seq < 0) {
+      if ((e = enqueue_attention(ctx, kv, ctx->lsh, sb, l, B,
+                                 ctx->fast && !ec::use_group_attention(kv, sb, B))))
+        return e;
+    } else {
+      {
+        ProfScope ps(ctx, EC_K_KV_APPEND, 0.0);
+        if ((e = ec::launch_kv_append(kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
+      }
+      // every row's token is in the cache: the chunk's block centroids, the
+      // layer-0 LSH update in row order, each row's block selection
+      ProfScope ps(ctx, EC_K_SELECT, 0.0);
+      if ((e = ec::launch_paged_centroids(kv, l, prefill_seq, prefill_pos0, B, ctx->stream)))
+        return e;
+      if (l == 0 && (e = ec::launch_lsh_update_rows(kv, ctx->lsh, sb, B, ctx->stream))) return e;
+      if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
+      if ((e = ec::launch_attention(kv, sb, l, B, ctx->stream, true))) return e;
+      ctx->launches += 4 + (l == 0 && ctx->lsh.tables > 0);
+    }
     const bool last = l + 1 == L;
     for (int b0 = 0; b0 < B; b0 += ec::kTcMaxRows) {
       const int nb = B - b0 < ec::kTcMaxRows ? B - b0 : ec::kTcMaxRows;
@@ -1721,7 +1745,11 @@ int prefill_rows(ec_ctx* ctx, int seq, const int* tokens, int n, int pos0, float
     for (int i = 0; i < C; i++) pos[i] = pos0 + c0 + i;
     EC_CUDA_TRY(cudaMemcpyAsync(ctx->tokens, tokens + c0, C * 4, cudaMemcpyHostToDevice, ctx->stream));
     EC_CUDA_TRY(cudaMemcpyAsync(ctx->pos, pos.data(), C * 4, cudaMemcpyHostToDevice, ctx->stream));
-    cudaError_t e = enqueue_step_batched(ctx, ctx->tokens, ctx->pos, C, false, seq, pos0 + c0);
+    // chunks of at least tensor_min_batch rows run their projections on the
+    // tensor cores (within tolerance), smaller ones on the exact chain
+    cudaError_t e = (ctx->tc && C >= c.tensor_min_batch)
+                        ? enqueue_step_tc(ctx, ctx->tokens, ctx->pos, C, false, seq, pos0 + c0)
+                        : enqueue_step_batched(ctx, ctx->tokens, ctx->pos, C, false, seq, pos0 + c0);
     if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
     if (argmax_all)
       EC_CUDA_TRY(cudaMemcpyAsync(argmax_all + c0, ctx->argmax, C * 4, cudaMemcpyDeviceToHost,

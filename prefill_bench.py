@@ -1,4 +1,5 @@
-"""Prompt prefill through ec_prefill against token-by-token decode.
+"""Prompt prefill through ec_prefill (exact chain, and tensor cores with
+tensor_min_batch 16) against token-by-token decode.
 
 Llama-3-8B shape, INT8, paged KV: a P-token random prompt for sequence 0 run
 (1) by ec_prefill with max_batch rows per weight pass (bit-identical to
@@ -44,11 +45,12 @@ def main():
     out = {"workload": "llama3-8b-shape int8 prompt prefill", "prompt": args.prompt,
            "rows_per_pass": args.rows}
     res = {}
-    for mode in ("prefill", "decode"):
-        e = eng.Engine(cfg, max_batch=args.rows if mode == "prefill" else 1)
+    for mode in ("prefill", "prefill_tc", "decode"):
+        rows = args.rows if mode != "decode" else 1
+        e = eng.Engine(cfg, max_batch=rows, tensor_min_batch=16 if mode == "prefill_tc" else 0)
         lb.load_device_model(eng, e, S.DeviceModel(cfg, seed=3, device=0))
         torch.cuda.synchronize()
-        if mode == "prefill":
+        if mode != "decode":
             e.prefill(0, prompt[:64])  # warm-up (kernels, allocator)
             e.reset(0)
             t0 = time.perf_counter()
@@ -70,6 +72,8 @@ def main():
         torch.cuda.empty_cache()
     out["last_logits_bit_identical"] = bool(
         np.array_equal(res["prefill"].view(np.uint32), res["decode"].view(np.uint32)))
+    d = res["decode"]
+    out["tc_max_diff_of_range"] = float(np.abs(res["prefill_tc"] - d).max() / (d.max() - d.min()))
     print(json.dumps(out), flush=True)
 
 

@@ -126,3 +126,31 @@ def test_tensor_core_decode_matches_oracle(eng, torch, oracle, synth, B, steps):
         toks = [int(prompts[b][t + 1]) if t + 1 < 8 else int(am[b]) for b in range(B)]
     e.close()
     print(f"worst |d| / range = {worst:.2e}")
+
+
+def test_tensor_core_prefill(eng, torch, oracle, synth):
+    """ec_prefill with tensor_min_batch: chunks of >= 16 rows run their
+    projections on the tensor cores (the last chunk of 7 rows on the exact
+    chain).  The prompt's last logits within 2e-2 of the range of the
+    restatement's, its greedy token equal, and decode steps after it still
+    within tolerance with equal greedy tokens."""
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4,
+                            vocab_size=4096, seq_len=512, head_dim=64, rope_theta=1e4)
+    model = synth.make_model(cfg, seed=37)
+    e = eng.Engine(cfg, max_batch=32, tensor_min_batch=16, sparse_blocks_k=4)
+    e.load(model)
+    pm = oracle.PortModel(model, sparse_blocks_k=4)
+    P = oracle.port()
+    prompt = [int(t) for t in synth.prompt(cfg, 135, seed=12)]
+    lg, tok = e.prefill(0, prompt)
+    for p, t in enumerate(prompt):
+        want = pm.forward(t, p)
+    assert np.abs(lg - want).max() <= 2e-2 * (want.max() - want.min())
+    assert tok == P.port_argmax(want, want.size)
+    for p in range(135, 160):
+        lgs, am = e.step([tok], [p])
+        want = pm.forward(tok, p)
+        assert np.abs(lgs[0] - want).max() <= 2e-2 * (want.max() - want.min()), f"step {p}"
+        assert int(am[0]) == P.port_argmax(want, want.size), f"step {p}"
+        tok = int(am[0])
+    e.close()
