@@ -639,7 +639,9 @@ __global__ void __launch_bounds__(kAttnThreads, VF ? 1 : 3)
     const int kv_len = min(pos + 1, kv.seq_len);
     const int ns = sb.nsel[b];
     const int* sel = sb.sel + (long)b * sb.max_sel;
-    const bool sparse = ns > 0 && ns < kv_len;
+    // list_dense: the list is explicit even when it covers every position
+    // (rows of a paged cache, isolated LSH attention)
+    const bool sparse = ns > 0 && (ns < kv_len || sb.list_dense);
     const int T = sparse ? ns : kv_len;
     for (int i = tid; i < T; i += blockDim.x) trow[i] = sparse ? sel[i] : i;
     if (tid == 0) s_ntok = T;

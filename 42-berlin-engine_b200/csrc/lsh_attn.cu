@@ -43,6 +43,9 @@ struct ec_lsh_attn {
   int n_tokens = 0, n_units = 0;
   const uint16_t* k = nullptr;
   const uint16_t* v = nullptr;
+  const int* page_table = nullptr;  // paged cache: logical 16-token block -> physical (else null)
+  int* rows = nullptr;         // [Q][max_sel] paged: the selection as physical rows
+  int* rows_n = nullptr;       // [Q] their count
   int* cand = nullptr;         // [Q][max_tokens]
   float* cscore = nullptr;     // [Q][max_tokens]
   unsigned* seen = nullptr;    // [Q][max_units / 32 + 1]
@@ -57,8 +60,15 @@ struct ec_lsh_attn {
 namespace ec {
 namespace {
 
+// Row of position p in the cache: the position itself (linear), or the
+// physical row of a paged cache of 16-token blocks ([block][16][KV][hd]).
+__device__ __forceinline__ long cache_row(const int* pt, int p) {
+  return pt ? (long)pt[p >> 4] * 16 + (p & 15) : (long)p;
+}
+
 // code of unit u in table l
 __global__ void __launch_bounds__(128) lsh_unit_codes_kernel(const uint16_t* __restrict__ k,
+                                                             const int* __restrict__ pt,
                                                              int KV, int hd, int unit,
                                                              int n_units, int L, int bits,
                                                              const float* __restrict__ hp,
@@ -69,7 +79,7 @@ __global__ void __launch_bounds__(128) lsh_unit_codes_kernel(const uint16_t* __r
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float a = 0.0f;
     for (int t = 0; t < unit; t++)
-      a = __fadd_rn(a, bf16_to_f32(k[((size_t)(u * unit + t) * KV) * hd + d]));
+      a = __fadd_rn(a, bf16_to_f32(k[(cache_row(pt, u * unit + t) * KV) * hd + d]));
     key[d] = unit > 1 ? __fmul_rn(a, __fdiv_rn(1.0f, (float)unit)) : a;
   }
   __syncthreads();
@@ -88,6 +98,7 @@ __global__ void __launch_bounds__(128) lsh_unit_codes_kernel(const uint16_t* __r
 }
 
 struct QueryArgs {
+  const int* pt;  // paged cache page table (nullptr: linear)
   const float* q;  // [Q][H][hd]
   const uint16_t* k;
   const float* hp;
@@ -229,7 +240,7 @@ __global__ void __launch_bounds__(512) lsh_query_kernel(QueryArgs a) {
   // scores (inference.c:341-353)
   const int grp = a.H / a.KV;
   for (int i = tid; i < nc; i += blockDim.x) {
-    const uint16_t* kr = a.k + (size_t)cand[i] * a.KV * a.hd;
+    const uint16_t* kr = a.k + cache_row(a.pt, cand[i]) * a.KV * a.hd;
     float s = 0.0f;
     for (int kh = 0; kh < a.KV; kh++)
       s = __fadd_rn(s, dot_bf16_ref(kr + kh * a.hd, q + kh * grp * a.hd, a.hd));
@@ -246,6 +257,22 @@ __global__ void __launch_bounds__(512) lsh_query_kernel(QueryArgs a) {
       a.stats[qi * 2] = s_found;
       a.stats[qi * 2 + 1] = nc;
     }
+  }
+}
+
+// Paged cache: the selection (positions, heap order) as physical rows for the
+// attention kernel's linear addressing; every position in order when the
+// query attends densely.
+__global__ void lsh_rows_kernel(const int* __restrict__ pt, const int* __restrict__ sel,
+                                const int* __restrict__ nsel, int* rows, int* rows_n, int max_sel,
+                                int n_tokens) {
+  const int qi = blockIdx.x;
+  const int ns = nsel[qi];
+  const int n = ns > 0 ? ns : n_tokens;
+  if (threadIdx.x == 0) rows_n[qi] = n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int p = ns > 0 ? sel[(long)qi * max_sel + i] : i;
+    rows[(long)qi * max_sel + i] = (int)cache_row(pt, p);
   }
 }
 
@@ -324,6 +351,8 @@ extern "C" int ec_lsh_attn_create(const ec_lsh_attn_config* c, int device, ec_ls
   TRY(la_alloc(h, &h->cscore, (size_t)Q * h->max_tokens));
   TRY(la_alloc(h, &h->seen, (size_t)Q * (max_units / 32 + 1)));
   TRY(la_alloc(h, &h->sel, (size_t)Q * h->max_sel));
+  TRY(la_alloc(h, &h->rows, (size_t)Q * h->max_sel));
+  TRY(la_alloc(h, &h->rows_n, (size_t)Q));
   TRY(la_alloc(h, &h->nsel, (size_t)Q));
   TRY(la_alloc(h, &h->stats, (size_t)Q * 2));
   TRY(la_alloc(h, &h->err, 1));
@@ -343,10 +372,29 @@ extern "C" int ec_lsh_attn_create(const ec_lsh_attn_config* c, int device, ec_ls
   return EC_OK;
 }
 
+namespace {
+int lsh_build(ec_lsh_attn* h, const uint16_t* k, const uint16_t* v, const int* page_table,
+              int n_tokens, void* stream);
+}  // namespace
+
 extern "C" int ec_lsh_attn_build(ec_lsh_attn* h, const uint16_t* k, const uint16_t* v,
                                  int n_tokens, void* stream) {
+  return lsh_build(h, k, v, nullptr, n_tokens, stream);
+}
+
+extern "C" int ec_lsh_attn_build_paged(ec_lsh_attn* h, const uint16_t* k_blocks,
+                                       const uint16_t* v_blocks, const int* page_table,
+                                       int n_tokens, void* stream) {
+  if (!page_table) return fail_la(EC_ERR_ARG, "null page table");
+  return lsh_build(h, k_blocks, v_blocks, page_table, n_tokens, stream);
+}
+
+namespace {
+int lsh_build(ec_lsh_attn* h, const uint16_t* k, const uint16_t* v, const int* page_table,
+              int n_tokens, void* stream) {
   if (!h || !k || !v || n_tokens <= 0 || n_tokens > h->max_tokens)
     return fail_la(EC_ERR_ARG, "bad argument");
+  h->page_table = page_table;
   cudaSetDevice(h->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int max_units = h->max_tokens / h->unit + 1;
@@ -357,7 +405,8 @@ extern "C" int ec_lsh_attn_build(ec_lsh_attn* h, const uint16_t* k, const uint16
   h->n_units = nu;
   std::vector<uint32_t> codes((size_t)h->L * nu);
   if (nu > 0) {
-    ec::lsh_unit_codes_kernel<<<nu, 128, 0, s>>>(k, h->KV, h->hd, h->unit, nu, h->L, h->bits,
+    ec::lsh_unit_codes_kernel<<<nu, 128, 0, s>>>(k, page_table, h->KV, h->hd, h->unit, nu, h->L,
+                                                 h->bits,
                                                  h->hp, h->codes, max_units);
     EC_CUDA_TRY(cudaGetLastError());
     for (int l = 0; l < h->L; l++)
@@ -382,6 +431,7 @@ extern "C" int ec_lsh_attn_build(ec_lsh_attn* h, const uint16_t* k, const uint16
   EC_CUDA_TRY(cudaStreamSynchronize(s));
   return EC_OK;
 }
+}  // namespace
 
 extern "C" int ec_lsh_attn_query(ec_lsh_attn* h, const float* q, int n_queries, float* out,
                                  int* selected_out, int* n_selected_out, void* stream) {
@@ -392,6 +442,7 @@ extern "C" int ec_lsh_attn_query(ec_lsh_attn* h, const float* q, int n_queries, 
   ec::QueryArgs a{};
   a.q = q;
   a.k = h->k;
+  a.pt = h->page_table;
   a.hp = h->hp;
   a.codes = h->codes;
   a.boff = h->boff;
@@ -438,6 +489,15 @@ extern "C" int ec_lsh_attn_query(ec_lsh_attn* h, const float* q, int n_queries, 
   sb.att = out;
   sb.sel = h->sel;
   sb.nsel = h->nsel;
+  if (h->page_table) {
+    // the attention reads physical rows of the blocks in the selection's order
+    ec::lsh_rows_kernel<<<n_queries, 256, 0, s>>>(h->page_table, h->sel, h->nsel, h->rows,
+                                                  h->rows_n, h->max_sel, h->n_tokens);
+    EC_CUDA_TRY(cudaGetLastError());
+    sb.sel = h->rows;
+    sb.nsel = h->rows_n;
+    sb.list_dense = 1;
+  }
   sb.max_sel = h->max_sel;
   sb.sparse_k = h->top_k;
   sb.window = h->window;

@@ -35,7 +35,7 @@ EXPORTS = [
     "ec_transformer_free", "ec_profile_enable", "ec_profile_read", "ec_lsh_attn_create",
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
     "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill", "ec_set_weight_bf16",
-    "ec_tp_unique_id", "ec_create_tp", "ec_verify",
+    "ec_tp_unique_id", "ec_create_tp", "ec_verify", "ec_lsh_attn_build_paged",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
@@ -126,6 +126,7 @@ def lib():
             "ec_lsh_attn_create": (i, [C.POINTER(LshAttnConfig), i, C.POINTER(vp)]),
             "ec_lsh_attn_destroy": (None, [vp]),
             "ec_lsh_attn_build": (i, [vp, vp, vp, i, vp]),
+            "ec_lsh_attn_build_paged": (i, [vp, vp, vp, vp, i, vp]),
             "ec_lsh_attn_query": (i, [vp, vp, i, vp, vp, vp, vp]),
             "ec_lsh_attn_read": (i, [vp, i, vp, C.c_size_t]),
             "ec_profile_enable": (i, [vp, i]),

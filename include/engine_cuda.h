@@ -416,6 +416,15 @@ void	ec_lsh_attn_destroy(ec_lsh_attn *h);
 ** table per full unit, buckets newest first (lsh_update's chain order). */
 int		ec_lsh_attn_build(ec_lsh_attn *h, const uint16_t *k, const uint16_t *v,
 			int n_tokens, void *stream);
+/* The same over a paged cache (BASELINE configuration 3's layout): k_blocks,
+** v_blocks [physical block][16][n_kv_heads][head_dim] BF16 and page_table
+** [logical block] -> physical block (device; the handle keeps the
+** pointers).  Position p lives in row p % 16 of block page_table[p / 16];
+** selection and attention are identical to the linear cache holding the
+** same values.  max_tokens bounds the physical rows (blocks x 16). */
+int		ec_lsh_attn_build_paged(ec_lsh_attn *h, const uint16_t *k_blocks,
+			const uint16_t *v_blocks, const int *page_table, int n_tokens,
+			void *stream);
 /* n_queries queries q [n][n_heads][head_dim] (device, rotated) at position
 ** n_tokens - 1: selection then attention into out [n][n_heads][head_dim].
 ** selected_out [n][top_k] and n_selected_out [n] (device, optional)

@@ -2,7 +2,9 @@
 against the restatement (oracle/port/lsh_attn.c), bit for bit: the selected
 positions in the reference's heap order and every head's output.  Cases:
 per-key units with and without the candidate cut-off, 16-token units, and
-the reference's own setting (1 table x 16 bits x 64-token units)."""
+the reference's own setting (1 table x 16 bits x 64-token units); and the
+same cache as paged 16-token blocks under a shuffled page table
+(ec_lsh_attn_build_paged), which must give the identical result."""
 import ctypes as C
 
 import numpy as np
@@ -80,5 +82,64 @@ def test_lsh_attention_matches_oracle(torch, oracle, synth, tables, bits, unit, 
         if unit == 1 and max_cand >= 4096:
             # the planted keys are found (recall of the configuration's check)
             assert len(set(planted) & set(want_sel[:n].tolist())) >= 32
+    finally:
+        L.ec_lsh_attn_destroy(h)
+
+
+@pytest.mark.parametrize("T,top_k", [(3000, 64), (100, 256)])
+def test_lsh_attention_paged_cache(torch, oracle, synth, T, top_k):
+    """The cache as paged blocks ([block][16][KV][hd], blocks shuffled by a
+    page table): selection and output bit-identical to the restatement over
+    the linear cache -- the sparse case, and a context shorter than top_k
+    (every position attended, in order, through the page table)."""
+    from conftest import load_pkg_module
+    eng = load_pkg_module("engine")
+    H, KV, hd, window, tables, bits, unit, max_cand, radius = 8, 2, 64, 128, 4, 8, 16, 64, 4
+    q, k, v, _ = planted_case(synth, max(T, 300), H, KV, hd, window, seed=T)
+    k, v = k[:T], v[:T]
+    P = oracle.port()
+    lsh = P.port_lsh_create(tables, bits, hd, unit, T // unit + 1, radius, 42)
+    k0 = bf16_to_f32(k[:, 0, :]).astype(np.float32)
+    for t in range(T):
+        P.port_lsh_update(lsh, np.ascontiguousarray(k0[t]), t)
+    want_sel = np.zeros(T, np.int32)
+    want_out = np.zeros(H * hd, np.float32)
+    n = P.port_lsh_attend(lsh, np.ascontiguousarray(k.reshape(-1)),
+                          np.ascontiguousarray(v.reshape(-1)), T, np.ascontiguousarray(q.reshape(-1)),
+                          H, KV, hd, window, max_cand, top_k, want_sel, want_out)
+    P.port_lsh_free(lsh)
+    nblk = (T + 15) // 16
+    rng = np.random.default_rng(3)
+    pt = rng.permutation(nblk + 5)[:nblk].astype(np.int32)   # logical -> physical
+    kp = np.zeros((nblk + 5, 16, KV, hd), np.uint16)
+    vp = np.zeros_like(kp)
+    for lb in range(nblk):
+        m = min(16, T - lb * 16)
+        kp[pt[lb], :m] = k[lb * 16:lb * 16 + m]
+        vp[pt[lb], :m] = v[lb * 16:lb * 16 + m]
+    L = eng.lib()
+    cfg = eng.LshAttnConfig(H, KV, hd, (nblk + 5) * 16, tables, bits, unit, radius, max_cand,
+                            window, top_k, 1)
+    h = C.c_void_p()
+    eng.check(L.ec_lsh_attn_create(C.byref(cfg), 0, C.byref(h)))
+    try:
+        dk = torch.from_numpy(kp.reshape(-1)).cuda()
+        dv = torch.from_numpy(vp.reshape(-1)).cuda()
+        dpt = torch.from_numpy(pt).cuda()
+        dq = torch.from_numpy(q.reshape(-1)).cuda()
+        out = torch.full((H * hd,), float("nan"), device="cuda")
+        sel = torch.full((top_k,), -7, dtype=torch.int32, device="cuda")
+        ns = torch.zeros(1, dtype=torch.int32, device="cuda")
+        eng.check(L.ec_lsh_attn_build_paged(h, dk.data_ptr(), dv.data_ptr(), dpt.data_ptr(), T,
+                                            None))
+        eng.check(L.ec_lsh_attn_query(h, dq.data_ptr(), 1, out.data_ptr(), sel.data_ptr(),
+                                      ns.data_ptr(), None))
+        torch.cuda.synchronize()
+        if n < T:
+            assert int(ns.item()) == n
+            assert np.array_equal(sel.cpu().numpy()[:n], want_sel[:n])
+        else:
+            assert int(ns.item()) == -1  # dense: every position
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), want_out.view(np.uint32))
     finally:
         L.ec_lsh_attn_destroy(h)
