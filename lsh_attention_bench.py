@@ -70,6 +70,8 @@ def main():
     ap.add_argument("--queries", default="1,32")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--cpu", action="store_true", help="also time the restatement (one query)")
+    ap.add_argument("--paged", action="store_true",
+                    help="the cache as 16-token blocks under a shuffled page table")
     args = ap.parse_args()
     eng = _load("engine")
     L = eng.lib()
@@ -84,8 +86,21 @@ def main():
             cfg = eng.LshAttnConfig(H, KV, HD, T, TABLES, BITS, 1, RADIUS, MAX_CAND, WINDOW, TOP_K, Q)
             h = C.c_void_p()
             eng.check(L.ec_lsh_attn_create(C.byref(cfg), 0, C.byref(h)))
+            if args.paged:
+                # blocks of 16 positions stored in a shuffled physical order
+                nblk = T // 16
+                pt = torch.randperm(nblk, device="cuda").to(torch.int32)
+                kb = torch.empty_like(k).view(nblk, 16, KV, HD)
+                vb = torch.empty_like(v).view(nblk, 16, KV, HD)
+                kb[pt.long()] = k.view(nblk, 16, KV, HD)
+                vb[pt.long()] = v.view(nblk, 16, KV, HD)
+                torch.cuda.synchronize()
             t0 = time.perf_counter()
-            eng.check(L.ec_lsh_attn_build(h, k.data_ptr(), v.data_ptr(), T, None))
+            if args.paged:
+                eng.check(L.ec_lsh_attn_build_paged(h, kb.data_ptr(), vb.data_ptr(), pt.data_ptr(),
+                                                    T, None))
+            else:
+                eng.check(L.ec_lsh_attn_build(h, k.data_ptr(), v.data_ptr(), T, None))
             build_s = time.perf_counter() - t0
             out = torch.empty((Q, H, HD), device="cuda")
             sel = torch.empty((Q, TOP_K), dtype=torch.int32, device="cuda")
@@ -114,7 +129,8 @@ def main():
                                     for i in range(Q)]))
             ncand = stats[1::2].astype(np.float64)
             algo = (TABLES * 4 * T + ncand * KV * HD * 2 + 2 * TOP_K * KV * HD * 2).sum()
-            line = {"config": "lsh_attention", "tokens": T, "queries": Q, "ms": round(ms, 4),
+            line = {"config": "lsh_attention", "cache": "paged" if args.paged else "linear",
+                    "tokens": T, "queries": Q, "ms": round(ms, 4),
                     "queries_per_s": round(Q / (ms * 1e-3), 1), "recall": round(recall, 4),
                     "units_found_mean": float(stats[0::2].mean()),
                     "candidates_mean": float(ncand.mean()),
