@@ -36,6 +36,7 @@ EXPORTS = [
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
     "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill", "ec_set_weight_bf16",
     "ec_tp_unique_id", "ec_create_tp", "ec_verify", "ec_lsh_attn_build_paged",
+    "ec_op_sample_top_p", "ec_op_sample_temperature",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
@@ -113,6 +114,8 @@ def lib():
             "ec_op_silu_mul": (i, [vp, vp, vp, i, vp]),
             "ec_op_quant_int8": (i, [vp, vp, vp, i, i, vp]),
             "ec_op_argmax": (i, [vp, i, i, vp, vp]),
+            "ec_op_sample_top_p": (i, [vp, i, i, vp, vp, i, f, f, f, i, vp, vp, vp]),
+            "ec_op_sample_temperature": (i, [vp, i, i, f, vp, vp, vp]),
             "ec_op_paged_append": (i, [C.POINTER(PagedView), vp, vp, i, vp]),
             "ec_op_paged_attention": (i, [C.POINTER(PagedView), vp, vp, i, i, i, vp, vp, vp]),
             "ec_op_paged_attention_static": (i, [C.POINTER(PagedView), vp, vp, i, i, i, vp, vp,
@@ -304,6 +307,19 @@ class Engine:
         out = np.empty(tokens.size, np.int32)
         check(lib().ec_verify(self.h, int(seq), _ptr(tokens), tokens.size, int(pos0), _ptr(out)))
         return out
+
+    def sample_device(self, B, r_ptr, out_ptr, history_ptr=None, history_len_ptr=None,
+                      history_stride=0, temperature=0.7, top_p=0.9, penalty=1.2,
+                      block_token0=True):
+        """The server's sampling step (worker.c:436-497) on the last step's
+        device logits, on the context's stream: no logits leave the device.
+        out_ptr may be the next step's tokens_dev."""
+        check(lib().ec_op_sample_top_p(
+            lib().ec_logits_device(self.h), self.c.vocab_size, B,
+            C.c_void_p(history_ptr) if history_ptr else None,
+            C.c_void_p(history_len_ptr) if history_len_ptr else None, int(history_stride),
+            float(temperature), float(top_p), float(penalty), int(block_token0),
+            C.c_void_p(r_ptr), C.c_void_p(out_ptr), self.stream()))
 
     def step_device(self, tokens_ptr, pos_ptr, B, feedback=True):
         check(lib().ec_decode_step_device(self.h, C.c_void_p(tokens_ptr), C.c_void_p(pos_ptr),

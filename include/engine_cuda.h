@@ -324,6 +324,36 @@ int		ec_op_quant_int8(int8_t *out, float *scales, const float *in, int rows,
 /* sample_argmax (src/compute/sampler.h:19) of B rows of n logits. */
 int		ec_op_argmax(const float *logits, int n, int B, int *out, void *stream);
 
+/* The server's sampling step on the device, `rows` rows of n logits each
+** (device pointers; the logits are modified in place, as the reference does):
+**   repetition penalty (src/server/worker.c:436-442, 477-490): for each of
+**     history_len[row] ids at history + row * history_stride (prompt then
+**     generated, every occurrence), l > 0 ? l / penalty : l * penalty;
+**     history may be NULL (no penalty);
+**   block_token0 != 0: logits[0] = -1e9 (worker.c:444, 492);
+**   sample_top_p (src/compute/sampler_topp.c:113): softmax at temperature,
+**     the nucleus of the descending order whose running sum first exceeds
+**     top_p, and the first token of it whose running sum exceeds r[row] times
+**     the nucleus' mass.  r[row] in [0, 1] is the caller's draw (the
+**     reference takes rand() / RAND_MAX).
+** Equal probabilities are ordered by index (the reference's qsort leaves it
+** unspecified).  Running sums are exact 2^-50 fixed point rather than the
+** reference's float sequence, so a draw within float rounding of a boundary
+** can pick the token next to the reference's in the sorted order.  One
+** cluster of 8 CTAs per row, the row held in their shared memory
+** (n <= 327680, else EC_ERR_UNSUPPORTED); no allocation. */
+int		ec_op_sample_top_p(float *logits, int n, int rows, const int *history,
+			const int *history_len, int history_stride, float temperature,
+			float top_p, float penalty, int block_token0, const float *r,
+			int *out, void *stream);
+
+/* sample_temperature (src/compute/sampler_temp.c:96): softmax at
+** temperature, then the first index, in index order, whose running sum
+** exceeds r[row].  A draw above the whole mass gives n - 1 (the reference
+** returns n). */
+int		ec_op_sample_temperature(const float *logits, int n, int rows,
+			float temperature, const float *r, int *out, void *stream);
+
 /* One layer's paged INT8 KV cache in device memory
 ** (t_kv_block / t_block_manager, src/memory/paged.h:53-88).  Blocks hold 16
 ** tokens; within a block K rows are stored rotated by 16-byte pieces (piece p

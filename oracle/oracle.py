@@ -101,6 +101,9 @@ def port():
         _sig(lib, "port_silu_mul", None, f32p, f32p, f32p, C.c_int)
         _sig(lib, "port_quant_int8", C.c_float, i8p, f32p, C.c_int)
         _sig(lib, "port_argmax", C.c_int, f32p, C.c_int)
+        _sig(lib, "port_sample_top_p", C.c_int, f32p, C.c_int, i32p, C.c_int, C.c_float,
+             C.c_float, C.c_float, C.c_int, C.c_float, i32p, f32p)
+        _sig(lib, "port_sample_temperature", C.c_int, f32p, C.c_int, C.c_float, C.c_float)
         _sig(lib, "port_heap_topk", C.c_int, f32p, i32p, C.c_int, C.c_int, i32p)
         _sig(lib, "port_fast_expf", C.c_float, C.c_float)
         _sig(lib, "port_fast_expf_vec", C.c_float, C.c_float)
@@ -192,6 +195,8 @@ def _bind(lib):
     _sig(lib, "refd_silu_mul", None, f32p, f32p, f32p, C.c_int)
     _sig(lib, "refd_quant_int8", C.c_float, i8p, f32p, C.c_int)
     _sig(lib, "refd_argmax", C.c_int, f32p, C.c_int)
+    _sig(lib, "refd_first_rand", C.c_float, C.c_uint)
+    _sig(lib, "refd_sample_top_p", C.c_int, f32p, C.c_int, C.c_float, C.c_float, C.c_uint)
     _sig(lib, "refd_heap_topk", C.c_int, f32p, i32p, C.c_int, C.c_int, i32p)
     _sig(lib, "refd_lsh_ctx_create", vp, C.c_int, C.c_uint)
     _sig(lib, "refd_lsh_hyperplanes", C.POINTER(C.c_float), vp)

@@ -164,4 +164,13 @@ const t_port_paged	*port_model_paged(void *m, int layer);
 const uint16_t	*port_model_linear_k(void *m, int layer);
 void	port_model_counters(void *m, unsigned long long *out);
 
+/* ---- sampling (sample.c) ---------------------------------------------- */
+void	port_repetition_penalty(float *logits, const int *hist, int hn,
+			float penalty);
+int		port_sample_top_p(float *logits, int n, const int *hist, int hn,
+			float temperature, float top_p, float penalty, int block0, float r,
+			int *cut_out, float *cum_out);
+int		port_sample_temperature(const float *logits, int n, float temperature,
+			float r);
+
 #endif

@@ -424,6 +424,29 @@ int	refd_argmax(const float *logits, int n)
 	return (sample_argmax(&l));
 }
 
+/* the reference's own sample_top_p (sampler_topp.c:113) after srand(seed);
+** refd_first_rand gives the draw it takes: the first rand() / RAND_MAX */
+float	refd_first_rand(unsigned int seed)
+{
+	srand(seed);
+	return ((float)rand() / (float)RAND_MAX);
+}
+
+int	refd_sample_top_p(const float *logits, int n, float temperature,
+		float top_p, unsigned int seed)
+{
+	t_tensor	l;
+	t_arena		a;
+	int			tok;
+
+	col(&l, (void *)logits, n, DTYPE_F32);
+	arena_init(&a, (size_t)n * 8 + 4096);
+	srand(seed);
+	tok = sample_top_p(&l, temperature, top_p, &a);
+	arena_free(&a);
+	return (tok);
+}
+
 /* min-heap top-K exactly as inference.c:410-418 drives it */
 int	refd_heap_topk(const float *scores, const int *idx, int n, int k,
 		int *out)
