@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(256, 4) kv_append_kernel(KvLayout kv, LshLayou
     }
   } else if (pos < kv.seq_len) {
     // kv_cache_append with F32 -> BF16 (kv_cache.c:55-75)
-    const long row = (((long)b * kv.n_layers + layer) * kv.seq_len + pos) * KV * hd;
+    const long row = (((long)kv_seq(kv, b) * kv.n_layers + layer) * kv.seq_len + pos) * KV * hd;
     for (int i = tid; i < KV * hd; i += blockDim.x) {
       kv.lk[row + i] = f32_to_bf16(k[i]);
       kv.lv[row + i] = f32_to_bf16(v[i]);
@@ -148,8 +148,15 @@ __global__ void __launch_bounds__(256) linear_cand_kernel(KvLayout kv, LshLayout
     return;
   }
   const int ws = kv_len > sb.window ? kv_len - sb.window : 0;
-  const int* meta = lsh.meta + b * 4;
-  const int n_units = meta[2];
+  // the sequence whose index this row queries (prefill: every row's)
+  const int sq = kv_seq(kv, b);
+  const int* meta = lsh.meta + sq * 4;
+  const int* ustart = lsh.unit_start + (long)sq * lsh.max_units;
+  const int* ulen = lsh.unit_len + (long)sq * lsh.max_units;
+  // A unit enters the index with its last token (lsh_update); a prefill row
+  // at `pos` sees the index as decode would: units that end by `pos`
+  // (units are added in position order, so unit 0 is the first to exist).
+  const int n_units = meta[2] > 0 && ustart[0] + ulen[0] - 1 <= pos ? meta[2] : 0;
   if (tid == 0) s_nu = 0;
   __syncthreads();
   if (ws > 0 && n_units > 0 && lsh.tables > 0) {
@@ -175,14 +182,17 @@ __global__ void __launch_bounds__(256) linear_cand_kernel(KvLayout kv, LshLayout
       int n = 0;
       const int maxc = lsh.max_cand < 64 ? lsh.max_cand : 64;
       for (int t = 0; t < lsh.tables && n < maxc; t++) {
-        const long tb = (long)b * lsh.tables + t;
+        const long tb = (long)sq * lsh.tables + t;
         const uint32_t qh = s_code[t];
         for (int p = 0; p <= lsh.bits && n < maxc; p++) {
           const uint32_t probe = (p == 0) ? qh : (qh ^ (1u << (p - 1)));
           int id = lsh.heads[(tb << lsh.bits) + probe];
           while (id != -1 && n < maxc) {
             const uint32_t hh = lsh.unit_hash[tb * lsh.max_units + id];
-            if (__popc(qh ^ hh) <= lsh.radius && !(s_seen[id >> 5] & (1u << (id & 31)))) {
+            // units added after this row's token did not exist yet: skipped
+            // without counting, the chain below them is as it was
+            if (ustart[id] + ulen[id] - 1 <= pos && __popc(qh ^ hh) <= lsh.radius &&
+                !(s_seen[id >> 5] & (1u << (id & 31)))) {
               s_seen[id >> 5] |= 1u << (id & 31);
               s_units[n++] = id;
             }
@@ -194,11 +204,11 @@ __global__ void __launch_bounds__(256) linear_cand_kernel(KvLayout kv, LshLayout
       int m = 0;
       for (int i = 0; i < n; i++) {
         const int u = s_units[i];
-        const int st = lsh.unit_start[(long)b * lsh.max_units + u];
-        const int ln = lsh.unit_len[(long)b * lsh.max_units + u];
+        const int st = ustart[u];
+        const int ln = ulen[u];
         if (st + ln <= ws) {
           int j = m++;
-          while (j > 0 && lsh.unit_start[(long)b * lsh.max_units + s_units[j - 1]] > st) {
+          while (j > 0 && ustart[s_units[j - 1]] > st) {
             s_units[j] = s_units[j - 1];
             j--;
           }
@@ -215,8 +225,8 @@ __global__ void __launch_bounds__(256) linear_cand_kernel(KvLayout kv, LshLayout
     int n = 0;
     for (int i = 0; i < s_nu; i++) {
       const int u = s_units[i];
-      const int st = lsh.unit_start[(long)b * lsh.max_units + u];
-      const int ln = lsh.unit_len[(long)b * lsh.max_units + u];
+      const int st = ustart[u];
+      const int ln = ulen[u];
       int take = ws - st < ln ? ws - st : ln;
       if (take < 0) take = 0;
       if (take > cap_c - n) take = cap_c - n;
@@ -255,7 +265,7 @@ __global__ void __launch_bounds__(256) linear_score_kernel(KvLayout kv, StepBuff
   if (blockIdx.x * cpb >= nc) return;
   const bool live = tid < cpb * KV && c < nc;
   const float* q = sb.qrot + (long)b * H * hd;
-  const long lrow = ((long)b * kv.n_layers + layer) * kv.seq_len;
+  const long lrow = ((long)(kv.shared_cache ? 0 : kv_seq(kv, b)) * kv.n_layers + layer) * kv.seq_len;
   if (live) {
     const int pos = sb.lcand[(long)b * cap_c + c];
     part[tid] = dot_bf16_ref(kv.lk + ((lrow + pos) * KV + kh) * hd, q + kh * grp * hd, hd);
@@ -297,7 +307,7 @@ __global__ void lsh_update_key_kernel(LshLayout lsh, StepBuffers sb, const float
 // warp per sequence replays the heap; sel[b] receives the positions in the
 // reference's heap array order.
 __global__ void __launch_bounds__(32) linear_heap_kernel(LshLayout lsh, StepBuffers sb,
-                                                         int cap_c) {
+                                                         int cap_c, int seq_plus1) {
   __shared__ __align__(16) uint2 hp[1024];  // heap nodes, 1-based
   const int b = blockIdx.x, lane = threadIdx.x;
   pdl_launch_dependents();
@@ -313,9 +323,11 @@ __global__ void __launch_bounds__(32) linear_heap_kernel(LshLayout lsh, StepBuff
   int* out = sb.sel + (long)b * sb.max_sel;
   for (int i = lane; i < size; i += 32) out[i] = (int)hp[i + 1].y;
   if (lane == 0) {
+    // prefill rows of one sequence share its counters
+    const int sq = seq_plus1 ? seq_plus1 - 1 : b;
     sb.nsel[b] = size;
-    lsh.counters[b * 2] += 1ull;
-    lsh.counters[b * 2 + 1] += (unsigned long long)size;
+    atomicAdd(&lsh.counters[sq * 2], 1ull);
+    atomicAdd(&lsh.counters[sq * 2 + 1], (unsigned long long)size);
   }
 }
 
@@ -586,7 +598,8 @@ __global__ void __launch_bounds__(kAttnThreads, VF ? 1 : 3)
   const float* qg = sb.qrot + (long)b * H * hd;
   for (int d = tid; d < hd; d += blockDim.x) qs[d] = qg[h * hd + d];
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
-  const long lrow = ((long)(kv.shared_cache ? 0 : b) * kv.n_layers + layer) * kv.seq_len;  // linear
+  const long lrow =
+      ((long)(kv.shared_cache ? 0 : kv_seq(kv, b)) * kv.n_layers + layer) * kv.seq_len;  // linear
 
   // ------------------------------------------ selected blocks / positions
   if constexpr (PAGED) {
@@ -1432,7 +1445,8 @@ cudaError_t launch_linear_select(const KvLayout& kv, const LshLayout& lsh, const
   if (!e)
     e = launch_ex(linear_score_kernel, dim3((cap_c + cpb - 1) / cpb, B), dim3(256), 0, s, pdl, kv,
                   sb, layer, cap_c);
-  if (!e) e = launch_ex(linear_heap_kernel, dim3(B), dim3(32), 0, s, pdl, lsh, sb, cap_c);
+  if (!e)
+    e = launch_ex(linear_heap_kernel, dim3(B), dim3(32), 0, s, pdl, lsh, sb, cap_c, kv.seq_plus1);
   return e;
 }
 
@@ -1456,7 +1470,7 @@ cudaError_t launch_linear_sum_heap(const LshLayout& lsh, const StepBuffers& sb,
   const int cap_c = linear_cand_cap(sb, lsh);
   tp_sum_scores_kernel<<<dim3(32, B), 256, 0, s>>>(sb, parts_all, world, kv_local, cap_c, B);
   cudaError_t e = cudaGetLastError();
-  if (!e) e = launch_ex(linear_heap_kernel, dim3(B), dim3(32), 0, s, false, lsh, sb, cap_c);
+  if (!e) e = launch_ex(linear_heap_kernel, dim3(B), dim3(32), 0, s, false, lsh, sb, cap_c, 0);
   return e;
 }
 

@@ -1036,16 +1036,23 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
     }
     if (prefill_seq >= 0) {
       // every row's token is in the cache: the centroids of the blocks this
-      // chunk filled, then each row's block selection
+      // chunk filled, the layer-0 LSH update in row order, then (paged) each
+      // row's block selection; linear mode selects below, each row seeing
+      // the LSH units that end by its own position
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
-      if ((e = ec::launch_paged_centroids(kv, l, prefill_seq, prefill_pos0, B, ctx->stream)))
-        return e;
+      if (kv.paged) {
+        if ((e = ec::launch_paged_centroids(kv, l, prefill_seq, prefill_pos0, B, ctx->stream)))
+          return e;
+        ctx->launches++;
+      }
       if (l == 0) {
         if ((e = ec::launch_lsh_update_rows(kv, ctx->lsh, sb, B, ctx->stream))) return e;
         if (ctx->lsh.tables > 0) ctx->launches++;
       }
-      if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
-      ctx->launches += 2;
+      if (kv.paged) {
+        if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
+        ctx->launches++;
+      }
     }
     if (!kv.paged && !split) {
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
@@ -1219,14 +1226,22 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
         if ((e = ec::launch_kv_append(kv, ctx->lsh, sb, l, B, ctx->stream, true))) return e;
       }
       // every row's token is in the cache: the chunk's block centroids, the
-      // layer-0 LSH update in row order, each row's block selection
+      // layer-0 LSH update in row order, each row's selection (paged blocks,
+      // or linear candidates from the LSH units that end by the row's
+      // position)
       ProfScope ps(ctx, EC_K_SELECT, 0.0);
-      if ((e = ec::launch_paged_centroids(kv, l, prefill_seq, prefill_pos0, B, ctx->stream)))
+      if (kv.paged &&
+          (e = ec::launch_paged_centroids(kv, l, prefill_seq, prefill_pos0, B, ctx->stream)))
         return e;
       if (l == 0 && (e = ec::launch_lsh_update_rows(kv, ctx->lsh, sb, B, ctx->stream))) return e;
-      if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
+      if (kv.paged) {
+        if ((e = ec::launch_paged_select_rows(kv, sb, l, B, ctx->stream))) return e;
+      } else if ((e = ec::launch_linear_select(kv, ctx->lsh, sb, l, B, ctx->stream, true))) {
+        return e;
+      }
       if ((e = ec::launch_attention(kv, sb, l, B, ctx->stream, true))) return e;
-      ctx->launches += 4 + (l == 0 && ctx->lsh.tables > 0);
+      ctx->launches += (kv.paged ? 4 : 2 + ec::kLinearSelectLaunches) +
+                       (l == 0 && ctx->lsh.tables > 0);
     }
     const bool last = l + 1 == L;
     for (int b0 = 0; b0 < B; b0 += ec::kTcMaxRows) {
@@ -1732,8 +1747,8 @@ int prefill_rows(ec_ctx* ctx, int seq, const int* tokens, int n, int pos0, float
   const ec_model_config& c = ctx->c;
   if (seq < 0 || seq >= c.max_batch) return fail(EC_ERR_ARG, "bad sequence");
   if (pos0 < 0 || (long)pos0 + n > c.seq_len) return fail(EC_ERR_ARG, "positions past seq_len");
-  if (!ctx->kv.paged || !ctx->chain || ctx->tp_world > 1)
-    return fail(EC_ERR_UNSUPPORTED, "prefill needs paged KV and the chain GEMV layout (one rank)");
+  if (!ctx->chain || ctx->tp_world > 1)
+    return fail(EC_ERR_UNSUPPORTED, "prefill needs the chain GEMV layout (one rank)");
   for (int i = 0; i < n; i++)
     if (tokens[i] < 0 || tokens[i] >= c.vocab_size) return fail(EC_ERR_ARG, "token out of range");
   cudaSetDevice(ctx->device);

@@ -265,14 +265,16 @@ int		ec_op_gemv_packed(int wkind, const void *w_packed, const float *scale,
 ** src/inference/inference.c:718-1112): tokens[0..n) at positions
 ** pos0..pos0+n-1 go through the model max_batch at a time as rows of one
 ** batched step (each weight pass serves every row of a chunk), with every row
-** addressing `seq`'s paged KV cache; each row's KV append, block selection
-** and attention keep the decode step's arithmetic, so the cache and the
-** logits are bit-identical to decoding the tokens one at a time.  With
+** addressing `seq`'s KV cache; each row's KV append, selection (paged
+** blocks, or in linear mode LSH candidates from the units that end by the
+** row's own position) and attention keep the decode step's arithmetic, so
+** the cache, the LSH index and the logits are bit-identical to decoding the
+** tokens one at a time.  With
 ** tensor_min_batch = m > 0 (INT8), chunks of at least m rows run their
 ** projections on the tensor cores instead (the tcgen05 GEMM of batched
 ** steps: within about 1e-6 relative, not bit-identical).  The last
 ** token's logits and greedy token go to logits_host / argmax_host (either
-** may be NULL).  Paged KV mode only. */
+** may be NULL).  Both KV modes; one rank (not under tensor parallelism). */
 int		ec_prefill(ec_ctx *ctx, int seq, const int *tokens, int n, int pos0,
 			float *logits_host, int *argmax_host);
 

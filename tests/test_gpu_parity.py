@@ -447,6 +447,54 @@ def test_group_attention_sparse(eng, torch, oracle, synth, heads, hd):
     e.close()
 
 
+@pytest.mark.parametrize("max_batch", [16, 5])
+def test_linear_prefill_matches_sequential_decode(eng, torch, oracle, synth, max_batch):
+    """ec_prefill in linear KV mode: a 400-token prompt as rows of batched
+    steps into one sequence's BF16 cache.  Past the 128-token window the
+    rows select top-32 keys from LSH candidates; the layer-0 index is built
+    for the whole chunk before the rows query it, and each row sees only the
+    units that end by its own position (as decode would).  The last token's
+    logits, every decode step after it and the sparse-query counters are
+    bit-identical to feeding the tokens one at a time and to the
+    restatement."""
+    cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4,
+                            vocab_size=2048, seq_len=512, head_dim=64, rope_theta=1e4)
+    model = synth.make_model(cfg, seed=43)
+    a = eng.Engine(cfg, use_paged_kv=False, sparse_k=32, max_batch=max_batch)
+    b = eng.Engine(cfg, use_paged_kv=False, sparse_k=32, max_batch=1)
+    a.load(model)
+    b.load(model)
+    pm = oracle.PortModel(model, use_paged_kv=False, sparse_k=32)
+    n = 400
+    prompt = [int(t) for t in synth.prompt(cfg, n, seed=10)]
+    lg_a, tok_a = a.prefill(0, prompt)
+    for p, t in enumerate(prompt):
+        lg_b, am_b = b.step([t], [p])
+        want = pm.forward(t, p)
+    assert np.array_equal(bits(lg_a), bits(lg_b[0])), "prompt logits"
+    assert np.array_equal(bits(lg_a), bits(want)), "prompt logits against the restatement"
+    assert tok_a == int(am_b[0])
+    assert a.counters(0) == b.counters(0)
+    assert a.counters(0)[0] > 0, "the sparse path ran"
+    la_idx, lb_idx = a.lsh(0), b.lsh(0)
+    assert la_idx["n_units"] == lb_idx["n_units"] == n // 64
+    nu = la_idx["n_units"]
+    for key in ("unit_hash", "next"):
+        assert np.array_equal(la_idx[key][:, :nu], lb_idx[key][:, :nu]), key
+    assert np.array_equal(la_idx["heads"], lb_idx["heads"])
+    tok = tok_a
+    for p in range(n, n + 6):
+        la, _ = a.step([tok], [p])
+        lb, amb = b.step([tok], [p])
+        want = pm.forward(tok, p)
+        assert np.array_equal(bits(la[0]), bits(lb[0])), f"decode step {p}"
+        assert np.array_equal(bits(la[0]), bits(want)), f"decode step {p} against the restatement"
+        tok = int(amb[0])
+    assert a.counters(0) == b.counters(0)
+    a.close()
+    b.close()
+
+
 @pytest.mark.parametrize("max_batch", [8, 3])
 def test_prefill_matches_sequential_decode(eng, torch, oracle, synth, max_batch):
     """ec_prefill runs a 150-token prompt as rows of batched steps (chunks of

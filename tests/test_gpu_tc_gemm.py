@@ -128,18 +128,23 @@ def test_tensor_core_decode_matches_oracle(eng, torch, oracle, synth, B, steps):
     print(f"worst |d| / range = {worst:.2e}")
 
 
-def test_tensor_core_prefill(eng, torch, oracle, synth):
+@pytest.mark.parametrize("mode", ["paged", "linear"])
+def test_tensor_core_prefill(eng, torch, oracle, synth, mode):
     """ec_prefill with tensor_min_batch: chunks of >= 16 rows run their
     projections on the tensor cores (the last chunk of 7 rows on the exact
-    chain).  The prompt's last logits within 2e-2 of the range of the
-    restatement's, its greedy token equal, and decode steps after it still
-    within tolerance with equal greedy tokens."""
+    chain), in both KV modes.  The prompt's last logits within 2e-2 of the
+    range of the restatement's, its greedy token equal, and decode steps
+    after it still within tolerance with equal greedy tokens."""
     cfg = synth.ModelConfig(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4,
                             vocab_size=4096, seq_len=512, head_dim=64, rope_theta=1e4)
     model = synth.make_model(cfg, seed=37)
-    e = eng.Engine(cfg, max_batch=32, tensor_min_batch=16, sparse_blocks_k=4)
+    if mode == "paged":
+        kw = dict(sparse_blocks_k=4)
+    else:
+        kw = dict(use_paged_kv=False, sparse_k=32)
+    e = eng.Engine(cfg, max_batch=32, tensor_min_batch=16, **kw)
     e.load(model)
-    pm = oracle.PortModel(model, sparse_blocks_k=4)
+    pm = oracle.PortModel(model, **kw)
     P = oracle.port()
     prompt = [int(t) for t in synth.prompt(cfg, 135, seed=12)]
     lg, tok = e.prefill(0, prompt)
