@@ -9,11 +9,16 @@ namespace ec {
 
 // simd_bf16_to_f32 of the token's embedding row (inference.c:83-88)
 __global__ void embed_kernel(const uint16_t* __restrict__ emb, const int* __restrict__ tokens,
-                             float* __restrict__ x, int dim, int vocab) {
+                             float* __restrict__ x, int dim, int vocab, TokenHistory th) {
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x;
   int tok = tokens[b];
+  // token_history[pos] = token (inference.c:69-70), for the context bias
+  if (th.hist && threadIdx.x == 0) {
+    const int p = th.pos[b];
+    if (p >= 0 && p < th.seq_len) th.hist[(long)th.seq(b) * th.seq_len + p] = tok;
+  }
   if (tok < 0 || tok >= vocab) tok = 0;
   const uint16_t* row = emb + (long)tok * dim;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(long)b * dim + i] = bf16_to_f32(row[i]);
@@ -190,7 +195,7 @@ __global__ void quant_kernel(int8_t* out, float* scales, const float* in, int ro
 }
 
 cudaError_t launch_embed(const uint16_t* emb, const int* tokens, float* x, int dim, int vocab, int B,
-                         cudaStream_t s, bool pdl) {
+                         cudaStream_t s, bool pdl, const TokenHistory* th) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(B);
   cfg.blockDim = dim3(256);
@@ -200,7 +205,8 @@ cudaError_t launch_embed(const uint16_t* emb, const int* tokens, float* x, int d
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, embed_kernel, emb, tokens, x, dim, vocab);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, emb, tokens, x, dim, vocab,
+                            th ? *th : TokenHistory{});
 }
 
 // argmax_simd_f32 split over kArgParts CTAs per row: CTA p reduces an
@@ -396,6 +402,48 @@ __global__ void logit_bias_kernel(float* logits, const float* __restrict__ bias,
 
 cudaError_t launch_logit_bias(float* logits, const float* bias, int V, int B, cudaStream_t s) {
   logit_bias_kernel<<<dim3(64, B), 256, 0, s>>>(logits, bias, V);
+  return cudaGetLastError();
+}
+
+// The context-aware bias cache (inference.c:657-693): key = the previous
+// token (token_history[pos - 1], or 1 at position 0) as uint64; slot =
+// fmix64(key) % size (MurmurHash3's 64-bit finaliser); linear probing over
+// at most 16 slots: a slot holding the key adds its bias to its target
+// token's logit and ends the search, an empty slot (key 0) ends it.  A key
+// of 0 matches an empty slot, whose bias is 0.  One thread per row.
+__global__ void context_bias_kernel(float* __restrict__ logits, int V, int B, TokenHistory th,
+                                    ContextBias cb) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int p = th.pos[b];
+  if (p > th.seq_len) return;  // the reference reads past its history there
+  const int prev = p > 0 ? th.hist[(long)th.seq(b) * th.seq_len + p - 1] : 1;
+  const uint64_t key = (uint64_t)(long long)prev;
+  uint64_t h = key;
+  h ^= h >> 33;
+  h *= 0xff51afd7ed558ccdULL;
+  h ^= h >> 33;
+  h *= 0xc4ceb9fe1a85ec53ULL;
+  h ^= h >> 33;
+  const uint32_t idx = (uint32_t)(h % (uint64_t)cb.size);
+  for (int i = 0; i < 16; i++) {
+    const uint32_t cur = (uint32_t)(((uint64_t)idx + i) % (uint64_t)cb.size);
+    const uint64_t k = cb.keys[cur];
+    if (k == key) {
+      const int t = cb.tokens[cur];
+      if (t >= 0 && t < V) {
+        float* l = logits + (long)b * V + t;
+        *l = __fadd_rn(*l, cb.biases[cur]);
+      }
+      break;
+    }
+    if (k == 0) break;
+  }
+}
+
+cudaError_t launch_context_bias(float* logits, int V, int B, const TokenHistory& th,
+                                const ContextBias& cb, cudaStream_t s) {
+  context_bias_kernel<<<(B + 127) / 128, 128, 0, s>>>(logits, V, B, th, cb);
   return cudaGetLastError();
 }
 

@@ -4,8 +4,27 @@
 #include <cuda_runtime.h>
 
 namespace ec {
+// Where the embedding launch records each row's input token (pos[b] of
+// sequence seq(b)), as the reference's token_history; hist == nullptr: not.
+struct TokenHistory {
+  const int* pos = nullptr;
+  int* hist = nullptr;     // [S][seq_len]
+  int seq_len = 0;
+  int seq0 = 0;            // row b is sequence seq0 + b ...
+  int seq_plus1 = 0;       // ... or, when set, every row is seq_plus1 - 1
+  __host__ __device__ int seq(int b) const { return seq_plus1 ? seq_plus1 - 1 : seq0 + b; }
+};
+// The reference's context-aware bias cache (t_transformer.context_bias).
+struct ContextBias {
+  const uint64_t* keys = nullptr;
+  const int* tokens = nullptr;
+  const float* biases = nullptr;
+  int size = 0;
+};
 cudaError_t launch_embed(const uint16_t* emb, const int* tokens, float* x, int dim, int vocab, int B,
-                         cudaStream_t s, bool pdl);
+                         cudaStream_t s, bool pdl, const TokenHistory* th = nullptr);
+cudaError_t launch_context_bias(float* logits, int V, int B, const TokenHistory& th,
+                                const ContextBias& cb, cudaStream_t s);
 // The decode step's argmax over kArgParts CTAs per row; scratch holds
 // argmax_scratch_bytes(B), its counters zero (they return to zero).
 size_t argmax_scratch_bytes(int B);

@@ -69,6 +69,14 @@ struct ec_ctx {
   uint16_t* adapter = nullptr;
   float* logit_bias = nullptr;
   bool adapter_on = false, bias_on = false;
+  // the reference's token_history [S][seq_len] and context bias cache
+  int* tok_hist = nullptr;
+  ec::ContextBias cbias;
+  uint64_t* cb_keys = nullptr;
+  int* cb_tokens = nullptr;
+  float* cb_biases = nullptr;
+  int cb_cap = 0;
+  bool cbias_on = false;
   float* xa = nullptr;  // [max_batch][D] adapted final hidden state
   std::vector<unsigned> have;  // bit per tensor per layer
   unsigned have_global = 0;
@@ -407,6 +415,7 @@ int create_ctx(const ec_model_config& c, int device, const ec_model_config* glob
     TRY(dalloc(ctx, &lsh.next, (size_t)S * lsh.tables * lsh.max_units));
     TRY(dalloc(ctx, &lsh.counters, (size_t)S * 2));
   }
+  TRY(dalloc(ctx, &ctx->tok_hist, (size_t)S * c.seq_len));
   // GEMV plans
   const int wk = c.weight_kind;
   const int fr = gemv_force_r();
@@ -733,6 +742,44 @@ extern "C" int ec_set_weight(ec_ctx* ctx, int layer, int which, const void* data
   return EC_OK;
 }
 
+extern "C" int ec_set_context_bias(ec_ctx* ctx, const uint64_t* keys, const int* tokens,
+                                   const float* biases, int size) {
+  if (!ctx || size < 0 || (size > 0 && (!keys || !tokens || !biases)))
+    return fail(EC_ERR_ARG, "bad context bias table");
+  if (ctx->tp_world > 1)
+    return fail(EC_ERR_UNSUPPORTED, "context bias with tensor parallelism");
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  bool any = false;
+  for (int i = 0; i < size && !any; i++) any = keys[i] != 0;
+  if (e == cudaSuccess && any) {
+    if (size > ctx->cb_cap) {
+      // a larger table: new buffers (the old ones are freed with the context)
+      e = dalloc(ctx, &ctx->cb_keys, (size_t)size);
+      if (e == cudaSuccess) e = dalloc(ctx, &ctx->cb_tokens, (size_t)size);
+      if (e == cudaSuccess) e = dalloc(ctx, &ctx->cb_biases, (size_t)size);
+      if (e == cudaSuccess) ctx->cb_cap = size;
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(ctx->cb_keys, keys, (size_t)size * 8, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(ctx->cb_tokens, tokens, (size_t)size * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(ctx->cb_biases, biases, (size_t)size * 4, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess) return fail(EC_ERR_CUDA, cudaGetErrorString(e));
+  // an all-zero (or empty) table changes nothing: the step stays without it
+  ctx->cbias_on = any;
+  ctx->cbias.keys = any ? ctx->cb_keys : nullptr;
+  ctx->cbias.tokens = any ? ctx->cb_tokens : nullptr;
+  ctx->cbias.biases = any ? ctx->cb_biases : nullptr;
+  ctx->cbias.size = any ? size : 0;
+  if (ctx->gexec) {
+    // the captured step changes shape: capture again on the next step
+    cudaGraphExecDestroy(ctx->gexec);
+    ctx->gexec = nullptr;
+  }
+  return EC_OK;
+}
+
 extern "C" int ec_set_weight_bf16(ec_ctx* ctx, int layer, int which, const uint16_t* data,
                                   int on_device) {
   if (!ctx || !data) return fail(EC_ERR_ARG, "null argument");
@@ -878,6 +925,27 @@ ec::ChainPhase chain_phase(const Mat& m, int pro, int epi, const float* x, const
 // adapter or logit bias is registered (inference.c:580-651): RMSNorm of x
 // (rows of D floats) into xn, the adapter xn -> xa, the LM head on it
 // (lm(in, out, rows) issues the caller's GEMV), the logit bias.
+// The embedding launch's token history: rows of sequences seq0.. or, in a
+// prefill, rows of one sequence.
+ec::TokenHistory token_history(ec_ctx* ctx, const int* pos, int seq0, int prefill_seq = -1) {
+  ec::TokenHistory th;
+  th.pos = pos;
+  th.hist = ctx->tok_hist;
+  th.seq_len = ctx->c.seq_len;
+  th.seq0 = seq0;
+  th.seq_plus1 = prefill_seq >= 0 ? prefill_seq + 1 : 0;
+  return th;
+}
+
+// The context bias (inference.c:657-693) on B rows of logits, when a table
+// with a key is registered; before the argmax, which advances positions.
+cudaError_t enqueue_context_bias(ec_ctx* ctx, float* logits, int V, int B,
+                                 const ec::TokenHistory& th) {
+  if (!ctx->cbias_on) return cudaSuccess;
+  ctx->launches++;
+  return ec::launch_context_bias(logits, V, B, th, ctx->cbias, ctx->stream);
+}
+
 template <typename LM>
 cudaError_t enqueue_final_extras(ec_ctx* ctx, const float* x, float* xn, float* xa, int B,
                                  float* logits, LM lm) {
@@ -1005,7 +1073,9 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
   };
   {
     ProfScope ps(ctx, EC_K_EMBED, (2.0 + 4.0) * D * B);
-    if ((e = ec::launch_embed(ctx->emb, tokens, ctx->x, D, c.vocab_size, B, ctx->stream, true)))
+    const ec::TokenHistory th = token_history(ctx, pos, 0, prefill_seq);
+    if ((e = ec::launch_embed(ctx->emb, tokens, ctx->x, D, c.vocab_size, B, ctx->stream, true,
+                              &th)))
       return e;
     ctx->launches++;
   }
@@ -1112,6 +1182,8 @@ cudaError_t enqueue_step_batched(ec_ctx* ctx, const int* tokens, const int* pos,
     };
     if ((e = enqueue_final_extras(ctx, ctx->x, ctx->xn, ctx->xa, B, ctx->logits, lm))) return e;
   }
+  if ((e = enqueue_context_bias(ctx, ctx->logits, V, B, token_history(ctx, pos, 0, prefill_seq))))
+    return e;
   {
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
     // one launch for all B sequences (scratch slice b per sequence)
@@ -1198,7 +1270,9 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
   };
   {
     ProfScope ps(ctx, EC_K_EMBED, (2.0 + 4.0) * D * B);
-    if ((e = ec::launch_embed(ctx->emb, tokens, ctx->x, D, c.vocab_size, B, ctx->stream, true)))
+    const ec::TokenHistory th = token_history(ctx, pos, 0, prefill_seq);
+    if ((e = ec::launch_embed(ctx->emb, tokens, ctx->x, D, c.vocab_size, B, ctx->stream, true,
+                              &th)))
       return e;
     ctx->launches++;
   }
@@ -1274,6 +1348,8 @@ cudaError_t enqueue_step_tc(ec_ctx* ctx, const int* tokens, const int* pos, int 
     };
     if ((e = enqueue_final_extras(ctx, ctx->x, ctx->xn, ctx->xa, B, ctx->logits, lm))) return e;
   }
+  if ((e = enqueue_context_bias(ctx, ctx->logits, V, B, token_history(ctx, pos, 0, prefill_seq))))
+    return e;
   {
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * V * B);
     // one launch for all B sequences (scratch slice b per sequence)
@@ -1401,7 +1477,8 @@ cudaError_t enqueue_step_tp(ec_ctx* ctx, const int* tokens, const int* pos, int 
     }
     ec::LshLayout no_lsh = lsh;  // the append leaves the LSH update to the gathered keys
     no_lsh.tables = 0;
-    if ((e = ec::launch_embed(ctx->emb, tokens + b, x, D, Vg, 1, ctx->stream, true))) return e;
+    const ec::TokenHistory th = token_history(ctx, pos + b, b);
+    if ((e = ec::launch_embed(ctx->emb, tokens + b, x, D, Vg, 1, ctx->stream, true, &th))) return e;
     ctx->launches++;
     float* hb = ctx->hbuf + (size_t)b * F;
     int kinds[2];
@@ -1568,8 +1645,9 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
     }
     {
       ProfScope ps(ctx, EC_K_EMBED, 2.0 * D + 4.0 * D);
+      const ec::TokenHistory th = token_history(ctx, pos + b, b);
       if ((e = ec::launch_embed(ctx->emb, tokens + b, x, D, ctx->cg.vocab_size, 1, ctx->stream,
-                                true)))
+                                true, &th)))
         return e;
     }
     ctx->launches++;
@@ -1637,6 +1715,8 @@ cudaError_t enqueue_step(ec_ctx* ctx, const int* tokens, const int* pos, int B, 
                     ctx->final_norm, lg)))
         return e;
     }
+    if ((e = enqueue_context_bias(ctx, lg, c.vocab_size, 1, token_history(ctx, pos + b, b))))
+      return e;
     ProfScope ps(ctx, EC_K_ARGMAX, 4.0 * c.vocab_size);
     // sequence b's partials and counter live at offset b of the scratch
     if ((e = ec::launch_argmax_split(lg, c.vocab_size, 1, ctx->argmax + b,
@@ -1853,18 +1933,20 @@ extern "C" int ec_launches_per_step(ec_ctx* ctx, int B) {
   // LM head on its own, [bias]
   const bool extras = ctx->adapter_on || ctx->bias_on;
   const int ex = extras ? 1 + ctx->adapter_on + ctx->bias_on : 0;
+  // a registered context bias table: one launch before the argmax
+  const int cb = ctx->cbias_on ? 1 : 0;
   if (ctx->tc && B >= ctx->c.tensor_min_batch) {
     // embed, per pass QKV(0) (quant, GEMM, combine), per layer append,
     // [select], attention and 4 projections per pass, argmax per sequence
     const int passes = (B + ec::kTcMaxRows - 1) / ec::kTcMaxRows;
-    return 1 + 3 * passes + ctx->c.n_layers * (2 + sel + 12 * passes) + 1 + ex;
+    return 1 + 3 * passes + ctx->c.n_layers * (2 + sel + 12 * passes) + 1 + ex + cb;
   }
   if (ctx->chain && B > 1) {
     const int packs = (B + kPack - 1) / kPack;
-    return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + 1 + (extras ? ex + packs : 0);
+    return 1 + packs + ctx->c.n_layers * (2 + sel + packs) + 1 + (extras ? ex + packs : 0) + cb;
   }
-  if (ctx->chain) return B * (2 + ctx->c.n_layers * (3 + sel) + 1 + (extras ? ex + 1 : 0));
-  return B * (1 + ctx->c.n_layers * (6 + sel) + 2 + ex);
+  if (ctx->chain) return B * (2 + ctx->c.n_layers * (3 + sel) + 1 + (extras ? ex + 1 : 0) + cb);
+  return B * (1 + ctx->c.n_layers * (6 + sel) + 2 + ex + cb);
 }
 
 extern "C" int ec_read_state(ec_ctx* ctx, int which, int seq, float* out, size_t n) {

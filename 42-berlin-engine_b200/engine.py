@@ -36,7 +36,7 @@ EXPORTS = [
     "ec_lsh_attn_destroy", "ec_lsh_attn_build", "ec_lsh_attn_query", "ec_lsh_attn_read",
     "ec_gemm_tc_bytes", "ec_gemm_tc_pack", "ec_op_gemm_tc", "ec_prefill", "ec_set_weight_bf16",
     "ec_tp_unique_id", "ec_create_tp", "ec_verify", "ec_lsh_attn_build_paged",
-    "ec_op_sample_top_p", "ec_op_sample_temperature",
+    "ec_op_sample_top_p", "ec_op_sample_temperature", "ec_set_context_bias",
 ]
 K_NAMES = ["gemv_qkv", "gemv_o", "gemv_gateup", "gemv_down", "gemv_lm", "kv_append", "select",
            "attention", "embed", "argmax", "gemv_chain", "tc_gemm", "tc_quant", "tc_combine"]
@@ -116,6 +116,7 @@ def lib():
             "ec_op_argmax": (i, [vp, i, i, vp, vp]),
             "ec_op_sample_top_p": (i, [vp, i, i, vp, vp, i, f, f, f, i, vp, vp, vp]),
             "ec_op_sample_temperature": (i, [vp, i, i, f, vp, vp, vp]),
+            "ec_set_context_bias": (i, [vp, vp, vp, vp, i]),
             "ec_op_paged_append": (i, [C.POINTER(PagedView), vp, vp, i, vp]),
             "ec_op_paged_attention": (i, [C.POINTER(PagedView), vp, vp, i, i, i, vp, vp, vp]),
             "ec_op_paged_attention_static": (i, [C.POINTER(PagedView), vp, vp, i, i, i, vp, vp,
@@ -237,6 +238,15 @@ class Engine:
         if logit_bias is not None:
             check(L.ec_set_weight(self.h, -1, EC_LOGIT_BIAS,
                                   _ptr(np.ascontiguousarray(logit_bias, np.float32)), None, 0))
+
+    def set_context_bias(self, keys, tokens, biases):
+        """The reference's context-aware bias cache (t_transformer.context_bias):
+        uint64 keys (0 = empty), int32 target tokens, float biases."""
+        keys = np.ascontiguousarray(keys, np.uint64)
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        biases = np.ascontiguousarray(biases, np.float32)
+        check(lib().ec_set_context_bias(self.h, _ptr(keys), _ptr(tokens), _ptr(biases),
+                                        keys.size))
 
     def set_weight_device(self, layer, which, ptr, scale_ptr):
         check(lib().ec_set_weight(self.h, layer, which, C.c_void_p(ptr),

@@ -161,6 +161,19 @@ int		ec_create_tp(const ec_model_config *c, int device, int rank, int world,
 int		ec_set_weight(ec_ctx *ctx, int layer, int which, const void *data,
 			const float *scales, int on_device);
 
+/* The context-aware bias cache (t_transformer.context_bias,
+** src/inference/inference.h:180-185, applied at inference.c:657-693): after
+** the LM head (and logit bias) of every row, key = the previous input token
+** of the sequence (1 at position 0) as uint64, slot = MurmurHash3's 64-bit
+** finaliser of the key modulo `size`, linear probing over at most 16 slots;
+** a slot holding the key adds biases[slot] to the logit of tokens[slot], a
+** slot holding 0 ends the search.  The engine records every sequence's input
+** tokens as the reference's token_history does.  Host arrays of `size`
+** entries, copied; a table without a nonzero key (or size 0) switches the
+** lookup off.  Not with tensor parallelism (EC_ERR_UNSUPPORTED). */
+int		ec_set_context_bias(ec_ctx *ctx, const uint64_t *keys, const int *tokens,
+			const float *biases, int size);
+
 /* Quantise-at-load: the reference loads BF16 tensors only
 ** (loader_parse.c:35-49, t_dtype tensor.h:20-24).  `data` is a BF16 matrix
 ** [out_features][in_features] (host, or device when on_device); it is

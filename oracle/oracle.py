@@ -196,6 +196,8 @@ def _bind(lib):
     _sig(lib, "refd_quant_int8", C.c_float, i8p, f32p, C.c_int)
     _sig(lib, "refd_argmax", C.c_int, f32p, C.c_int)
     _sig(lib, "refd_first_rand", C.c_float, C.c_uint)
+    _sig(lib, "refd_set_context_bias", None, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+         C.c_int)
     _sig(lib, "refd_sample_top_p", C.c_int, f32p, C.c_int, C.c_float, C.c_float, C.c_uint)
     _sig(lib, "refd_heap_topk", C.c_int, f32p, i32p, C.c_int, C.c_int, i32p)
     _sig(lib, "refd_lsh_ctx_create", vp, C.c_int, C.c_uint)
@@ -329,6 +331,19 @@ class RefModel:
         self.lib.refd_set_adapter(self.h, adapter.ctypes.data if adapter is not None else None)
         self.lib.refd_set_logit_bias(self.h,
                                      logit_bias.ctypes.data if logit_bias is not None else None)
+
+    def set_context_bias(self, keys=None, tokens=None, biases=None):
+        """Attach the context-aware bias cache (uint64 keys, int32 target
+        tokens, float biases, one table size); None detaches."""
+        if keys is None:
+            self.lib.refd_set_context_bias(self.h, None, None, None, 0)
+            return
+        keys = np.ascontiguousarray(keys, np.uint64)
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        biases = np.ascontiguousarray(biases, np.float32)
+        self._keep += [keys, tokens, biases]
+        self.lib.refd_set_context_bias(self.h, keys.ctypes.data, tokens.ctypes.data,
+                                       biases.ctypes.data, int(keys.size))
 
     def fill_context(self, n, seed=1):
         """Positions 0..n-1 of the paged cache from synthetic K/V through the

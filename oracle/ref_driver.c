@@ -214,6 +214,19 @@ void	refd_set_logit_bias(void *h, const float *bias)
 	((t_refd *)h)->t.logit_bias = (float *)bias;
 }
 
+/* the context-aware bias cache (inference.c:657-693); keys == NULL detaches */
+void	refd_set_context_bias(void *h, const uint64_t *keys, const int *tokens,
+		const float *biases, int size)
+{
+	t_transformer	*t = &((t_refd *)h)->t;
+
+	t->context_bias.keys = (uint64_t *)keys;
+	t->context_bias.tokens = (int *)tokens;
+	t->context_bias.biases = (float *)biases;
+	t->context_bias.size = size;
+	t->context_bias.count = 0;
+}
+
 /*
 ** Fill positions 0..n-1 of every layer's paged KV cache with seeded
 ** synthetic keys and values through the reference's own paged_kv_append

@@ -82,3 +82,78 @@ def test_zero_adapter_and_bias_stay_off(eng, torch, ref, synth):
     e.set_final(adapter, bias)
     assert e.launches_per_step(1) == n0 + 4  # final norm, adapter, LM head, bias
     e.close()
+
+
+def _fmix64(k):
+    m = (1 << 64) - 1
+    k ^= k >> 33
+    k = (k * 0xff51afd7ed558ccd) & m
+    k ^= k >> 33
+    k = (k * 0xc4ceb9fe1a85ec53) & m
+    k ^= k >> 33
+    return k
+
+
+def _context_table(cfg, prompts, size=97, seed=3):
+    """A context bias table as the reference's training fills it: for a
+    previous token key, linear probing from fmix64(key) % size to the first
+    empty slot.  Keys: token 1 (position 0's key) and previous tokens of the
+    prompts, enough of them to make probe chains collide."""
+    rng = np.random.default_rng(seed)
+    keys = np.zeros(size, np.uint64)
+    tokens = np.zeros(size, np.int32)
+    biases = np.zeros(size, np.float32)
+    wanted = [1] + sorted({int(t) for p in prompts for t in p[:30]})[:40]
+    for k in wanted:
+        if k == 0:
+            continue
+        i = _fmix64(k) % size
+        while keys[i] != 0:
+            i = (i + 1) % size
+        keys[i] = k
+        tokens[i] = int(rng.integers(0, cfg.vocab_size))
+        biases[i] = np.float32(rng.uniform(2.0, 9.0))
+    return keys, tokens, biases
+
+
+@pytest.mark.parametrize("B", [1, 3])
+def test_context_bias_matches_reference(eng, torch, ref, synth, B):
+    """The context-aware bias cache (inference.c:657-693): every step's logits
+    bit-identical to the reference with the same table attached, including
+    keys whose slots collide and greedy tokens the biases change; then a
+    prompt prefilled as rows of one sequence."""
+    cfg, model, _, _ = _setup(synth, seed=8)
+    prompts = [synth.prompt(cfg, 40, seed=50 + b) for b in range(B)]
+    keys, tokens, biases = _context_table(cfg, prompts)
+    e = eng.Engine(cfg, max_batch=max(B, 8))
+    e.load(model)
+    n0 = e.launches_per_step(B)
+    e.set_context_bias(keys, tokens, biases)
+    assert e.launches_per_step(B) == n0 + 1
+    rms = []
+    for _ in range(B):
+        m = ref.RefModel(model, use_paged_kv=True, sparse_k=64)
+        m.set_context_bias(keys, tokens, biases)
+        rms.append(m)
+    toks = [int(p[0]) for p in prompts]
+    P = ref.port()
+    hits = 0
+    for t in range(48):
+        lg, am = e.step(toks, [t] * B)
+        for b in range(B):
+            want = rms[b].forward(toks[b], t)
+            assert np.array_equal(lg[b].view(np.uint32), want.view(np.uint32)), \
+                f"step {t} sequence {b}"
+            assert int(am[b]) == P.port_argmax(want, want.size)
+            hits += int(int(am[b]) in set(tokens[keys != 0].tolist()))
+        toks = [int(prompts[b][t + 1]) if t + 1 < 40 else int(am[b]) for b in range(B)]
+    assert hits > 0, "the biases reached a greedy token"
+    # prefill: rows of one sequence read their predecessors' tokens
+    e.reset(0)
+    m = ref.RefModel(model, use_paged_kv=True, sparse_k=64)
+    m.set_context_bias(keys, tokens, biases)
+    lg, tok = e.prefill(0, prompts[0][:21])
+    for p, t in enumerate(prompts[0][:21]):
+        want = m.forward(int(t), p)
+    assert np.array_equal(lg.view(np.uint32), want.view(np.uint32))
+    e.close()
