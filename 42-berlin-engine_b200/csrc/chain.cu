@@ -80,6 +80,45 @@ __device__ __forceinline__ Split split_t(const ChainPhase& ph, int b, int G) {
   return r;
 }
 
+// RMSNorm of xs[0..K) in place with the norm weights already in shared
+// memory: rmsnorm_f32_avx2 (ops_norm.c:105-124) -- lane l of 8 sums x[j]^2
+// over j = l (mod 8) with one fused multiply-add per element, in order; the
+// lanes' sums are added by hsum8, the scalar tail follows.  The 8 summing
+// threads load their elements 32 at a time ahead of the chain, so the
+// sum costs the chain of dependent FMAs rather than a shared-memory latency
+// per element (padding with zeros adds +0 to a non-negative sum: exact).
+__device__ __forceinline__ void rmsnorm_chain(float* xs, const uint16_t* wn, int K, float eps,
+                                              float* red, int ct, int nc) {
+  if (ct < 8) {
+    constexpr int B = 32;
+    const int n8 = K >> 3;
+    const float* xl = xs + ct;
+    float acc = 0.0f, cur[B], nxt[B];
+#pragma unroll
+    for (int b = 0; b < B; b++) cur[b] = b < n8 ? xl[8 * b] : 0.0f;
+    for (int base = 0; base < n8; base += B) {
+#pragma unroll
+      for (int b = 0; b < B; b++) nxt[b] = base + B + b < n8 ? xl[8 * (base + B + b)] : 0.0f;
+#pragma unroll
+      for (int b = 0; b < B; b++) acc = __fmaf_rn(cur[b], cur[b], acc);
+#pragma unroll
+      for (int b = 0; b < B; b++) cur[b] = nxt[b];
+    }
+    red[ct] = acc;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nc));
+  if (ct == 0) {
+    float ss = hsum8(red);
+    for (int j = K & ~7; j < K; j++) ss = __fmaf_rn(xs[j], xs[j], ss);
+    ss = __fdiv_rn(ss, (float)K);
+    red[8] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, eps)));
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(nc));
+  const float inv = red[8];
+  for (int j = ct; j < K; j += nc) xs[j] = __fmul_rn(__fmul_rn(xs[j], inv), bf16_to_f32(wn[j]));
+  asm volatile("bar.sync 1, %0;" ::"r"(nc));
+}
+
 template <int WK, int KCE>
 __global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_kernel(ChainParams P) {
   auto split = [](const ChainPhase& ph, int b, int G) { return split_t<KCE>(ph, b, G); };
@@ -90,7 +129,8 @@ __global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_kernel(ChainPa
   uint64_t* xbar = empty + kStagesMax;
   float* red = reinterpret_cast<float*>(xbar + 2);  // 16 floats
   float* xs = red + 16;                              // [kmax]
-  uint8_t* stages = reinterpret_cast<uint8_t*>(xs + P.kmax);
+  uint16_t* wn = reinterpret_cast<uint16_t*>(xs + P.kmax);  // [knorm] norm weights
+  uint8_t* stages = reinterpret_cast<uint8_t*>(wn) + ((P.knorm * 2 + 15) & ~15);
   constexpr int QS = kWarps;  // quads per stage
   constexpr int stage_bytes = QS * 4 * KCE;
   __shared__ int s_go;
@@ -170,11 +210,16 @@ __global__ void __launch_bounds__(32 + 32 * kWarps, 1) gemv_chain_kernel(ChainPa
     }
     CHAIN_MARK(mk && ct == 0, mb + 1 + 2 * p);
     if (ct == 0 && ok) {
-      mbar_expect_tx(xbar, (uint32_t)(ph.K * 4));
+      // the vector and, for an RMSNorm prologue, its weights
+      const bool nw = ph.pro == PRO_RMSNORM;
+      mbar_expect_tx(xbar, (uint32_t)(ph.K * 4 + (nw ? ph.K * 2 : 0)));
       bulk_g2s(xs, ph.x, (uint32_t)(ph.K * 4), xbar);
+      if (nw) bulk_g2s(wn, ph.norm_w, (uint32_t)(ph.K * 2), xbar);
     }
     if (ok) ok = mbar_wait(xbar, p & 1, P.err);
-    if (ph.pro == PRO_RMSNORM && ok) rmsnorm_smem(xs, ph.norm_w, ph.K, P.eps, red, ct, nc);
+    CHAIN_MARK(mk && ct == 0 && p < 4, mb + 10 + p);
+    if (ph.pro == PRO_RMSNORM && ok) rmsnorm_chain(xs, wn, ph.K, P.eps, red, ct, nc);
+    CHAIN_MARK(mk && ct == 0 && p < 4, mb + 14 + p);
 
     // ---- this CTA's rows, group by group, slot by slot
     const Split sp = split(ph, blockIdx.x, G);
@@ -619,7 +664,7 @@ cudaError_t chain_launch_nb(int wkind, ChainParams P, int nb, int grid, cudaStre
 }
 
 int chain_smem(const ChainParams& P, int kce, int* stages) {
-  const int fixed = (2 * kStagesMax + 2) * 8 + 16 * 4 + P.kmax * 4;
+  const int fixed = (2 * kStagesMax + 2) * 8 + 16 * 4 + P.kmax * 4 + ((P.knorm * 2 + 15) & ~15);
   const int sb = kWarps * 4 * kce;
   int s = (227 * 1024 - 256 - fixed) / sb;
   if (s > kStagesMax) s = kStagesMax;
@@ -628,9 +673,10 @@ int chain_smem(const ChainParams& P, int kce, int* stages) {
   return fixed + s * sb;
 }
 
-int chain_blocks_per_sm(int wkind, int kce, int kmax) {
+int chain_blocks_per_sm(int wkind, int kce, int kmax, int knorm) {
   ChainParams P{};
   P.kmax = kmax;
+  P.knorm = knorm;
   int stages = 0;
   const int smem = chain_smem(P, kce, &stages);
   if (smem < 0) return 0;
@@ -654,7 +700,11 @@ cudaError_t chain_launch(int wkind, ChainParams P, int grid, cudaStream_t s, boo
   const int kce = chain_kce(P);
   if (!kce || P.nph < 1 || P.nph > kMaxChainPhases) return cudaErrorInvalidValue;
   P.kmax = 0;
-  for (int p = 0; p < P.nph; p++) P.kmax = P.ph[p].K > P.kmax ? P.ph[p].K : P.kmax;
+  P.knorm = 0;
+  for (int p = 0; p < P.nph; p++) {
+    P.kmax = P.ph[p].K > P.kmax ? P.ph[p].K : P.kmax;
+    if (P.ph[p].pro == PRO_RMSNORM && P.ph[p].K > P.knorm) P.knorm = P.ph[p].K;
+  }
   int stages = 0;
   const int smem = chain_smem(P, kce, &stages);
   if (smem < 0) return cudaErrorInvalidValue;

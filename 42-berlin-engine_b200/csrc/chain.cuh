@@ -36,6 +36,7 @@ struct ChainParams {
   float eps;
   int mark;    // record phase timestamps (builds with EC_PHASE_TIMING)
   int kmax;    // set by chain_launch
+  int knorm;   // set by chain_launch: the largest K of an RMSNorm phase
   int stages;  // set by chain_launch
   // Grid-counter waits between phases: iterations before EC_ERR_TIMEOUT
   // (0: the default limit, about a second); wait_extra > 0 makes the first
@@ -50,7 +51,8 @@ int chain_kce(const ChainParams& P);
 cudaError_t chain_prepare();
 // CTAs of the batch-1 chain kernel one SM holds at once (every CTA of the
 // chain must be resident together: the grid is the SM count).
-int chain_blocks_per_sm(int wkind, int kce, int kmax);
+// knorm: the largest K of an RMSNorm phase (the model dimension).
+int chain_blocks_per_sm(int wkind, int kce, int kmax, int knorm);
 // grid = the SM count (every CTA resident at once).
 cudaError_t chain_launch(int wkind, ChainParams P, int grid, cudaStream_t s, bool pdl);
 // The same chain over nb sequences (2..8) at once: each weight byte is

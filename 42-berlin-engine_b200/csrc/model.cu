@@ -480,7 +480,7 @@ int create_ctx(const ec_model_config& c, int device, const ec_model_config* glob
     // the chain's grid-wide phase counters need every CTA resident at once
     int kmax = D > F ? D : F;
     if (H * hd > kmax) kmax = H * hd;
-    if (ec::chain_blocks_per_sm(c.weight_kind, ctx->chain_kce, kmax) < 1) {
+    if (ec::chain_blocks_per_sm(c.weight_kind, ctx->chain_kce, kmax, D) < 1) {
       ec_destroy(ctx);
       return fail(EC_ERR_UNSUPPORTED, "the GEMV chain kernel cannot keep one CTA per SM resident "
                                       "on this device");
