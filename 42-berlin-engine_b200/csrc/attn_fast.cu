@@ -58,7 +58,7 @@ constexpr int kFastMaxSplits = 8;  // CTAs per cluster (portable cluster size)
 // the current block, the centroids) is loaded or prefetched before the wait
 // for the previous kernel; after it, every dependent load is issued at once.
 // ------------------------------------------------------------------------
-constexpr int kSelChunk = 64;  // centroids staged in shared memory per round
+constexpr int kSelChunk = 128;  // centroids staged in shared memory per round
 
 // Dynamic shared memory of fast_select_kernel: the step's q/k/v rows and one
 // chunk of centroids.
@@ -111,8 +111,19 @@ __global__ void __launch_bounds__(kFastThreads) fast_select_kernel(KvLayout kv, 
       cp_async16(s_cb + 16 * i, src + 16 * i);
     if (tid - 128 < kBlk - 1) s_cs[tid - 128] = __ldcg(kv.ks + (blk * KV) * kBlk + tid - 128);
   }
-  if (sparse)
+  if (sparse) {
     for (int i = tid; i < nmid; i += kFastThreads) s_pt[i] = pt[1 + i];
+    // the first chunk of middle-block centroids: blocks before this step's
+    // block, written by earlier steps, so they load while the projection
+    // that precedes this kernel finishes
+    if (tid < 128) {
+      const int nc = min(kSelChunk, nmid), per = hd >> 2;
+      for (int i = tid; i < nc * per; i += 128) {
+        const int bk = i / per, pc = i - bk * per;
+        cp_async16(s_cen + (size_t)bk * hd + 4 * pc, kv.centroid + (base + pt[1 + bk]) * hd + 4 * pc);
+      }
+    }
+  }
   pdl_launch_dependents();
   pdl_wait();
   FAST_MARK(mk, 1);
@@ -150,11 +161,12 @@ __global__ void __launch_bounds__(kFastThreads) fast_select_kernel(KvLayout kv, 
       const int grp = ta >> 3, l = ta & 7;
       for (int c0 = 0; c0 < nmid; c0 += kSelChunk) {
         const int nc = min(kSelChunk, nmid - c0), per = hd >> 2;
-        for (int i = ta; i < nc * per; i += 128) {
-          const int bk = i / per, pc = i - bk * per;
-          cp_async16(s_cen + (size_t)bk * hd + 4 * pc,
-                     kv.centroid + (base + s_pt[c0 + bk]) * hd + 4 * pc);
-        }
+        if (c0 > 0)  // (the first chunk was issued before the wait)
+          for (int i = ta; i < nc * per; i += 128) {
+            const int bk = i / per, pc = i - bk * per;
+            cp_async16(s_cen + (size_t)bk * hd + 4 * pc,
+                       kv.centroid + (base + s_pt[c0 + bk]) * hd + 4 * pc);
+          }
         asm volatile("cp.async.wait_all;" ::: "memory");
         asm volatile("bar.sync 1, 128;" ::: "memory");
         // the same trip count on every lane (the shuffles name the whole warp)
