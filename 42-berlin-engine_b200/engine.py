@@ -255,12 +255,20 @@ class Engine:
     def reset(self, seq=0):
         check(lib().ec_reset(self.h, seq))
 
-    def step(self, tokens, pos, want_logits=True):
+    def step(self, tokens, pos, want_logits=True, out=None):
+        """One decode step through ec_decode_step with host buffers.  `out`
+        (optional): caller-owned (logits [B][vocab] float32, argmax [B] int32)
+        arrays to fill instead of new ones -- e.g. views of pinned memory, as
+        a serving loop keeps them."""
         tokens = np.ascontiguousarray(tokens, np.int32)
         pos = np.ascontiguousarray(pos, np.int32)
         B = tokens.size
-        lg = np.empty((B, self.c.vocab_size), np.float32) if want_logits else None
-        am = np.empty(B, np.int32)
+        if out is not None:
+            lg, am = out
+            lg = lg if want_logits else None
+        else:
+            lg = np.empty((B, self.c.vocab_size), np.float32) if want_logits else None
+            am = np.empty(B, np.int32)
         check(lib().ec_decode_step(self.h, _ptr(tokens), _ptr(pos), B, _ptr(lg), _ptr(am)))
         return lg, am
 

@@ -289,17 +289,27 @@ def timed_steps(e, torch, stream, tok, pos, B, steps, warmup, local):
 
 def e2e_steps(e, cur_tok, cur_pos, steps, local):
     """The same step through the C ABI with host buffers: tokens and positions
-    copied in, logits and greedy tokens copied out, every step."""
+    copied in from pinned host memory, logits and greedy tokens copied out
+    into pinned host memory, every step (the buffers a serving loop keeps)."""
+    import torch
     dp = _load("dp")
+    B, V = len(cur_tok), e.c.vocab_size
+    pin = lambda shape, dt: torch.empty(shape, dtype=dt, pin_memory=True).numpy()
+    tok_h, pos_h = pin(B, torch.int32), pin(B, torch.int32)
+    out = (pin((B, V), torch.float32), pin(B, torch.int32))
+    tok_h[:] = cur_tok
+    pos_h[:] = cur_pos
     for _ in range(2):
-        lg, am = e.step(cur_tok, cur_pos)
-        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
+        lg, am = e.step(tok_h, pos_h, out=out)
+        tok_h[:] = am
+        pos_h += 1
     t0 = time.perf_counter()
     for _ in range(steps):
-        lg, am = e.step(cur_tok, cur_pos)
-        cur_tok, cur_pos = [int(a) for a in am], [p + 1 for p in cur_pos]
+        lg, am = e.step(tok_h, pos_h, out=out)
+        tok_h[:] = am
+        pos_h += 1
     ms = (time.perf_counter() - t0) * 1000.0 / steps
-    return dp.max_over_ranks(ms, f"cuda:{local}"), cur_tok, cur_pos
+    return dp.max_over_ranks(ms, f"cuda:{local}"), [int(t) for t in tok_h], [int(p) for p in pos_h]
 
 
 def run_cuda(args):
