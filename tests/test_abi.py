@@ -74,6 +74,20 @@ def test_argument_errors_without_device(eng):
     assert L.ec_create(C.byref(c), 0, C.byref(h)) == eng.EC_ERR_UNSUPPORTED
     assert L.ec_last_error()
     assert L.ec_op_gemv(0, None, None, None, None, 4, 32, None) == eng.EC_ERR_ARG
+    # sampling: missing buffers, non-positive temperature / top_p / penalty,
+    # a history without its lengths -- rejected before any device work
+    assert L.ec_op_sample_top_p(None, 10, 1, None, None, 0, 0.7, 0.9, 1.2, 1, None, None,
+                                None) == eng.EC_ERR_ARG
+    fake = C.c_void_p(16)  # never dereferenced: the arguments fail first
+    assert L.ec_op_sample_top_p(fake, 10, 1, None, None, 0, 0.0, 0.9, 1.2, 1, fake, fake,
+                                None) == eng.EC_ERR_ARG
+    assert L.ec_op_sample_top_p(fake, 10, 1, None, None, 0, 0.7, 0.0, 1.2, 1, fake, fake,
+                                None) == eng.EC_ERR_ARG
+    assert L.ec_op_sample_top_p(fake, 10, 1, fake, None, 4, 0.7, 0.9, 1.2, 1, fake, fake,
+                                None) == eng.EC_ERR_ARG
+    assert L.ec_op_sample_temperature(fake, 0, 1, 0.7, fake, fake, None) == eng.EC_ERR_ARG
+    # context bias: no context / a table without arrays
+    assert L.ec_set_context_bias(None, None, None, None, 4) == eng.EC_ERR_ARG
 
 
 def test_no_device_fails_loudly(eng):
